@@ -1,0 +1,448 @@
+"""Benchmark of the W8A16 projection-GEMM path (BASELINE.json metric).
+
+Workload of the headline (`value`): BASELINE config 2 - the decode projection
+set of a Qwen2.5-0.5B-shaped decoder, 24 layers x {q 896->896 +bias,
+k 896->128 +bias, v 896->128 +bias, o 896->896, gate/up 896->9728,
+down 4864->896}, e4m3 weights with fp32 per-channel scales drawn from
+N(0, 0.02), fp16 activations from N(0, 1), fp32 biases, run at
+M in {1, 8, 32, 64}.  One step = the 24-layer set at each of the four M
+(576 GEMMs).  `value` is algorithmic bytes (weights + scales +
+bias + activations in + outputs) per second over all ranks, in TB/s, with
+every input resident in HBM; the 357.8 MB of weights per pass exceed the
+126 MB L2, so every pass reads them from HBM.  The step is captured once in a
+CUDA graph and replayed.
+
+`e2e` is the same metric through the public API (ddq_b200.gemm_fp8.f8_forward,
+eager, one Python call per GEMM) with each step's activations copied in from
+pinned host memory and every output copied back inside the timed region.
+
+`--impl reference` times the reference semantics on the host cores (the CPU
+oracle in PyTorch: per-call dequantisation + fp32 matmul), which is the
+reference's CPU path for this metric.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "W8A16 GEMM HBM TB/s (M<=64) & TFLOP/s (M=4096); decode tok/s at 1/8 GPU"
+LAYERS = 24
+HIDDEN, INTER = 896, 4864
+# (name, K, N, has_bias) - engine.py:185-187, 206-209 with gate/up fused
+PROJS = [("q", 896, 896, True), ("k", 896, 128, True), ("v", 896, 128, True),
+         ("o", 896, 896, False), ("gate_up", 896, 9728, False), ("down", 4864, 896, False)]
+DECODE_M = (1, 8, 32, 64)
+
+
+def proj_bytes(M, K, N, bias):
+    """Algorithmic bytes of one GEMM: wq + scales + fp32 bias + x in + y out."""
+    return N * K + 4 * N + (4 * N if bias else 0) + 2 * M * K + 2 * M * N
+
+
+def step_bytes():
+    return sum(LAYERS * proj_bytes(M, K, N, b) for M in DECODE_M for _, K, N, b in PROJS)
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples nvidia-smi clocks/throttle reasons while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            p = [t.strip() for t in ln.split(",")]
+            if len(p) < 8:
+                continue
+            try:
+                sm.append(float(p[0]))
+                mx = float(p[1])
+            except ValueError:
+                continue
+            for nm, v in zip(names, p[4:8]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- workload
+class DecodeWorkload:
+    def __init__(self, device, seed=0):
+        from ddq_b200 import gemm_fp8
+        self.device = device
+        g = torch.Generator(device=device).manual_seed(seed)
+        self.layers = []
+        for _ in range(LAYERS):
+            layer = {}
+            for name, K, N, has_bias in PROJS:
+                w = torch.randn(N, K, generator=g, device=device) * 0.02
+                wq, s = gemm_fp8.quantize(w)
+                b = (torch.randn(N, generator=g, device=device) * 0.02) if has_bias else None
+                layer[name] = (wq, s, b)
+                del w
+            self.layers.append(layer)
+        self.x = {M: {name: torch.randn(M, K, generator=g, device=device).half()
+                      for name, K, _, _ in PROJS} for M in DECODE_M}
+        self.y = {M: [{name: torch.empty(M, N, dtype=torch.float16, device=device)
+                       for name, _, N, _ in PROJS} for _ in range(LAYERS)] for M in DECODE_M}
+        torch.cuda.synchronize(device)
+
+    def launch_list(self):
+        """Raw C-ABI argument tuples for every GEMM of one step (no allocation)."""
+        from ddq_b200 import _lib
+        from ddq_b200.gemm_fp8 import workspace
+        L = _lib.load()
+        out = []
+        for M in DECODE_M:
+            for li, layer in enumerate(self.layers):
+                for name, K, N, has_bias in PROJS:
+                    wq, s, b = layer[name]
+                    nws = L.ddq_w8a16_gemm_workspace_size(M, N, K)
+                    ws = workspace(self.device, nws) if nws else None
+                    out.append((self.x[M][name].data_ptr(), wq.data_ptr(), s.data_ptr(),
+                                b.data_ptr() if b is not None else None,
+                                _lib.DTYPE_F32 if b is not None else _lib.DTYPE_NONE,
+                                self.y[M][li][name].data_ptr(), M, N, K,
+                                ws.data_ptr() if ws is not None else None,
+                                ws.numel() if ws is not None else 0))
+        return out
+
+
+def run_ours(args, rank, world, device):
+    from ddq_b200 import _lib, gemm_fp8
+    L = _lib.load()
+    wl = DecodeWorkload(device, seed=1234 + rank)
+    calls = wl.launch_list()
+    gemm = L.ddq_w8a16_gemm
+
+    def step(stream_ptr):
+        for c in calls:
+            st = gemm(*c, stream_ptr)
+            if st:
+                raise RuntimeError(f"ddq_w8a16_gemm failed: {_lib.status_string(st)}")
+
+    # capture one step in a CUDA graph on a side stream
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        step(side.cuda_stream)          # eager warm-up (module load, attributes)
+    torch.cuda.current_stream(device).wait_stream(side)
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        step(side.cuda_stream)
+    torch.cuda.synchronize(device)
+
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(device)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device.index) as clk:
+        ev0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        ev1.record()
+        torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(device)
+    ms = ev0.elapsed_time(ev1)
+    ms_max = reduce_max(ms, world, device)
+    sbytes = step_bytes()
+    value = sbytes * args.steps * world / (ms_max * 1e-3) / 1e12
+
+    # ---- roofline of the dominant kernel: gate/up (58% of the bytes), per launch,
+    # cold weights (24 distinct 8.7 MB matrices in turn), CUDA events on the launch stream
+    per_m = {}
+    dom = None
+    stream = torch.cuda.current_stream(device)
+    for M in DECODE_M:
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(LAYERS * 2)]
+        sel = [c for c in calls if c[6] == M]
+        for rep in range(2):
+            for li in range(LAYERS):
+                c = sel[li * len(PROJS) + 4]
+                e0, e1 = evs[rep * LAYERS + li]
+                e0.record(stream)
+                gemm(*c, stream.cuda_stream)
+                e1.record(stream)
+        torch.cuda.synchronize(device)
+        t = [a.elapsed_time(b) for a, b in evs[LAYERS:]]
+        avg = sum(t) / len(t)
+        nb = proj_bytes(M, 896, 9728, False)
+        per_m[M] = {"gate_up_us": avg * 1e3, "gate_up_gbs": nb / (avg * 1e-3) / 1e9}
+        if M == 64:
+            dom = (nb, avg)
+
+    peaks = load_peaks()
+    nb, avg = dom
+    achieved = nb / (avg * 1e-3) / 1e9
+    roofline = {"kernel": "gemv_skinny_kernel (gate/up 896->9728, M=64)", "bound": "hbm",
+                "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
+                "traffic": None, "bytes_per_launch": nb}
+
+    # ---- e2e through the public API, host buffers, copies inside the timed region
+    e2e = run_e2e(args, wl, device, world)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args.cpu_seconds)
+
+    line = {
+        "metric": METRIC, "value": round(value, 4), "unit": "TB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e4m3xf16->f32",
+        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations; no dataset)",
+        "config": {"workload": "config2: 24-layer decode projection set at M=1,8,32,64",
+                   "layers": LAYERS, "M": list(DECODE_M),
+                   "shapes": [f"{n} {k}->{nn}" + ("+bias" if b else "") for n, k, nn, b in PROJS],
+                   "bytes_per_step": sbytes, "gemms_per_step": len(calls),
+                   "l2": "inputs larger than L2 (357.8 MB of weights per M pass > 126 MB)",
+                   "timing": "CUDA graph of one step, replayed; CUDA events; max over ranks",
+                   "parallelism": f"replicas x{world}"},
+        "per_m_gate_up": per_m,
+        "roofline": roofline,
+        "e2e": e2e,
+        "gpu_launches": len(calls) * args.steps,
+        "clocks": clk.summary(),
+        "cpu_baseline": cpu,
+    }
+    return line
+
+
+def run_e2e(args, wl, device, world):
+    from ddq_b200 import gemm_fp8
+    host_x = {M: {n: t.cpu().pin_memory() for n, t in wl.x[M].items()} for M in DECODE_M}
+    host_y = {M: [{n: torch.empty(t.shape, dtype=t.dtype).pin_memory() for n, t in d.items()}
+                  for d in wl.y[M]] for M in DECODE_M}
+    h2d = sum(t.numel() * 2 for M in DECODE_M for t in host_x[M].values())
+    d2h = sum(t.numel() * 2 for M in DECODE_M for d in host_y[M] for t in d.values())
+
+    def one_step():
+        for M in DECODE_M:
+            xs = {n: t.to(device, non_blocking=True) for n, t in host_x[M].items()}
+            for li, layer in enumerate(wl.layers):
+                for name, _, _, _ in PROJS:
+                    wq, s, b = layer[name]
+                    y = gemm_fp8.f8_forward(xs[name], wq, s, b)
+                    host_y[M][li][name].copy_(y, non_blocking=True)
+
+    steps = max(1, min(args.steps, args.e2e_steps))
+    for _ in range(2):
+        one_step()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(steps):
+        one_step()
+    ev1.record()
+    torch.cuda.synchronize(device)
+    ms = reduce_max(ev0.elapsed_time(ev1), world, device)
+    value = step_bytes() * steps * world / (ms * 1e-3) / 1e12
+    return {"value": round(value, 4), "unit": "TB/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "steps": steps, "ms_per_step": round(ms / steps, 3),
+            "api": "ddq_b200.gemm_fp8.f8_forward (eager, one call per GEMM)"}
+
+
+# ----------------------------------------------------------------------------- CPU side
+def cpu_sample_once(layers=1, seed=0):
+    """One bounded sample of the reference path on the host: `layers` layers of the
+    projection set at every M, per-call dequant + fp32 matmul (oracle, PyTorch CPU)."""
+    from oracle.w8a16 import f8_forward_torch_cpu, quantize
+    rng = np.random.default_rng(seed)
+    mats = []
+    for _ in range(layers):
+        for name, K, N, has_bias in PROJS:
+            wq, s = quantize(rng.normal(0, 0.02, (N, K)).astype(np.float32))
+            b = torch.from_numpy(rng.normal(0, 0.02, N).astype(np.float32)) if has_bias else None
+            mats.append((torch.from_numpy(wq), torch.from_numpy(s), b, K, N, has_bias))
+    xs = {(M, K): torch.from_numpy(rng.normal(0, 1, (M, K)).astype(np.float16))
+          for M in DECODE_M for K in (HIDDEN, INTER)}
+    nbytes = sum(proj_bytes(M, K, N, hb) for M in DECODE_M for (_, _, _, K, N, hb) in mats)
+
+    def run():
+        for M in DECODE_M:
+            for wq, s, b, K, N, _ in mats:
+                f8_forward_torch_cpu(xs[(M, K)], wq, s, b)
+    return run, nbytes
+
+
+def cpu_baseline(budget_s=15.0):
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    run, nbytes = cpu_sample_once(layers=1)
+    run()  # warm-up
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        run()
+        reps += 1
+        if time.perf_counter() - t0 > budget_s or reps >= 50:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(nbytes * reps / dt / 1e12, 6), "unit": "TB/s", "cores": threads,
+            "kind": "port",
+            "sample": f"1 of 24 layers of the projection set at M=1,8,32,64, {reps} reps "
+                      f"({dt:.1f} s); oracle in PyTorch CPU with per-call e4m3 dequant",
+            "cpu": cpu_model()}
+
+
+def cpu_model():
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    run, nbytes = cpu_sample_once(layers=1)
+    for _ in range(args.warmup):
+        run()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        run()
+    dt = time.perf_counter() - t0
+    value = nbytes * args.steps / dt / 1e12
+    sample = ("each step = 1 of the 24 layers of the config-2 projection set at M=1,8,32,64 "
+              "(14.9 MB of weights per M), PyTorch CPU oracle with per-call dequant")
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(value, 6), "unit": "TB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt * 1e3 / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "e4m3xf16->f32",
+        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations; no dataset)",
+        "config": {"workload": "config2: 24-layer decode projection set at M=1,8,32,64 "
+                               "(bounded sample: 1 layer per step)",
+                   "parallelism": "host cores of rank 0"},
+        "cpu_baseline": {"value": round(value, 6), "unit": "TB/s", "cores": threads,
+                         "kind": "port", "sample": sample, "cpu": cpu_model()},
+        "e2e": {"value": round(value, 6), "unit": "TB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+# ----------------------------------------------------------------------------- utils
+def load_peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured (MEASURED_PEAKS.json)"}
+    except (OSError, KeyError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+                "source": "fallback (profiling recipe)"}
+
+
+def reduce_max(v, world, device):
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=device)
+    try:
+        line = run_ours(args, rank, world, device)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,188 @@
+// capi.cu - the extern "C" entry points declared in include/ddq_b200.h:
+// argument validation, per-device attribute cache and kernel dispatch.
+#include <cstdlib>
+#include <mutex>
+
+#include "common.cuh"
+#include "launch.cuh"
+
+namespace ddq {
+
+namespace {
+constexpr int kMaxDevices = 64;
+int g_sm_count[kMaxDevices];
+std::once_flag g_sm_once[kMaxDevices];
+}  // namespace
+
+int current_device() {
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess) return -1;
+  return d;
+}
+
+int device_sm_count(int device) {
+  if (device < 0 || device >= kMaxDevices) return -1;
+  std::call_once(g_sm_once[device], [device] {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) v = -1;
+    g_sm_count[device] = v;
+  });
+  return g_sm_count[device];
+}
+
+int check_launch() {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? DDQ_OK : DDQ_ERR_LAUNCH;
+}
+
+namespace {
+// Smallest M routed to the tensor-core kernel (below it the CUDA-core skinny
+// kernel streams the weight); DDQ_TC_MIN_M overrides it for benchmarking.
+int tc_min_m() {
+  static int v = [] {
+    const char* e = std::getenv("DDQ_TC_MIN_M");
+    int x = e ? std::atoi(e) : 4;
+    return x < 1 ? 1 : x;
+  }();
+  return v;
+}
+
+// Test hooks (ddq_set_debug): bounded-wait limit and fault-injection flags.
+unsigned long long g_wait_timeout_ns = 1000000000ull;  // 1 s
+int g_debug_flags = 0;
+
+bool tc_eligible(const void* x, const void* wq, int64_t K) {
+  return K > 0 && (K % 16 == 0) && aligned16(x) && aligned16(wq);
+}
+}  // namespace
+
+}  // namespace ddq
+
+using namespace ddq;
+
+extern "C" const char* ddq_status_string(int status) {
+  switch (status) {
+    case DDQ_OK: return "ok";
+    case DDQ_ERR_INVALID_ARGUMENT: return "invalid argument (null pointer or bad dtype code)";
+    case DDQ_ERR_SHAPE: return "unsupported or inconsistent shape";
+    case DDQ_ERR_ALIGNMENT: return "pointer alignment not supported";
+    case DDQ_ERR_WORKSPACE: return "workspace missing or too small";
+    case DDQ_ERR_DEVICE: return "no usable sm_100 device";
+    case DDQ_ERR_LAUNCH: return "CUDA kernel launch failed";
+    case DDQ_ERR_TIMEOUT: return "device-side bounded wait timed out";
+    default: return "unknown ddq status";
+  }
+}
+
+extern "C" int ddq_version(void) { return (0 << 16) | 1; }
+
+extern "C" size_t ddq_w8a16_gemm_workspace_size(int64_t M, int64_t N, int64_t K) {
+  if (M < tc_min_m() || M <= 0 || N <= 0 || K <= 0 || K % 16 != 0) return 0;
+  const int dev = current_device();
+  const int sms = dev >= 0 ? device_sm_count(dev) : -1;
+  return tc_plan(M, N, K, sms > 0 ? sms : 148).ws_bytes;
+}
+
+extern "C" int ddq_w8a16_gemm(const void* x, const uint8_t* wq, const float* scales,
+                              const void* bias, int bias_dtype, void* y, int64_t M, int64_t N,
+                              int64_t K, void* workspace, size_t workspace_bytes, void* stream) {
+  (void)workspace; (void)workspace_bytes;
+  if (M < 0 || N < 0 || K < 0) return DDQ_ERR_SHAPE;
+  if (bias_dtype != DDQ_DTYPE_NONE && bias_dtype != DDQ_DTYPE_F16 && bias_dtype != DDQ_DTYPE_F32)
+    return DDQ_ERR_INVALID_ARGUMENT;
+  if (bias_dtype != DDQ_DTYPE_NONE && !bias) return DDQ_ERR_INVALID_ARGUMENT;
+  if (M == 0 || N == 0) return DDQ_OK;
+  if (!x || !wq || !scales || !y) return DDQ_ERR_INVALID_ARGUMENT;
+  if (M > 0x7fffffff || N > 0x7fffffff || K > 0x7fffffff) return DDQ_ERR_SHAPE;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const __half* xh = reinterpret_cast<const __half*>(x);
+  __half* yh = reinterpret_cast<__half*>(y);
+  if (tc_eligible(x, wq, K) && M >= tc_min_m())
+    return launch_tc(xh, wq, scales, bias, bias_dtype, yh, nullptr, 0, (int)M, (int)N, (int)K,
+                     workspace, workspace_bytes, g_wait_timeout_ns, g_debug_flags, s);
+  const bool fast = tc_eligible(x, wq, K) && K <= 12288;
+  if (!fast) return launch_generic(xh, wq, scales, bias, bias_dtype, yh, M, N, K, s);
+  return launch_skinny(xh, wq, scales, bias, bias_dtype, yh, (int)M, (int)N, (int)K, s);
+}
+
+extern "C" int ddq_argmax_f16(const void* logits, int64_t B, int64_t V, int64_t* out,
+                              void* stream) {
+  if (B < 0 || V < 0) return DDQ_ERR_SHAPE;
+  if (B == 0) return DDQ_OK;
+  if (!logits || !out) return DDQ_ERR_INVALID_ARGUMENT;
+  if (V > 0xFFFFFFFFll) return DDQ_ERR_SHAPE;
+  return launch_argmax_f16(reinterpret_cast<const __half*>(logits), B, V, out,
+                           reinterpret_cast<cudaStream_t>(stream));
+}
+
+// The fused lm_head runs token rows in chunks of at most 64 (one tensor-core
+// token tile); chunks reuse one workspace in stream order.
+static const int64_t kLmChunk = 64;
+
+extern "C" size_t ddq_lm_head_argmax_workspace_size(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0 || K % 16 != 0) return 0;
+  const int64_t mc = M < kLmChunk ? M : kLmChunk;
+  if (mc < tc_min_m()) return 0;
+  const int dev = current_device();
+  const int sms = dev >= 0 ? device_sm_count(dev) : -1;
+  return tc_plan(mc, N, K, sms > 0 ? sms : 148).ws_bytes;
+}
+
+extern "C" int ddq_lm_head_argmax(const void* x, const uint8_t* wq, const float* scales, int64_t M,
+                                  int64_t N, int64_t K, int64_t vocab_offset, uint64_t* packed,
+                                  int64_t* ids, void* workspace, size_t workspace_bytes,
+                                  void* stream) {
+  (void)workspace; (void)workspace_bytes;
+  if (M < 0 || N < 0 || K < 0 || vocab_offset < 0) return DDQ_ERR_SHAPE;
+  if (M == 0) return DDQ_OK;
+  if (!x || !packed || (N > 0 && (!wq || !scales))) return DDQ_ERR_INVALID_ARGUMENT;
+  if (M > 0x7fffffff || N > 0x7fffffff || vocab_offset + N > 0xFFFFFFFFll) return DDQ_ERR_SHAPE;
+  if (!(K > 0 && K % 16 == 0 && K <= 12288 && aligned16(x) && aligned16(wq))) return DDQ_ERR_ALIGNMENT;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(packed, 0, (size_t)M * sizeof(uint64_t), s) != cudaSuccess) return DDQ_ERR_LAUNCH;
+  if (N > 0) {
+    const __half* xh = reinterpret_cast<const __half*>(x);
+    unsigned long long* pk = reinterpret_cast<unsigned long long*>(packed);
+    for (int64_t m0 = 0; m0 < M; m0 += kLmChunk) {
+      const int mc = (int)(M - m0 < kLmChunk ? M - m0 : kLmChunk);
+      int st;
+      if (mc >= tc_min_m())
+        st = launch_tc(xh + m0 * K, wq, scales, nullptr, DDQ_DTYPE_NONE, nullptr, pk + m0,
+                       vocab_offset, mc, (int)N, (int)K, workspace, workspace_bytes,
+                       g_wait_timeout_ns, g_debug_flags, s);
+      else
+        st = launch_skinny_argmax(xh + m0 * K, wq, scales, pk + m0, vocab_offset, mc, (int)N,
+                                  (int)K, s);
+      if (st != DDQ_OK) return st;
+    }
+  }
+  if (ids) return launch_unpack_argmax(reinterpret_cast<const unsigned long long*>(packed), M, ids, s);
+  return DDQ_OK;
+}
+
+extern "C" int ddq_unpack_argmax(const uint64_t* packed, int64_t M, int64_t* ids, void* stream) {
+  if (M < 0) return DDQ_ERR_SHAPE;
+  if (M == 0) return DDQ_OK;
+  if (!packed || !ids) return DDQ_ERR_INVALID_ARGUMENT;
+  return launch_unpack_argmax(reinterpret_cast<const unsigned long long*>(packed), M, ids,
+                              reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ddq_set_debug(int flags, uint64_t wait_timeout_ns) {
+  if (flags < 0) return DDQ_ERR_INVALID_ARGUMENT;
+  g_debug_flags = flags;
+  g_wait_timeout_ns = wait_timeout_ns ? wait_timeout_ns : 1000000000ull;
+  return DDQ_OK;
+}
+
+extern "C" int ddq_device_error(int* code, void* stream) {
+  if (!code) return DDQ_ERR_INVALID_ARGUMENT;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int zero = 0;
+  if (cudaMemcpyFromSymbolAsync(code, g_device_error, sizeof(int), 0, cudaMemcpyDeviceToHost, s) != cudaSuccess)
+    return DDQ_ERR_LAUNCH;
+  if (cudaMemcpyToSymbolAsync(g_device_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s) != cudaSuccess)
+    return DDQ_ERR_LAUNCH;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return DDQ_ERR_LAUNCH;
+  return DDQ_OK;
+}

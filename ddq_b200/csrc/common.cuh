@@ -1,0 +1,64 @@
+// common.cuh - shared device helpers for the sm_100a W8A16 kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <stdint.h>
+
+#include "../../include/ddq_b200.h"
+
+namespace ddq {
+
+// ----------------------------------------------------------------------------
+// e4m3fn <-> fp16/fp32 with the hardware converters (sm_89+).
+// Every e4m3fn value is exactly representable in fp16, so the decode is exact.
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t e4m3x2_to_half2_bits(uint16_t two_bytes) {
+  __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)two_bytes, __NV_E4M3);
+  return (uint32_t)h.x | ((uint32_t)h.y << 16);
+}
+
+__device__ __forceinline__ float2 e4m3x2_to_float2(uint16_t two_bytes) {
+  __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)two_bytes, __NV_E4M3);
+  __half2 hh;
+  hh = *reinterpret_cast<__half2*>(&h);
+  return __half22float2(hh);
+}
+
+// Two fp32 values -> two e4m3fn bytes (a -> low byte), round to nearest even,
+// saturating to +-448.  For |v| <= 464 this equals torch's float8_e4m3fn cast.
+__device__ __forceinline__ uint16_t float2_to_e4m3x2(float a, float b) {
+  float2 f = make_float2(a, b);
+  return (uint16_t)__nv_cvt_float2_to_fp8x2(f, __NV_SATFINITE, __NV_E4M3);
+}
+
+// Monotone 16-bit key of an fp16 value: larger fp16 -> larger key.
+__device__ __forceinline__ uint32_t f16_order_key(__half h) {
+  uint16_t b = __half_as_ushort(h);
+  return (b & 0x8000u) ? (uint32_t)(uint16_t)(~b) : (uint32_t)(b | 0x8000u);
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Device error word set by bounded waits that give up (read by ddq_device_error).
+extern __device__ int g_device_error;
+
+__device__ __forceinline__ void record_device_error(int code) {
+  atomicCAS(&g_device_error, 0, code);
+}
+
+// ----------------------------------------------------------------------------
+// Host-side helpers
+// ----------------------------------------------------------------------------
+int device_sm_count(int device);
+int current_device();
+int check_launch();
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace ddq

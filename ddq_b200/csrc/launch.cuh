@@ -1,0 +1,30 @@
+// launch.cuh - internal launcher declarations shared by the C-ABI dispatcher.
+#pragma once
+#include "common.cuh"
+
+namespace ddq {
+
+int launch_skinny(const __half* x, const uint8_t* wq, const float* scales, const void* bias,
+                  int bias_dtype, __half* y, int M, int N, int K, cudaStream_t s);
+int launch_skinny_argmax(const __half* x, const uint8_t* wq, const float* scales,
+                         unsigned long long* packed, int64_t vocab_offset, int M, int N, int K,
+                         cudaStream_t s);
+int launch_generic(const __half* x, const uint8_t* wq, const float* scales, const void* bias,
+                   int bias_dtype, __half* y, int64_t M, int64_t N, int64_t K, cudaStream_t s);
+int launch_argmax_f16(const __half* logits, int64_t B, int64_t V, int64_t* out, cudaStream_t s);
+struct TcPlan {
+  int bt;            // token tile (MMA N)
+  int splits;        // split-K factor (grid.z)
+  int kps;           // 64-wide K steps per split
+  int64_t tiles;     // 128 x bt output tiles
+  size_t ws_part_bytes;
+  size_t ws_bytes;   // workspace needed (0 without split-K)
+};
+TcPlan tc_plan(int64_t M, int64_t N, int64_t K, int sms);
+int launch_tc(const __half* x, const uint8_t* wq, const float* scales, const void* bias,
+              int bias_dtype, __half* y, unsigned long long* packed, int64_t vocab_offset,
+              int M, int N, int K, void* ws, size_t ws_bytes, unsigned long long timeout_ns,
+              int debug_flags, cudaStream_t s);
+int launch_unpack_argmax(const unsigned long long* packed, int64_t M, int64_t* ids, cudaStream_t s);
+
+}  // namespace ddq

@@ -1,0 +1,111 @@
+"""Drop-in mirror of the reference operator module ``gemm_FP8_d.cu``.
+
+Same names, argument names, defaults, output shapes/dtypes and error
+behaviour as the pybind11 module of ``gemm_FP8_d.cu:221-228``:
+
+* ``quantize(w) -> [wq uint8 [N,K], scales fp32 [N]]``   (``gemm_FP8_d.cu:150-167``)
+* ``f8_forward(x, wq, scales, bias=None) -> y``          (``gemm_FP8_d.cu:171-210``)
+* ``forward(x, w, bias=None) -> y``                      (``gemm_FP8_d.cu:214-217``)
+
+so ``engine.py``'s ``_linear`` (``engine.py:85-86``) can call
+``f8_forward(x, module.wq, module.scales, module.bias)`` in place of
+``gemm_naive.forward(x, module.weight, module.bias)``.
+
+Differences from the reference, all widening what is accepted:
+``quantize`` also takes fp32 weights and ``f8_forward`` also takes an fp32
+bias (the reference takes fp16 only, ``gemm_FP8_d.cu:151,191``).  Errors are
+``RuntimeError`` with the reference's message text, as ``TORCH_CHECK`` raises.
+All work runs on the caller's current CUDA stream, asynchronously, through the
+C ABI of ``libddq_b200.so``; nothing falls back to the CPU.
+"""
+from __future__ import annotations
+
+from typing import List, Optional
+
+import torch
+
+from . import _lib
+
+_workspaces: dict = {}
+
+
+def _check(cond: bool, msg: str) -> None:
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Zero-filled per-device scratch, grown on demand and then reused.
+
+    The kernels leave the counters in it at zero after each call, so one
+    workspace serves every call ordered on a stream.
+    """
+    key = (device.type, device.index)
+    buf = _workspaces.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
+        _workspaces[key] = buf
+    return buf
+
+
+def quantize(w: torch.Tensor) -> List[torch.Tensor]:
+    """Quantize fp16/fp32 [N,K] weights to e4m3fn bytes + per-row fp32 scales."""
+    _check(w.is_cuda and w.dtype in (torch.float16, torch.float32),
+           "gemm_fp8: fp16 CUDA weight required")
+    _check(w.dim() == 2, "gemm_fp8: weight must be [N,K]")
+    wc = w.contiguous()
+    N, K = wc.shape
+    wq = torch.empty((N, K), dtype=torch.uint8, device=w.device)
+    scales = torch.empty((N,), dtype=torch.float32, device=w.device)
+    code = _lib.DTYPE_F16 if wc.dtype == torch.float16 else _lib.DTYPE_F32
+    with torch.cuda.device(w.device):
+        st = _lib.load().ddq_quantize_e4m3(wc.data_ptr(), code, N, K, wq.data_ptr(),
+                                           scales.data_ptr(), _stream_ptr(w.device))
+    _lib.check(st, "gemm_fp8.quantize")
+    return [wq, scales]
+
+
+def f8_forward(x: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor,
+               bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """FP8 GEMM on pre-quantized weights: y[...,N] = x[...,K] @ (e4m3(wq)*s)^T (+bias)."""
+    _check(x.is_cuda and wq.is_cuda, "gemm_fp8: CUDA tensors required")
+    _check(x.dtype == torch.float16, "gemm_fp8: fp16 x required")
+    _check(wq.dtype == torch.uint8, "gemm_fp8: wq must be uint8 e4m3")
+    _check(wq.dim() == 2 and wq.size(0) == scales.numel(), "gemm_fp8: shape mismatch")
+    _check(scales.is_cuda and scales.dtype == torch.float32, "gemm_fp8: scales must be fp32 CUDA")
+    N, K = wq.shape
+    _check(x.dim() >= 1 and x.size(-1) == K, "gemm_fp8: inner dim mismatch")
+    xc = x.contiguous()
+    x2 = xc.reshape(-1, K)
+    M = x2.size(0)
+    y2 = torch.empty((M, N), dtype=torch.float16, device=x.device)
+    bptr, bcode = None, _lib.DTYPE_NONE
+    if bias is not None and bias.numel() > 0:
+        _check(bias.numel() == N, "gemm_fp8: bias length mismatch")
+        _check(bias.is_cuda and bias.dtype in (torch.float16, torch.float32),
+               "gemm_fp8: bias must be fp16 or fp32 CUDA")
+        bias = bias.contiguous()
+        bptr = bias.data_ptr()
+        bcode = _lib.DTYPE_F16 if bias.dtype == torch.float16 else _lib.DTYPE_F32
+    wqc = wq.contiguous()
+    sc = scales.contiguous()
+    L = _lib.load()
+    with torch.cuda.device(x.device):
+        nws = L.ddq_w8a16_gemm_workspace_size(M, N, K)
+        ws = workspace(x.device, nws) if nws else None
+        st = L.ddq_w8a16_gemm(x2.data_ptr(), wqc.data_ptr(), sc.data_ptr(), bptr, bcode,
+                              y2.data_ptr(), M, N, K,
+                              ws.data_ptr() if ws is not None else None,
+                              ws.numel() if ws is not None else 0, _stream_ptr(x.device))
+    _lib.check(st, "gemm_fp8.f8_forward")
+    return y2.reshape(*x.shape[:-1], N)
+
+
+def forward(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Drop-in for gemm_d.forward: quantize w (every call, as the reference does), then GEMM."""
+    wq, scales = quantize(w)
+    return f8_forward(x, wq, scales, bias)

@@ -1,0 +1,151 @@
+/*
+ * ddq_b200.h - C ABI of the B200 (sm_100a) W8A16 projection-GEMM library.
+ *
+ * Every entry point takes raw device pointers, sizes and a CUDA stream
+ * (passed as void*, i.e. a cudaStream_t; NULL = legacy default stream),
+ * launches asynchronously on that stream and returns a ddq_status.  Nothing
+ * here allocates device memory; nothing synchronises the device.  The
+ * library keeps no mutable global state except per-device cached attributes
+ * (SM count, the driver's tensor-map encoder) and the device error word
+ * read by ddq_device_error().
+ *
+ * Data formats (all row-major, contiguous):
+ *   x      fp16  [M, K]   activations
+ *   wq     uint8 [N, K]   e4m3fn weight bytes (K contiguous)
+ *   scales fp32  [N]      per-output-channel scale: w ~= e4m3(wq) * scale
+ *   bias   fp16 or fp32 [N], or NULL
+ *   y      fp16  [M, N]
+ *
+ * Each declaration names the reference interface it replaces
+ * (hdahroug/ddq, file:line).
+ */
+#ifndef DDQ_B200_H
+#define DDQ_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  The Python mirror turns a non-zero status into a
+ * RuntimeError carrying ddq_status_string(), as the reference's TORCH_CHECK
+ * does (gemm_FP8_d.cu:151-152, 173-180, 190). */
+typedef enum ddq_status {
+  DDQ_OK = 0,
+  DDQ_ERR_INVALID_ARGUMENT = 1, /* NULL pointer, negative size, bad dtype code */
+  DDQ_ERR_SHAPE = 2,            /* inconsistent or unsupported M/N/K */
+  DDQ_ERR_ALIGNMENT = 3,        /* pointer not aligned as the kernel needs */
+  DDQ_ERR_WORKSPACE = 4,        /* workspace missing or smaller than required */
+  DDQ_ERR_DEVICE = 5,           /* no sm_100 device / attribute query failed */
+  DDQ_ERR_LAUNCH = 6,           /* CUDA launch error (cudaGetLastError) */
+  DDQ_ERR_TIMEOUT = 7           /* a device-side bounded wait gave up */
+} ddq_status;
+
+/* Element type codes for bias / weight inputs. */
+enum {
+  DDQ_DTYPE_NONE = 0,
+  DDQ_DTYPE_F16 = 1,
+  DDQ_DTYPE_F32 = 2
+};
+
+/* Human-readable text of a status code (static storage). */
+const char* ddq_status_string(int status);
+
+/* Library version, (major << 16) | minor. */
+int ddq_version(void);
+
+/*
+ * Quantize a weight matrix to e4m3fn with a per-row fp32 scale.
+ * Replaces: quantize() + quantize_kernel, gemm_FP8_d.cu:150-167, 66-86.
+ *   scale[n] = max_k |w[n,k]| / 448   (1.0 for an all-zero row)
+ *   wq[n,k]  = e4m3fn(w[n,k] / scale[n]), IEEE fp32 division, round to
+ *              nearest even (torch's float8_e4m3fn cast; the reference
+ *              encoder rounds ties half-up instead, gemm_FP8_d.cu:56).
+ * w_dtype is DDQ_DTYPE_F16 (the reference's only input, :151) or
+ * DDQ_DTYPE_F32.
+ */
+int ddq_quantize_e4m3(const void* w, int w_dtype, int64_t N, int64_t K,
+                      uint8_t* wq, float* scales, void* stream);
+
+/*
+ * Bytes of device workspace ddq_w8a16_gemm needs for this shape (0 if none).
+ * The workspace holds split-K partial sums and per-tile arrival counters.
+ * It must be zero-filled once when allocated; every call leaves its counters
+ * at zero again.  Calls sharing one workspace must be ordered on one stream.
+ */
+size_t ddq_w8a16_gemm_workspace_size(int64_t M, int64_t N, int64_t K);
+
+/*
+ * y = fp16( x @ (e4m3(wq) * scale)^T + bias ), fp32 accumulation.
+ * Replaces: f8_forward() + fp8_gemm_kernel, gemm_FP8_d.cu:171-210, 94-146,
+ * and, at the engine's dispatch point, gemm_d.cu:36-87 (cuBLAS + the
+ * separate add_bias_kernel, here folded into the epilogue).
+ * bias_dtype: DDQ_DTYPE_NONE (bias may be NULL), _F16 (the reference's only
+ * bias type, gemm_FP8_d.cu:191) or _F32.
+ * Requirements: M >= 0, N >= 1, K >= 1; the fast paths need K % 16 == 0 and
+ * 16-byte aligned x / wq (a generic CUDA kernel covers the rest).
+ */
+int ddq_w8a16_gemm(const void* x, const uint8_t* wq, const float* scales,
+                   const void* bias, int bias_dtype, void* y,
+                   int64_t M, int64_t N, int64_t K,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Greedy argmax over fp16 logits [B, V] -> int64 [B]; ties go to the
+ * lowest index.  Replaces: sampler_d.cu:10-70 (argmax_kernel + forward).
+ */
+int ddq_argmax_f16(const void* logits, int64_t B, int64_t V, int64_t* out,
+                   void* stream);
+
+/*
+ * Bytes of workspace ddq_lm_head_argmax needs (per-tile partial maxima).
+ */
+size_t ddq_lm_head_argmax_workspace_size(int64_t M, int64_t N, int64_t K);
+
+/*
+ * Fused lm_head GEMM + greedy argmax over one vocabulary shard:
+ *   logits[m, n] = fp16( x[m,:] . (e4m3(wq[n,:]) * scale[n]) )   (no bias)
+ *   packed[m]    = max over n of  (ordered_fp16(logits[m,n]) << 32)
+ *                                 | (0xFFFFFFFF - (n + vocab_offset))
+ * i.e. the largest fp16 logit, ties to the lowest global index, encoded so
+ * that a MAX over packed values of several shards (an NCCL all-gather or
+ * all-reduce MAX) yields the global greedy token.  ids[m] (may be NULL)
+ * receives the decoded global index of this shard's best logit.
+ * The logits are never written to memory.
+ * Replaces: engine.py:338 (lm_head via gemm_d) + engine.py:345/351
+ * (sampler_d.forward on the last position), sampler_d.cu:10-49.
+ */
+int ddq_lm_head_argmax(const void* x, const uint8_t* wq, const float* scales,
+                       int64_t M, int64_t N, int64_t K, int64_t vocab_offset,
+                       uint64_t* packed, int64_t* ids,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Decode packed (key, index) words produced by ddq_lm_head_argmax (or their
+ * element-wise MAX across shards) into int64 token ids.
+ */
+int ddq_unpack_argmax(const uint64_t* packed, int64_t M, int64_t* ids,
+                      void* stream);
+
+/*
+ * Read (and clear) the device error word that bounded device-side waits set
+ * when they give up.  Synchronises `stream`.  *code = 0 means no error.
+ */
+int ddq_device_error(int* code, void* stream);
+
+/*
+ * Test hook (no reference counterpart): set the limit of every device-side
+ * bounded wait (0 = the 1 s default) and fault-injection flags for later
+ * launches in this process.  flags bit 0 makes the tensor-core kernel skip
+ * the accumulator-ready signal, so its epilogue wait runs out and reports
+ * DDQ_ERR_TIMEOUT through ddq_device_error() without faulting the GPU.
+ */
+int ddq_set_debug(int flags, uint64_t wait_timeout_ns);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DDQ_B200_H */

@@ -1,0 +1,177 @@
+"""GPU parity tests of the W8A16 operators against the CPU oracle.
+
+Quantization is byte-exact; the GEMM is held to the north_star tolerance
+(normwise relative error <= 1e-2 against the fp32 semantics; in practice the
+fp16 output rounding, ~5e-4, dominates)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import w8a16 as o
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2          # north_star: max relative error vs the fp32 result
+TIGHT = 3e-3        # what the kernels actually achieve (fp16 output rounding + fp32 sums)
+
+PROJ_SHAPES = [(896, 896), (128, 896), (1152, 896), (896, 4864), (9728, 896), (4864, 896)]
+
+
+def gen(M, N, K, seed=0, wdtype=np.float32):
+    rng = np.random.default_rng(seed)
+    x = rng.normal(0, 1, (M, K)).astype(np.float16)
+    w = rng.normal(0, 0.02, (N, K)).astype(wdtype)
+    b = rng.normal(0, 0.02, N).astype(np.float32)
+    return x, w, b
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.fixture(scope="module")
+def g(cuda_device):
+    from ddq_b200 import gemm_fp8
+    return gemm_fp8
+
+
+@pytest.mark.parametrize("N,K", PROJ_SHAPES + [(136, 48), (3, 40), (7, 1)])
+@pytest.mark.parametrize("wdtype", [np.float32, np.float16])
+def test_quantize_is_byte_exact(g, N, K, wdtype):
+    _, w, _ = gen(1, N, K, seed=N + K, wdtype=wdtype)
+    w[min(2, N - 1)] = 0  # an all-zero row
+    wq, s = g.quantize(dev(w))
+    wq_ref, s_ref = o.quantize(w)
+    np.testing.assert_array_equal(s.cpu().numpy(), s_ref)
+    np.testing.assert_array_equal(wq.cpu().numpy(), wq_ref)
+
+
+def test_quantize_crafted_values(g):
+    # ties, subnormal/normal boundary, signed zeros, saturation point
+    base = np.array([1.0625, 0.0146, 0.0155, 2.0 ** -10, 1.5 * 2.0 ** -10, -0.0, 0.0,
+                     3.0, -1.0625, 448.0 / 1.0001], np.float32)
+    w = np.tile(np.concatenate([base, [448.0]]).astype(np.float32), (4, 2))
+    wq, s = g.quantize(dev(w))
+    wq_ref, s_ref = o.quantize(w)
+    np.testing.assert_array_equal(s.cpu().numpy(), s_ref)
+    np.testing.assert_array_equal(wq.cpu().numpy(), wq_ref)
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 8, 16, 17, 32, 64])
+@pytest.mark.parametrize("N,K", PROJ_SHAPES)
+def test_f8_forward_decode_shapes(g, M, N, K):
+    x, w, b = gen(M, N, K, seed=M * 7 + N)
+    wq, s = o.quantize(w)
+    bias = b if N in (896, 128, 1152) and K == 896 else None
+    y = g.f8_forward(dev(x), dev(wq), dev(s), dev(bias) if bias is not None else None)
+    assert y.dtype == torch.float16 and tuple(y.shape) == (M, N)
+    y_ref = o.f8_forward(x, wq, s, bias)
+    err = o.normwise_rel_err(y.cpu().numpy(), y_ref)
+    assert err <= TIGHT, err
+
+
+@pytest.mark.parametrize("M", [100, 512, 1000])
+@pytest.mark.parametrize("N,K", [(896, 896), (1152, 896), (896, 4864)])
+def test_f8_forward_larger_m(g, M, N, K):
+    x, w, b = gen(M, N, K, seed=M + N + K)
+    wq, s = o.quantize(w)
+    y = g.f8_forward(dev(x), dev(wq), dev(s), dev(b))
+    err = o.normwise_rel_err(y.cpu().numpy(), o.f8_forward(x, wq, s, b))
+    assert err <= TIGHT, err
+
+
+@pytest.mark.parametrize("M,N,K", [(3, 136, 48), (5, 7, 40), (2, 33, 1), (9, 100, 24)])
+def test_f8_forward_ragged_and_generic_path(g, M, N, K):
+    x, w, b = gen(M, N, K, seed=11)
+    wq, s = o.quantize(w)
+    y = g.f8_forward(dev(x), dev(wq), dev(s), dev(b))
+    err = o.normwise_rel_err(y.cpu().numpy(), o.f8_forward(x, wq, s, b))
+    assert err <= TIGHT, err
+
+
+def test_unaligned_activation_pointer_uses_generic_path(g):
+    x, w, b = gen(5, 256, 896, seed=12)
+    wq, s = o.quantize(w)
+    xbig = torch.zeros(5 * 896 + 1, dtype=torch.float16, device="cuda")
+    xbig[1:] = dev(x).reshape(-1)
+    xv = xbig[1:].view(5, 896)  # 2-byte offset: not 16-byte aligned
+    y = g.f8_forward(xv, dev(wq), dev(s), dev(b))
+    assert o.normwise_rel_err(y.cpu().numpy(), o.f8_forward(x, wq, s, b)) <= TIGHT
+
+
+@pytest.mark.parametrize("bias_kind", ["none", "empty", "f16", "f32"])
+def test_bias_variants(g, bias_kind):
+    x, w, b = gen(8, 896, 896, seed=13)
+    wq, s = o.quantize(w)
+    if bias_kind == "none":
+        bt, bref = None, None
+    elif bias_kind == "empty":
+        bt, bref = torch.empty(0, device="cuda", dtype=torch.float16), None
+    elif bias_kind == "f16":
+        bt, bref = dev(b.astype(np.float16)), b.astype(np.float16)
+    else:
+        bt, bref = dev(b), b
+    y = g.f8_forward(dev(x), dev(wq), dev(s), bt)
+    assert o.normwise_rel_err(y.cpu().numpy(), o.f8_forward(x, wq, s, bref)) <= TIGHT
+
+
+def test_leading_dims_and_empty_batch(g):
+    x, w, b = gen(6, 128, 896, seed=14)
+    wq, s = o.quantize(w)
+    x3 = dev(x).reshape(2, 3, 896)
+    y = g.f8_forward(x3, dev(wq), dev(s), dev(b))
+    assert tuple(y.shape) == (2, 3, 128)
+    assert o.normwise_rel_err(y.reshape(6, 128).cpu().numpy(), o.f8_forward(x, wq, s, b)) <= TIGHT
+    y0 = g.f8_forward(torch.empty(0, 896, dtype=torch.float16, device="cuda"), dev(wq), dev(s))
+    assert tuple(y0.shape) == (0, 128)
+
+
+def test_forward_quantizes_then_multiplies(g):
+    x, w, b = gen(4, 896, 896, seed=15)
+    y = g.forward(dev(x), dev(w.astype(np.float16)), dev(b.astype(np.float16)))
+    y_ref = o.forward(x, w.astype(np.float16), b.astype(np.float16))
+    assert o.normwise_rel_err(y.cpu().numpy(), y_ref) <= TIGHT
+
+
+def test_error_messages_match_reference(g):
+    wq = torch.zeros(8, 16, dtype=torch.uint8, device="cuda")
+    s = torch.ones(8, dtype=torch.float32, device="cuda")
+    xh = torch.zeros(2, 16, dtype=torch.float16, device="cuda")
+    with pytest.raises(RuntimeError, match="fp16 x required"):
+        g.f8_forward(xh.float(), wq, s)
+    with pytest.raises(RuntimeError, match="wq must be uint8"):
+        g.f8_forward(xh, wq.half(), s)
+    with pytest.raises(RuntimeError, match="shape mismatch"):
+        g.f8_forward(xh, wq, s[:4])
+    with pytest.raises(RuntimeError, match="inner dim mismatch"):
+        g.f8_forward(torch.zeros(2, 8, dtype=torch.float16, device="cuda"), wq, s)
+    with pytest.raises(RuntimeError, match="bias length mismatch"):
+        g.f8_forward(xh, wq, s, torch.zeros(3, device="cuda", dtype=torch.float16))
+    with pytest.raises(RuntimeError, match="CUDA tensors required"):
+        g.f8_forward(xh.cpu(), wq, s)
+    with pytest.raises(RuntimeError, match="weight must be"):
+        g.quantize(torch.zeros(4, device="cuda", dtype=torch.float16))
+    with pytest.raises(RuntimeError, match="fp16 CUDA weight required"):
+        g.quantize(torch.zeros(4, 4, dtype=torch.float16))
+
+
+@pytest.mark.parametrize("M", [1, 16, 64, 512])
+def test_deterministic_bitwise(g, M):
+    x, w, b = gen(M, 1152, 896, seed=16)
+    wq, s = o.quantize(w)
+    args = (dev(x), dev(wq), dev(s), dev(b))
+    y1 = g.f8_forward(*args)
+    y2 = g.f8_forward(*args)
+    assert torch.equal(y1, y2)
+
+
+def test_runs_on_callers_stream(g):
+    x, w, b = gen(16, 896, 896, seed=17)
+    wq, s = o.quantize(w)
+    xs, wqs, ss, bs = dev(x), dev(wq), dev(s), dev(b)
+    st = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(st):
+        y = g.f8_forward(xs, wqs, ss, bs)
+    st.synchronize()
+    assert o.normwise_rel_err(y.cpu().numpy(), o.f8_forward(x, wq, s, b)) <= TIGHT
