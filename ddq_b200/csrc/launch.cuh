@@ -12,6 +12,11 @@ int launch_skinny_argmax(const __half* x, const uint8_t* wq, const float* scales
 int launch_generic(const __half* x, const uint8_t* wq, const float* scales, const void* bias,
                    int bias_dtype, __half* y, int64_t M, int64_t N, int64_t K, cudaStream_t s);
 int launch_argmax_f16(const __half* logits, int64_t B, int64_t V, int64_t* out, cudaStream_t s);
+// Split-K workspace: a fixed 4 KiB ticket region (one uint32 per output tile,
+// zero between calls) followed by the fp32 partial sums.
+constexpr size_t kTicketBytes = 4096;
+constexpr int64_t kTicketSlots = (int64_t)(kTicketBytes / 4);
+
 struct TcPlan {
   int bt;            // token tile (MMA N)
   int splits;        // split-K factor (grid.z)

@@ -403,7 +403,7 @@ TcPlan tc_plan(int64_t M, int64_t N, int64_t K, int sms) {
   const int64_t KT = (K + TC_BK - 1) / TC_BK;
   const int64_t tiles = ((N + TC_BN - 1) / TC_BN) * ((M + p.bt - 1) / p.bt);
   int64_t splits = 1, kps = KT;
-  if (sms > 0 && tiles < sms) {
+  if (sms > 0 && tiles < sms && tiles <= kTicketSlots) {
     splits = sms / tiles;
     if (splits > KT) splits = KT;
     if (splits < 1) splits = 1;
@@ -414,8 +414,11 @@ TcPlan tc_plan(int64_t M, int64_t N, int64_t K, int sms) {
   p.kps = (int)kps;
   p.tiles = tiles;
   if (splits > 1) {
+    // [0, 4 KiB): one ticket per tile, always at the same place, so whatever
+    // shape ran before, the tickets a call reads are the zeros the previous
+    // call left behind.  Partials follow.
     p.ws_part_bytes = (size_t)tiles * splits * TC_BN * p.bt * sizeof(float);
-    p.ws_bytes = p.ws_part_bytes + (((size_t)tiles * sizeof(unsigned) + 255) & ~(size_t)255);
+    p.ws_bytes = kTicketBytes + p.ws_part_bytes;
   }
   return p;
 }
@@ -437,10 +440,9 @@ int launch_tc(const __half* x, const uint8_t* wq, const float* scales, const voi
   a.y = y;
   a.packed = packed;
   a.vocab_offset = vocab_offset;
-  a.ws_part = p.ws_bytes ? reinterpret_cast<float*>(ws) : nullptr;
-  a.ws_cnt = p.ws_bytes ? reinterpret_cast<unsigned*>(reinterpret_cast<uint8_t*>(ws) +
-                                                      p.ws_part_bytes)
-                        : nullptr;
+  a.ws_cnt = p.ws_bytes ? reinterpret_cast<unsigned*>(ws) : nullptr;
+  a.ws_part = p.ws_bytes ? reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + kTicketBytes)
+                         : nullptr;
   a.M = M;
   a.N = N;
   a.K = K;

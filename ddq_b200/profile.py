@@ -1,0 +1,100 @@
+"""Micro-benchmark of one W8A16 GEMM shape (also the target of ncu captures).
+
+Runs ``--iters`` launches of ``ddq_w8a16_gemm`` (or the fused lm_head with
+``--lm-head``) for one (M, N, K), rotating through enough distinct weight
+copies that each launch reads its weight from HBM (the copies total more than
+twice the 126 MB L2, unless ``--copies`` says otherwise).  Each launch is
+bracketed by CUDA events on the launch stream; the host first parks the GPU
+on a sleep kernel so that every launch is queued before the first one runs
+and the events time the GPU alone.  Prints one JSON line.
+
+    python -m ddq_b200.profile --m 64 --n 9728 --k 896 --iters 50
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+
+import torch
+
+from . import _lib, gemm_fp8, lm_head
+
+
+def algorithmic_bytes(M, N, K, bias=False, lm=False):
+    out = 8 * M if lm else 2 * M * N
+    return N * K + 4 * N + (4 * N if bias else 0) + 2 * M * K + out
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--m", type=int, default=64)
+    ap.add_argument("--n", type=int, default=9728)
+    ap.add_argument("--k", type=int, default=896)
+    ap.add_argument("--bias", action="store_true")
+    ap.add_argument("--lm-head", action="store_true")
+    ap.add_argument("--iters", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--copies", type=int, default=0, help="distinct weight copies (0: > 2x L2)")
+    a = ap.parse_args(argv)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    L = _lib.load()
+    M, N, K = a.m, a.n, a.k
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    copies = a.copies or max(2, math.ceil(2.2 * l2 / (N * K)))
+    copies = min(copies, max(2, int(4e9 // (N * K))))
+    g = torch.Generator(device=dev).manual_seed(0)
+    ws_list = []
+    for _ in range(copies):
+        wq, s = gemm_fp8.quantize(torch.randn(N, K, generator=g, device=dev) * 0.02)
+        ws_list.append((wq, s))
+    x = torch.randn(M, K, generator=g, device=dev).half()
+    b = torch.randn(N, generator=g, device=dev) * 0.02 if a.bias else None
+    y = torch.empty(M, N, dtype=torch.float16, device=dev)
+    packed = torch.empty(M, dtype=torch.int64, device=dev)
+    nws = (L.ddq_lm_head_argmax_workspace_size(M, N, K) if a.lm_head
+           else L.ddq_w8a16_gemm_workspace_size(M, N, K))
+    ws = gemm_fp8.workspace(dev, nws) if nws else None
+    stream = torch.cuda.current_stream(dev)
+
+    def launch(i):
+        wq, s = ws_list[i % copies]
+        if a.lm_head:
+            st = L.ddq_lm_head_argmax(x.data_ptr(), wq.data_ptr(), s.data_ptr(), M, N, K, 0,
+                                      packed.data_ptr(), None,
+                                      ws.data_ptr() if ws is not None else None,
+                                      ws.numel() if ws is not None else 0, stream.cuda_stream)
+        else:
+            st = L.ddq_w8a16_gemm(x.data_ptr(), wq.data_ptr(), s.data_ptr(),
+                                  b.data_ptr() if b is not None else None,
+                                  _lib.DTYPE_F32 if b is not None else _lib.DTYPE_NONE,
+                                  y.data_ptr(), M, N, K,
+                                  ws.data_ptr() if ws is not None else None,
+                                  ws.numel() if ws is not None else 0, stream.cuda_stream)
+        _lib.check(st, "profile launch")
+
+    for i in range(a.warmup):
+        launch(i)
+    torch.cuda.synchronize(dev)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(a.iters)]
+    torch.cuda._sleep(int(2e8))  # ~0.1 s of GPU spin so every launch below is queued first
+    for i, (e0, e1) in enumerate(evs):
+        e0.record(stream)
+        launch(a.warmup + i)
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    t = sorted(e0.elapsed_time(e1) * 1e3 for e0, e1 in evs)
+    med = t[len(t) // 2]
+    avg = sum(t) / len(t)
+    nb = algorithmic_bytes(M, N, K, a.bias, a.lm_head)
+    print(json.dumps({"M": M, "N": N, "K": K, "lm_head": a.lm_head, "copies": copies,
+                      "us_median": round(med, 3), "us_avg": round(avg, 3),
+                      "us_min": round(t[0], 3), "bytes": nb,
+                      "gbs_median": round(nb / (med * 1e-6) / 1e9, 1),
+                      "tflops_median": round(2 * M * N * K / (med * 1e-6) / 1e12, 2),
+                      "workspace": nws}))
+
+
+if __name__ == "__main__":
+    main()

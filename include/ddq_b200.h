@@ -71,9 +71,12 @@ int ddq_quantize_e4m3(const void* w, int w_dtype, int64_t N, int64_t K,
 
 /*
  * Bytes of device workspace ddq_w8a16_gemm needs for this shape (0 if none).
- * The workspace holds split-K partial sums and per-tile arrival counters.
- * It must be zero-filled once when allocated; every call leaves its counters
- * at zero again.  Calls sharing one workspace must be ordered on one stream.
+ * The first 4 KiB of a workspace hold per-tile arrival tickets, the rest
+ * split-K partial sums.  Zero-fill a workspace once when allocating it;
+ * every call leaves its tickets at zero again, so one workspace (sized for
+ * the largest shape) serves any sequence of shapes.  Calls sharing one
+ * workspace must be ordered on one stream.  The pointer must be 256-byte
+ * aligned.
  */
 size_t ddq_w8a16_gemm_workspace_size(int64_t M, int64_t N, int64_t K);
 
