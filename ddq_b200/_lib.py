@@ -29,6 +29,7 @@ _SIGNATURES = {
     "ddq_unpack_argmax": (ctypes.c_int, [_vp, _c_int64, _vp, _vp]),
     "ddq_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), _vp]),
     "ddq_set_debug": (ctypes.c_int, [ctypes.c_int, ctypes.c_uint64]),
+    "ddq_read_trace": (ctypes.c_int, [_vp, ctypes.c_int, _vp]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

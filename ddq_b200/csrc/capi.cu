@@ -175,6 +175,17 @@ extern "C" int ddq_set_debug(int flags, uint64_t wait_timeout_ns) {
   return DDQ_OK;
 }
 
+extern "C" int ddq_read_trace(uint64_t* dst, int max_ctas, void* stream) {
+  if (!dst || max_ctas < 0) return DDQ_ERR_INVALID_ARGUMENT;
+  const int n = max_ctas < kTraceCtas ? max_ctas : kTraceCtas;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (n > 0 && cudaMemcpyFromSymbolAsync(dst, g_trace, (size_t)n * kTraceSlots * sizeof(uint64_t),
+                                         0, cudaMemcpyDeviceToHost, s) != cudaSuccess)
+    return DDQ_ERR_LAUNCH;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return DDQ_ERR_LAUNCH;
+  return DDQ_OK;
+}
+
 extern "C" int ddq_device_error(int* code, void* stream) {
   if (!code) return DDQ_ERR_INVALID_ARGUMENT;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);

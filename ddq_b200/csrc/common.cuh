@@ -26,6 +26,23 @@ __device__ __forceinline__ float2 e4m3x2_to_float2(uint16_t two_bytes) {
   return __half22float2(hh);
 }
 
+// Two e4m3fn bytes of v (the pair selected by `sel`: 0x4140 = bytes 0,1;
+// 0x4342 = bytes 2,3) -> two fp16 holding exactly e4m3 value * 2^-8, in the
+// byte order of v.  Integer arithmetic only (byte permute, and, add, shift),
+// so it runs on the full-rate ALU pipes instead of the converter:
+//   e4m3 s.eeee.mmm -> fp16 bits s.0eeee.mmm0000000; the 5-bit fp16 exponent
+//   field then reads e with bias 15 instead of 7, i.e. the value times 2^-8,
+//   and e4m3 subnormals (e = 0) land on fp16 subnormals with the same factor.
+//   The sign moves from bit 7 to bit 15 by adding (b & 0x80) before the
+//   shift: bit 7 + bit 7 carries into bit 8.
+// Caller multiplies the fp32 result by 256 (exact).  The NaN codes 0x7F/0xFF
+// come out as +-1.875 (i.e. +-480 after the factor) instead of NaN; the
+// quantizer never produces them from finite weights.
+__device__ __forceinline__ uint32_t e4m3x2_to_half2_bits_x2m8(uint32_t v, uint32_t sel) {
+  const uint32_t t = __byte_perm(v, 0u, sel);  // 0x00_b1_00_b0
+  return (t + (t & 0x00800080u)) << 7;
+}
+
 // Two fp32 values -> two e4m3fn bytes (a -> low byte), round to nearest even,
 // saturating to +-448.  For |v| <= 464 this equals torch's float8_e4m3fn cast.
 __device__ __forceinline__ uint16_t float2_to_e4m3x2(float a, float b) {
@@ -50,6 +67,22 @@ extern __device__ int g_device_error;
 
 __device__ __forceinline__ void record_device_error(int code) {
   atomicCAS(&g_device_error, 0, code);
+}
+
+// Phase trace (debug flag bit 1): %globaltimer stamps per CTA, read back with
+// ddq_read_trace().  kTraceSlots stamps for each of the first kTraceCtas CTAs.
+constexpr int kTraceCtas = 2048;
+constexpr int kTraceSlots = 8;
+extern __device__ unsigned long long g_trace[kTraceCtas * kTraceSlots];
+
+__device__ __forceinline__ void trace_stamp(bool on, int slot) {
+  if (!on) return;
+  const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  if (cta < (unsigned)kTraceCtas) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    g_trace[cta * kTraceSlots + slot] = t;
+  }
 }
 
 // ----------------------------------------------------------------------------

@@ -15,6 +15,7 @@
 namespace ddq {
 
 __device__ int g_device_error = 0;
+__device__ unsigned long long g_trace[kTraceCtas * kTraceSlots];
 
 __device__ __forceinline__ uint4 ld_stream(const uint4* p) {
   uint4 r;

@@ -12,10 +12,9 @@ int launch_skinny_argmax(const __half* x, const uint8_t* wq, const float* scales
 int launch_generic(const __half* x, const uint8_t* wq, const float* scales, const void* bias,
                    int bias_dtype, __half* y, int64_t M, int64_t N, int64_t K, cudaStream_t s);
 int launch_argmax_f16(const __half* logits, int64_t B, int64_t V, int64_t* out, cudaStream_t s);
-// Split-K workspace: a fixed 4 KiB ticket region (one uint32 per output tile,
-// zero between calls) followed by the fp32 partial sums.
-constexpr size_t kTicketBytes = 4096;
-constexpr int64_t kTicketSlots = (int64_t)(kTicketBytes / 4);
+// Largest split-K factor: the splits of one tile form a thread-block cluster
+// (8 = the portable cluster size).
+constexpr int64_t kMaxSplits = 8;
 
 struct TcPlan {
   int bt;            // token tile (MMA N)
@@ -23,7 +22,7 @@ struct TcPlan {
   int kps;           // 64-wide K steps per split
   int64_t tiles;     // 128 x bt output tiles
   size_t ws_part_bytes;
-  size_t ws_bytes;   // workspace needed (0 without split-K)
+  size_t ws_bytes;   // global workspace needed (0: split-K reduces in shared memory)
 };
 TcPlan tc_plan(int64_t M, int64_t N, int64_t K, int sms);
 int launch_tc(const __half* x, const uint8_t* wq, const float* scales, const void* bias,

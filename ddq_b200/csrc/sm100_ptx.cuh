@@ -38,31 +38,40 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
                : "memory");
 }
 
+// One potentially blocking probe of the phase: the thread is suspended until
+// the phase with `parity` completes or about 0.5 ms pass (suspend-time hint),
+// so waiting roles sleep instead of taking issue slots from the converters.
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(bar), "r"(parity)
+      : "r"(bar), "r"(parity), "r"(500000u)
       : "memory");
   return ok != 0;
 }
 
-// Wait for the phase with the given parity to complete, for at most
+// Wait for the phase with the given parity to complete, for at most about
 // `timeout_ns` (or until *abort is set by another role).  Returns false on
-// timeout/abort; the caller records the error and winds down.
+// timeout/abort; the caller records the error and winds down.  The limit is
+// kept in SM cycles (clock64, cheap to read) assuming at most 2 cycles per
+// ns, so at lower clocks the wait only lasts longer; the clock and the abort
+// flag are looked at every 16th poll.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint64_t timeout_ns,
                                           volatile int* abort) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  while (true) {
+  const long long t0 = clock64();
+  const long long limit = (long long)(timeout_ns * 2ull);
+  for (uint32_t n = 1;; ++n) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*abort) return false;
-    if (globaltimer_ns() - t0 > timeout_ns) {
-      *abort = 1;
-      return false;
+    if ((n & 15u) == 0) {
+      if (*abort) return false;
+      if (clock64() - t0 > limit) {
+        *abort = 1;
+        return false;
+      }
     }
   }
 }
@@ -187,6 +196,72 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n) {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+}  // namespace ptx
+}  // namespace ddq
+
+namespace ddq {
+namespace ptx {
+
+// ---------------------------------------------------------------- more TMA
+// Prefetch a 2-D tile of a tensor map into L2 (no shared-memory destination).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* m, int c0, int c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(c0), "r"(c1)
+               : "memory");
+}
+
+// 2-D tile store shared -> global (bulk-group completion).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, uint32_t src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(c0), "r"(c1), "r"(src)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// wait until all committed bulk stores have finished reading shared memory
+__device__ __forceinline__ void bulk_wait_group_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+// wait until all committed bulk stores have completed
+__device__ __forceinline__ void bulk_wait_group0() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- clusters
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// all threads of all CTAs of the cluster (release/acquire ordering of shared memory)
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// address of the same shared-memory offset in CTA `rank` of this cluster
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
 }
 
 }  // namespace ptx

@@ -36,6 +36,10 @@ def main(argv=None):
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--copies", type=int, default=0, help="distinct weight copies (0: > 2x L2)")
+    ap.add_argument("--empty", action="store_true",
+                    help="time a trivial one-thread kernel instead (launch + event floor)")
+    ap.add_argument("--trace", action="store_true",
+                    help="also run one launch with the per-CTA phase trace and summarise it")
     a = ap.parse_args(argv)
     dev = torch.device("cuda", torch.cuda.current_device())
     L = _lib.load()
@@ -57,9 +61,13 @@ def main(argv=None):
     ws = gemm_fp8.workspace(dev, nws) if nws else None
     stream = torch.cuda.current_stream(dev)
 
+    ids = torch.empty(M, dtype=torch.int64, device=dev)
+
     def launch(i):
         wq, s = ws_list[i % copies]
-        if a.lm_head:
+        if a.empty:  # a trivial kernel of this library: the launch + event floor
+            st = L.ddq_unpack_argmax(packed.data_ptr(), 1, ids.data_ptr(), stream.cuda_stream)
+        elif a.lm_head:
             st = L.ddq_lm_head_argmax(x.data_ptr(), wq.data_ptr(), s.data_ptr(), M, N, K, 0,
                                       packed.data_ptr(), None,
                                       ws.data_ptr() if ws is not None else None,
@@ -84,6 +92,28 @@ def main(argv=None):
         launch(a.warmup + i)
         e1.record(stream)
     torch.cuda.synchronize(dev)
+    trace = None
+    if a.trace:
+        import ctypes
+        import numpy as np
+        L.ddq_set_debug(2, 0)
+        launch(a.warmup + a.iters)       # cold weights (next copy in the rotation)
+        torch.cuda.synchronize(dev)
+        L.ddq_set_debug(0, 0)
+        buf = np.zeros((2048, 8), dtype=np.uint64)
+        _lib.check(L.ddq_read_trace(buf.ctypes.data_as(ctypes.c_void_p), 2048,
+                                    stream.cuda_stream), "read trace")
+        used = buf[(buf[:, 0] > 0) & (buf[:, 7] > 0)].astype(np.int64)
+        if len(used):
+            t0 = used[:, 0].min()
+            rel = (used - t0) / 1e3
+            names = ["entry", "setup", "w_issued", "w_landed", "mma_done", "acc_ready",
+                     "epi_done", "exit"]
+            trace = {"ctas": int(len(used)), "span_us": round(float(rel[:, 7].max()), 3)}
+            for j, nm in enumerate(names):
+                col = rel[:, j][used[:, j] > 0]
+                if len(col):
+                    trace[nm] = [round(float(np.median(col)), 3), round(float(col.max()), 3)]
     t = sorted(e0.elapsed_time(e1) * 1e3 for e0, e1 in evs)
     med = t[len(t) // 2]
     avg = sum(t) / len(t)
@@ -93,7 +123,7 @@ def main(argv=None):
                       "us_min": round(t[0], 3), "bytes": nb,
                       "gbs_median": round(nb / (med * 1e-6) / 1e9, 1),
                       "tflops_median": round(2 * M * N * K / (med * 1e-6) / 1e12, 2),
-                      "workspace": nws}))
+                      "workspace": nws, "trace_us_median_max": trace}))
 
 
 if __name__ == "__main__":

@@ -140,12 +140,23 @@ int ddq_device_error(int* code, void* stream);
 
 /*
  * Test hook (no reference counterpart): set the limit of every device-side
- * bounded wait (0 = the 1 s default) and fault-injection flags for later
- * launches in this process.  flags bit 0 makes the tensor-core kernel skip
- * the accumulator-ready signal, so its epilogue wait runs out and reports
- * DDQ_ERR_TIMEOUT through ddq_device_error() without faulting the GPU.
+ * bounded wait (0 = the 1 s default) and debug flags for later launches in
+ * this process.  flags bit 0 makes the tensor-core kernel skip the
+ * accumulator-ready signal, so its epilogue wait runs out and reports
+ * DDQ_ERR_TIMEOUT through ddq_device_error() without faulting the GPU;
+ * bit 1 turns on the phase trace read by ddq_read_trace().
  */
 int ddq_set_debug(int flags, uint64_t wait_timeout_ns);
+
+/*
+ * Tracing hook (no reference counterpart): with debug flag bit 1 set, each of
+ * the first 2048 CTAs of a tensor-core launch writes 8 %globaltimer stamps
+ * (ns): entry, set-up done, first weight loads issued, first weight tile
+ * landed, last MMA issued, accumulator ready, epilogue done, exit.  This
+ * copies the stamps of the first max_ctas CTAs (8 uint64 each) to host
+ * memory `dst` and synchronises `stream`.
+ */
+int ddq_read_trace(uint64_t* dst, int max_ctas, void* stream);
 
 #ifdef __cplusplus
 }

@@ -175,3 +175,37 @@ def test_runs_on_callers_stream(g):
         y = g.f8_forward(xs, wqs, ss, bs)
     st.synchronize()
     assert o.normwise_rel_err(y.cpu().numpy(), o.f8_forward(x, wq, s, b)) <= TIGHT
+
+
+@pytest.mark.parametrize("M", [1, 16, 64, 300])
+def test_e4m3_subnormal_weights_contribute(g, M):
+    """Rows whose values (but the row maximum) quantize to e4m3 subnormals: the
+    whole output comes from subnormal codes (the tensor-core operand then holds
+    fp16 subnormals), so a flushed subnormal would show as a zero output."""
+    N, K = 256, 896
+    rng = np.random.default_rng(21)
+    w = (rng.uniform(0.5, 1.5, (N, K)) * 1e-5 * rng.choice([-1, 1], (N, K))).astype(np.float32)
+    w[:, 0] = 1.0                                    # row max -> scale 1/448
+    x = rng.normal(0, 1, (M, K)).astype(np.float16)
+    x[:, 0] = 0                                      # the max column contributes nothing
+    wq, s = o.quantize(w)
+    assert ((wq[:, 1:] & 0x78) == 0).all()           # every other code is subnormal
+    y = g.f8_forward(dev(x), dev(wq), dev(s))
+    y_ref = o.f8_forward(x, wq, s)
+    assert np.abs(y_ref.astype(np.float32)).max() > 1e-4
+    assert o.normwise_rel_err(y.cpu().numpy(), y_ref) <= TIGHT
+
+
+def test_e4m3_all_codes_decode_exactly(g):
+    """Every finite e4m3 code (both signs) times a one-hot activation row."""
+    codes = np.array([c for c in range(256) if (c & 0x7F) != 0x7F], np.uint8)   # 254 codes
+    N, K = len(codes), 16
+    wq = np.zeros((N, K), np.uint8)
+    wq[:, 3] = codes
+    s = np.ones(N, np.float32)
+    x = np.zeros((4, K), np.float16)
+    x[:, 3] = 1.0
+    y = g.f8_forward(dev(x), dev(wq), dev(s)).cpu().numpy().astype(np.float32)
+    want = o.e4m3fn_decode(codes).astype(np.float16).astype(np.float32)
+    for r in range(4):
+        np.testing.assert_array_equal(y[r], want)
