@@ -30,22 +30,32 @@ int device_sm_count(int device) {
   return g_sm_count[device];
 }
 
+// Programmatic dependent launch for the tensor-core kernels (on unless
+// DDQ_NO_PDL is set, which exists to measure what it buys).
+bool pdl_enabled() {
+  static bool v = std::getenv("DDQ_NO_PDL") == nullptr;
+  return v;
+}
+
 int check_launch() {
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? DDQ_OK : DDQ_ERR_LAUNCH;
 }
 
 namespace {
-// Smallest M routed to the tensor-core kernel (below it the CUDA-core skinny
-// kernel streams the weight); DDQ_TC_MIN_M overrides it for benchmarking.
+// Kernel choice by M: M < tc_min_m -> CUDA-core skinny kernel; M <= 64 ->
+// decode kernel (e4m3 tensor cores, activation planes); M > 64 -> prefill
+// kernel (fp16 tensor cores on converted weight tiles).  DDQ_TC_MIN_M
+// overrides the first threshold for benchmarking.
 int tc_min_m() {
   static int v = [] {
     const char* e = std::getenv("DDQ_TC_MIN_M");
-    int x = e ? std::atoi(e) : 4;
+    int x = e ? std::atoi(e) : 1;
     return x < 1 ? 1 : x;
   }();
   return v;
 }
+constexpr int64_t kDecodeMaxM = 64;
 
 // Test hooks (ddq_set_debug): bounded-wait limit and fault-injection flags.
 unsigned long long g_wait_timeout_ns = 1000000000ull;  // 1 s
@@ -80,6 +90,7 @@ extern "C" size_t ddq_w8a16_gemm_workspace_size(int64_t M, int64_t N, int64_t K)
   if (M < tc_min_m() || M <= 0 || N <= 0 || K <= 0 || K % 16 != 0) return 0;
   const int dev = current_device();
   const int sms = dev >= 0 ? device_sm_count(dev) : -1;
+  if (M <= kDecodeMaxM) return dec_plan(M, N, K, sms > 0 ? sms : 148).ws_bytes;
   return tc_plan(M, N, K, sms > 0 ? sms : 148).ws_bytes;
 }
 
@@ -97,9 +108,13 @@ extern "C" int ddq_w8a16_gemm(const void* x, const uint8_t* wq, const float* sca
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const __half* xh = reinterpret_cast<const __half*>(x);
   __half* yh = reinterpret_cast<__half*>(y);
-  if (tc_eligible(x, wq, K) && M >= tc_min_m())
+  if (tc_eligible(x, wq, K) && M >= tc_min_m()) {
+    if (M <= kDecodeMaxM)
+      return launch_dec(xh, wq, scales, bias, bias_dtype, yh, nullptr, 0, (int)M, (int)N, (int)K,
+                        workspace, workspace_bytes, g_wait_timeout_ns, g_debug_flags, s);
     return launch_tc(xh, wq, scales, bias, bias_dtype, yh, nullptr, 0, (int)M, (int)N, (int)K,
                      workspace, workspace_bytes, g_wait_timeout_ns, g_debug_flags, s);
+  }
   const bool fast = tc_eligible(x, wq, K) && K <= 12288;
   if (!fast) return launch_generic(xh, wq, scales, bias, bias_dtype, yh, M, N, K, s);
   return launch_skinny(xh, wq, scales, bias, bias_dtype, yh, (int)M, (int)N, (int)K, s);
@@ -125,7 +140,7 @@ extern "C" size_t ddq_lm_head_argmax_workspace_size(int64_t M, int64_t N, int64_
   if (mc < tc_min_m()) return 0;
   const int dev = current_device();
   const int sms = dev >= 0 ? device_sm_count(dev) : -1;
-  return tc_plan(mc, N, K, sms > 0 ? sms : 148).ws_bytes;
+  return dec_plan(mc, N, K, sms > 0 ? sms : 148).ws_bytes;
 }
 
 extern "C" int ddq_lm_head_argmax(const void* x, const uint8_t* wq, const float* scales, int64_t M,
@@ -147,9 +162,9 @@ extern "C" int ddq_lm_head_argmax(const void* x, const uint8_t* wq, const float*
       const int mc = (int)(M - m0 < kLmChunk ? M - m0 : kLmChunk);
       int st;
       if (mc >= tc_min_m())
-        st = launch_tc(xh + m0 * K, wq, scales, nullptr, DDQ_DTYPE_NONE, nullptr, pk + m0,
-                       vocab_offset, mc, (int)N, (int)K, workspace, workspace_bytes,
-                       g_wait_timeout_ns, g_debug_flags, s);
+        st = launch_dec(xh + m0 * K, wq, scales, nullptr, DDQ_DTYPE_NONE, nullptr, pk + m0,
+                        vocab_offset, mc, (int)N, (int)K, workspace, workspace_bytes,
+                        g_wait_timeout_ns, g_debug_flags, s);
       else
         st = launch_skinny_argmax(xh + m0 * K, wq, scales, pk + m0, vocab_offset, mc, (int)N,
                                   (int)K, s);

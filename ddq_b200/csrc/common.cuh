@@ -91,6 +91,7 @@ __device__ __forceinline__ void trace_stamp(bool on, int slot) {
 int device_sm_count(int device);
 int current_device();
 int check_launch();
+bool pdl_enabled();
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

@@ -29,6 +29,21 @@ int launch_tc(const __half* x, const uint8_t* wq, const float* scales, const voi
               int bias_dtype, __half* y, unsigned long long* packed, int64_t vocab_offset,
               int M, int N, int K, void* ws, size_t ws_bytes, unsigned long long timeout_ns,
               int debug_flags, cudaStream_t s);
+// Decode-shape path (tc_decode.cu): activations split into three e4m3 planes,
+// e4m3 x e4m3 tensor-core GEMM.  Needs a workspace for the planes.
+struct DecPlan {
+  int bt;             // token tile: 16, 32 or 64
+  int splits;         // split-K factor (cluster size)
+  int kps;            // 128-wide K stages per split
+  int sms;
+  size_t plane_bytes; // 3 * M * K
+  size_t ws_bytes;    // planes + per-token scales
+};
+DecPlan dec_plan(int64_t M, int64_t N, int64_t K, int sms);
+int launch_dec(const __half* x, const uint8_t* wq, const float* scales, const void* bias,
+               int bias_dtype, __half* y, unsigned long long* packed, int64_t vocab_offset, int M,
+               int N, int K, void* ws, size_t ws_bytes, unsigned long long timeout_ns,
+               int debug_flags, cudaStream_t s);
 int launch_unpack_argmax(const unsigned long long* packed, int64_t M, int64_t* ids, cudaStream_t s);
 
 }  // namespace ddq

@@ -1,0 +1,741 @@
+// tc_decode.cu - the decode-shape (M <= 64) W8A16 GEMM on the e4m3 tensor
+// cores: no per-weight-byte conversion at all.
+//
+// Converting every weight byte to fp16 costs a few ALU instructions per byte;
+// at decode rates (tens of bytes per SM clock) that is more issue bandwidth
+// than an SM has.  Instead the activations - M x K, tiny - are split once,
+// per token row m, into three e4m3 planes under a power-of-two scale:
+//     z = x[m,:] * 2^e_m        (exact; e_m puts max|z| in [128, 256))
+//     h1 = e4m3(z), h2 = e4m3(z - h1), h3 = e4m3(z - h1 - h2)   (RNE)
+// h1 + h2 + h3 equals z to within 2^-12 |z| (or 2^-10 absolute for the
+// smallest elements), finer than fp16's own 2^-11 rounding of x.  Then
+//     y[m, n] = scale[n] * 2^-e_m * sum_k Wq[n,k] * (h1 + h2 + h3)[m,k] + bias[n]
+// is one tcgen05.mma kind::f8f6f4 (e4m3 x e4m3, fp32 accumulate in TMEM)
+// per 32-wide K step with the weight tile as the 128-row A operand straight
+// from TMA and the three planes stacked as the B operand (N = 3 * BT); the
+// epilogue adds the three accumulator column blocks.
+//
+// Kernels:
+//   xsplit_kernel   one CTA per token row: row max, e_m, the three planes
+//                   (written to the workspace) and 2^-e_m.
+//   w8a16_dec_kernel  persistent (or, for few tiles, split-K over a cluster
+//                   with a distributed-shared-memory reduction, as in
+//                   tc_gemm.cu), 256 threads:
+//     warp 0     TMA producer of the e4m3 weight stages (128 rows x 128 B,
+//                128-byte swizzle); issues its first stages and an L2
+//                prefetch of the rest of its first tile before the grid
+//                dependency (the split pre-pass) resolves
+//     warp 1     MMA issuer (4 MMAs of K = 32 per stage, double-buffered TMEM
+//                accumulator)
+//     warp 2     TMA producer of the activation planes (after the grid wait)
+//     warps 4-7  epilogue: tcgen05.ld of the three blocks -> sum -> weight and
+//                token scales, bias, fp16 -> TMA tile store; or the fused
+//                lm_head's running greedy key.
+// Every mbarrier wait is bounded (see sm100_ptx.cuh); on timeout the CTA
+// records DDQ_ERR_TIMEOUT, drains its copies and MMAs, frees TMEM and exits.
+#include <cudaTypedefs.h>
+
+#include <cfloat>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "launch.cuh"
+#include "sm100_ptx.cuh"
+
+namespace ddq {
+
+constexpr int DC_BN = 128;       // weight rows per tile (MMA M)
+constexpr int DC_BK = 128;       // K elements (= bytes) per stage
+constexpr int DC_THREADS = 256;  // 8 warps
+
+// ----------------------------------------------------------------------------
+// Activation split pre-pass
+// ----------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) xsplit_kernel(const __half* __restrict__ x,
+                                                     uint8_t* __restrict__ planes,
+                                                     float* __restrict__ xscale, int M, int K) {
+  // Let the GEMM that follows launch now (it prefetches its weights while
+  // this grid and the one before it finish), then wait for x, which may be
+  // the previous kernel's output (both no-ops without PDL).
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
+  const int m = blockIdx.x;
+  const __half* xr = x + (size_t)m * K;
+  __shared__ float red[8];
+  float amax = 0.f;
+  for (int c = threadIdx.x; c < K / 8; c += blockDim.x) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(xr) + c);
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __half22float2(h[i]);
+      amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+    }
+  }
+  amax = warp_max(amax);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  amax = red[0];
+  for (int w = 1; w < (int)(blockDim.x >> 5); ++w) amax = fmaxf(amax, red[w]);
+  int ex = 0;
+  if (amax > 0.f && amax <= FLT_MAX) frexpf(amax, &ex);  // amax = f * 2^ex, f in [0.5, 1)
+  const int e = (amax > 0.f && amax <= FLT_MAX) ? 8 - ex : 0;  // max |z| in [128, 256)
+  const float up = ldexpf(1.f, e);
+  if (threadIdx.x == 0) xscale[m] = ldexpf(1.f, -e);
+  const size_t plane = (size_t)M * K;
+  uint8_t* p1 = planes + (size_t)m * K;
+  uint8_t* p2 = p1 + plane;
+  uint8_t* p3 = p2 + plane;
+  for (int c = threadIdx.x; c < K / 8; c += blockDim.x) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(xr) + c);
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+    uint32_t o1[2], o2[2], o3[2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __half22float2(h[i]);
+      const float z0 = f.x * up, z1 = f.y * up;  // exact: power-of-two scale
+      const uint16_t b1 = float2_to_e4m3x2(z0, z1);
+      const float2 d1 = e4m3x2_to_float2(b1);
+      const float r0 = z0 - d1.x, r1 = z1 - d1.y;  // exact (Sterbenz)
+      const uint16_t b2 = float2_to_e4m3x2(r0, r1);
+      const float2 d2 = e4m3x2_to_float2(b2);
+      const uint16_t b3 = float2_to_e4m3x2(r0 - d2.x, r1 - d2.y);
+      const int word = i >> 1, sh = (i & 1) * 16;
+      if (sh == 0) {
+        o1[word] = b1;
+        o2[word] = b2;
+        o3[word] = b3;
+      } else {
+        o1[word] |= (uint32_t)b1 << 16;
+        o2[word] |= (uint32_t)b2 << 16;
+        o3[word] |= (uint32_t)b3 << 16;
+      }
+    }
+    *reinterpret_cast<uint2*>(p1 + (size_t)c * 8) = make_uint2(o1[0], o1[1]);
+    *reinterpret_cast<uint2*>(p2 + (size_t)c * 8) = make_uint2(o2[0], o2[1]);
+    *reinterpret_cast<uint2*>(p3 + (size_t)c * 8) = make_uint2(o3[0], o3[1]);
+  }
+}
+
+// ----------------------------------------------------------------------------
+// Decode GEMM
+// ----------------------------------------------------------------------------
+template <int BT, int ST>
+struct DcLayout {
+  static constexpr int CH = BT < 32 ? BT : 32;           // epilogue token chunk
+  static constexpr int W_BYTES = DC_BN * DC_BK;          // 16 KB e4m3 weight stage
+  static constexpr int XP_BYTES = BT * DC_BK;            // one activation plane tile
+  static constexpr int X_BYTES = 3 * XP_BYTES;           // the three planes (B operand, N = 3 BT)
+  static constexpr int S_BYTES = W_BYTES + X_BYTES;
+  static constexpr int O_BYTES = CH * DC_BN * 2;         // output staging chunk
+  static constexpr int OFF_S = 0;
+  static constexpr int OFF_O = ST * S_BYTES;
+  static constexpr int P_BYTES = DC_BN * BT * 4;         // split-K partial (ring reused)
+  static constexpr int OFF_BAR = OFF_O + 2 * O_BYTES;
+  static constexpr int NBAR = 3 * ST + 4 + 1;            // wfull, xfull, empty; acc x2 x2; drain
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int OFF_RED = OFF_MISC + 16;
+  static constexpr int RED_BYTES = 4 * BT * 8;
+  static constexpr int BYTES = OFF_RED + RED_BYTES;
+  static constexpr int ALLOC = BYTES + 1024;
+  static constexpr int ACC_COLS = 3 * BT <= 64 ? 64 : 3 * BT <= 128 ? 128 : 256;  // per buffer
+  static_assert(S_BYTES % 1024 == 0, "stages keep 1024-B alignment");
+  static_assert(P_BYTES <= OFF_O, "split-K partial must fit in the ring");
+  static_assert(ALLOC <= 232448, "shared memory budget");
+  static_assert(3 * BT <= 256, "N = 3 BT must fit one MMA");
+};
+
+struct DcArgs {
+  const float* scales;
+  const void* bias;
+  int bias_dtype;
+  __half* y;
+  unsigned long long* packed;
+  int64_t vocab_offset;
+  const float* xscale;  // 2^-e per token row
+  int M, N, K, kps;     // kps in 128-wide stages
+  int n_tiles;
+  int y_tma;
+  unsigned long long timeout_ns;
+  int debug_flags;
+};
+
+__device__ __forceinline__ float dc_load_bias(const void* bias, int bias_dtype, int n) {
+  if (bias_dtype == DDQ_DTYPE_F16) return __half2float(reinterpret_cast<const __half*>(bias)[n]);
+  if (bias_dtype == DDQ_DTYPE_F32) return reinterpret_cast<const float*>(bias)[n];
+  return 0.f;
+}
+
+__device__ __forceinline__ unsigned long long dc_warp_max_u64(unsigned long long v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long u = __shfl_xor_sync(0xffffffffu, v, o);
+    v = u > v ? u : v;
+  }
+  return v;
+}
+
+__device__ __forceinline__ void dc_epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+__device__ __forceinline__ bool dc_wait_drain(uint32_t bar, uint32_t parity, uint64_t timeout_ns) {
+  const long long t0 = clock64();
+  const long long limit = (long long)(timeout_ns * 2ull);
+  while (!ptx::mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > limit) return false;
+  }
+  return true;
+}
+
+// Instruction descriptor, kind::f8f6f4: D fp32, A/B e4m3 (format 0), K-major.
+__host__ __device__ constexpr uint32_t idesc_e4m3_f32(int m, int n) {
+  return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(n >> 3) << 17) |
+         ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_f8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+template <int BT, int ST, bool ARGMAX>
+__global__ void __launch_bounds__(DC_THREADS, 1)
+    w8a16_dec_kernel(const __grid_constant__ CUtensorMap tm_w,
+                     const __grid_constant__ CUtensorMap tm_x,
+                     const __grid_constant__ CUtensorMap tm_y, const DcArgs args) {
+  using L = DcLayout<BT, ST>;
+  constexpr int CH = L::CH;
+  constexpr uint32_t ACC_COLS = L::ACC_COLS;
+  constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = ptx::smem_u32(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nsplit = gridDim.z;
+  const int KS = (args.K + DC_BK - 1) / DC_BK;
+  const uint64_t tmo = args.timeout_ns;
+  const bool tr = (args.debug_flags & 2) != 0;
+  const int units = args.n_tiles;  // one token tile (M <= BT)
+  const int unit0 = (int)blockIdx.x;
+  const int ustride = (nsplit > 1) ? units : (int)gridDim.x;
+  const int mvalid = min(BT, args.M);
+  auto unit_k = [&](int& kb, int& nk) {
+    kb = (nsplit > 1 ? (int)blockIdx.z : 0) * args.kps;
+    nk = max(0, min(args.kps, KS - kb));
+  };
+
+  const uint32_t bar_wfull = sbase + L::OFF_BAR;
+  const uint32_t bar_xfull = bar_wfull + 8 * ST;
+  const uint32_t bar_empty = bar_xfull + 8 * ST;
+  const uint32_t bar_accfull = bar_empty + 8 * ST;   // [2]
+  const uint32_t bar_accempty = bar_accfull + 16;    // [2]
+  const uint32_t bar_drain = bar_accempty + 16;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
+
+  if (threadIdx.x == 0) trace_stamp(tr, 0);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ST; ++s) {
+      ptx::mbar_init(bar_wfull + 8 * s, 1);
+      ptx::mbar_init(bar_xfull + 8 * s, 1);
+      ptx::mbar_init(bar_empty + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(bar_accfull + 8 * b, 1);
+      ptx::mbar_init(bar_accempty + 8 * b, 4);
+    }
+    ptx::mbar_init(bar_drain, 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+    ptx::prefetch_tmap(&tm_w);
+    ptx::prefetch_tmap(&tm_x);
+    if (args.y_tma) ptx::prefetch_tmap(&tm_y);
+  }
+  if (warp == 0) {
+    ptx::tmem_alloc(ptx::smem_u32(tmem_holder), TMEM_COLS);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  if (threadIdx.x == 0) trace_stamp(tr, 1);
+  if (threadIdx.x == 0) ptx::pdl_launch_dependents();
+
+  bool have_acc = false;
+  if (warp == 0) {
+    // ------------------------------------------------------------ weight producer
+    if (lane == 0) {
+      int g = 0;
+      bool ok = true, waited = false;
+      for (int u = unit0; u < units && ok; u += ustride) {
+        int kb, nk;
+        unit_k(kb, nk);
+        const int n0 = u * DC_BN;
+        int i = 0;
+        if (!waited) {
+          const int pre = nk < ST ? nk : ST;
+          for (; i < pre; ++i, ++g) {  // fresh stages: no wait
+            ptx::mbar_arrive_expect_tx(bar_wfull + 8 * g, L::W_BYTES);
+            ptx::tma_load_2d(sbase + L::OFF_S + g * L::S_BYTES, &tm_w, (kb + i) * DC_BK, n0,
+                             bar_wfull + 8 * g);
+          }
+          for (int i2 = ST; i2 < nk; ++i2) ptx::tma_prefetch_l2_2d(&tm_w, (kb + i2) * DC_BK, n0);
+          trace_stamp(tr, 2);
+          ptx::pdl_wait();
+          waited = true;
+        }
+        for (; i < nk; ++i, ++g) {
+          const int s = g % ST;
+          if (!ptx::mbar_wait(bar_empty + 8 * s, ((uint32_t)(g / ST) & 1u) ^ 1u, tmo, abort_flag)) {
+            ok = false;
+            break;
+          }
+          ptx::mbar_arrive_expect_tx(bar_wfull + 8 * s, L::W_BYTES);
+          ptx::tma_load_2d(sbase + L::OFF_S + s * L::S_BYTES, &tm_w, (kb + i) * DC_BK, n0,
+                           bar_wfull + 8 * s);
+        }
+      }
+      if (!waited) ptx::pdl_wait();
+      if (*abort_flag) {
+        for (int i = g > ST ? g - ST : 0; i < g; ++i)
+          dc_wait_drain(bar_wfull + 8 * (i % ST), (uint32_t)(i / ST) & 1u, tmo);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 2) {
+    // ------------------------------------------------------------ activation-plane producer
+    if (lane == 0) {
+      ptx::pdl_wait();  // the planes come from the split pre-pass
+      int g = 0;
+      bool ok = true;
+      for (int u = unit0; u < units && ok; u += ustride) {
+        int kb, nk;
+        unit_k(kb, nk);
+        for (int i = 0; i < nk; ++i, ++g) {
+          const int s = g % ST;
+          if (!ptx::mbar_wait(bar_empty + 8 * s, ((uint32_t)(g / ST) & 1u) ^ 1u, tmo, abort_flag)) {
+            ok = false;
+            break;
+          }
+          ptx::mbar_arrive_expect_tx(bar_xfull + 8 * s, L::X_BYTES);
+          const uint32_t dst = sbase + L::OFF_S + s * L::S_BYTES + L::W_BYTES;
+#pragma unroll
+          for (int p = 0; p < 3; ++p)
+            ptx::tma_load_2d(dst + p * L::XP_BYTES, &tm_x, (kb + i) * DC_BK, p * args.M,
+                             bar_xfull + 8 * s);
+        }
+      }
+      if (*abort_flag) {
+        for (int i = g > ST ? g - ST : 0; i < g; ++i)
+          dc_wait_drain(bar_xfull + 8 * (i % ST), (uint32_t)(i / ST) & 1u, tmo);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_e4m3_f32(DC_BN, 3 * BT);
+      ptx::pdl_wait();
+      bool ok = true;
+      int g = 0, it = 0;
+      for (int u = unit0; u < units && ok; u += ustride, ++it) {
+        int kb, nk;
+        unit_k(kb, nk);
+        const int b = it & 1;
+        const uint32_t tmem_d = tmem_base + (uint32_t)(b * ACC_COLS);
+        ok = ptx::mbar_wait(bar_accempty + 8 * b, ((uint32_t)(it >> 1) & 1u) ^ 1u, tmo, abort_flag);
+        if (!ok) break;
+        ptx::tc_fence_after();
+        for (int i = 0; i < nk; ++i, ++g) {
+          const int s = g % ST;
+          const uint32_t ph = (uint32_t)(g / ST) & 1u;
+          ok = ptx::mbar_wait(bar_wfull + 8 * s, ph, tmo, abort_flag) &&
+               ptx::mbar_wait(bar_xfull + 8 * s, ph, tmo, abort_flag);
+          if (!ok) break;
+          ptx::tc_fence_after();
+          const uint32_t a0 = sbase + L::OFF_S + s * L::S_BYTES;
+          const uint32_t b0 = a0 + L::W_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < DC_BK / 32; ++kk)
+            mma_f8_ss(tmem_d, ptx::smem_desc_sw128(a0 + 32 * kk), ptx::smem_desc_sw128(b0 + 32 * kk),
+                      idesc, (i | kk) != 0 ? 1u : 0u);
+          ptx::mma_commit(bar_empty + 8 * s);
+        }
+        if (!ok) break;
+        if (!(args.debug_flags & 1)) ptx::mma_commit(bar_accfull + 8 * b);
+      }
+      trace_stamp(tr, 4);
+      ptx::mma_commit(bar_drain);
+      dc_wait_drain(bar_drain, 0, tmo);
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ epilogue
+    const int e = threadIdx.x - 128;
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    ptx::pdl_wait();
+    constexpr int NB = ARGMAX ? BT : 1;
+    uint32_t best[NB];
+#pragma unroll
+    for (int j = 0; j < NB; ++j) best[j] = 0u;
+    int it = 0, ostage = 0;
+    for (int u = unit0; u < units; u += ustride, ++it) {
+      int kb, nk;
+      unit_k(kb, nk);
+      const int n0 = u * DC_BN;
+      const int b = it & 1;
+      const bool got = nk > 0 && ptx::mbar_wait(bar_accfull + 8 * b, (uint32_t)(it >> 1) & 1u, tmo,
+                                                abort_flag);
+      if (e == 0 && it == 0) trace_stamp(tr, 5);
+      if (!got) break;
+      ptx::tc_fence_after();
+      const uint32_t taddr = tmem_base + (uint32_t)(b * ACC_COLS) + ((uint32_t)(q * 32) << 16);
+      const int n = n0 + row;
+      const bool nok = n < args.N;
+      const float sc = nok ? args.scales[n] : 0.f;
+      const float bb = nok ? dc_load_bias(args.bias, args.bias_dtype, n) : 0.f;
+
+#pragma unroll
+      for (int c0 = 0; c0 < BT; c0 += CH) {
+        if (c0 < mvalid) {
+          // the three plane blocks of these CH token columns, summed in order
+          float acc[CH];
+          uint32_t r[32];
+#pragma unroll
+          for (int p = 0; p < 3; ++p) {
+            if (CH == 32) ptx::tmem_ld_32x32b_x32(taddr + p * BT + c0, r);
+            else ptx::tmem_ld_32x32b_x16(taddr + p * BT + c0, r);
+            ptx::tmem_ld_wait();
+#pragma unroll
+            for (int jj = 0; jj < CH; ++jj)
+              acc[jj] = p == 0 ? __uint_as_float(r[jj]) : acc[jj] + __uint_as_float(r[jj]);
+          }
+          if (c0 + CH >= mvalid && nsplit == 1) {
+            ptx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(bar_accempty + 8 * b);
+          }
+          if (nsplit > 1) {
+            float* part = reinterpret_cast<float*>(smem);
+#pragma unroll
+            for (int jj = 0; jj < CH; ++jj) part[(c0 + jj) * DC_BN + row] = acc[jj];
+          } else if constexpr (ARGMAX) {
+#pragma unroll
+            for (int jj = 0; jj < CH; ++jj) {
+              const float xs = __ldg(args.xscale + min(c0 + jj, args.M - 1));
+              const __half v = __float2half_rn(acc[jj] * sc * xs);
+              const uint32_t cand = (nok && c0 + jj < mvalid && __half2float(v) > -FLT_MAX)
+                                        ? ((f16_order_key(v) << 16) | (0xFFFFu - (uint32_t)it))
+                                        : 0u;
+              best[c0 + jj] = cand > best[c0 + jj] ? cand : best[c0 + jj];
+            }
+          } else if (args.y_tma) {
+            __half* stg = reinterpret_cast<__half*>(smem + L::OFF_O + ostage * L::O_BYTES);
+            if (e == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+            dc_epi_bar();
+#pragma unroll
+            for (int jj = 0; jj < CH; ++jj) {
+              const float xs = __ldg(args.xscale + min(c0 + jj, args.M - 1));
+              stg[jj * DC_BN + row] = __float2half_rn(fmaf(acc[jj] * sc, xs, bb));
+            }
+            ptx::fence_proxy_async_smem();
+            dc_epi_bar();
+            if (e == 0) {
+              ptx::tma_store_2d(&tm_y, ptx::smem_u32(stg), n0, c0);
+              ptx::bulk_commit_group();
+            }
+            ostage ^= 1;
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < CH; ++jj)
+              if (nok && c0 + jj < mvalid)
+                args.y[(size_t)(c0 + jj) * args.N + n] =
+                    __float2half_rn(fmaf(acc[jj] * sc, __ldg(args.xscale + c0 + jj), bb));
+          }
+        }
+      }
+      if (nsplit > 1) {
+        have_acc = true;
+        break;  // one unit per CTA in split mode
+      }
+    }
+    if constexpr (ARGMAX) {
+      if (nsplit == 1) {
+        unsigned long long* red = reinterpret_cast<unsigned long long*>(smem + L::OFF_RED);
+#pragma unroll
+        for (int j = 0; j < BT; ++j) {
+          if (j < mvalid) {
+            unsigned long long k = 0ull;
+            if (best[j]) {
+              const int itb = 0xFFFF - (int)(best[j] & 0xFFFFu);
+              const int nb = (unit0 + itb * ustride) * DC_BN + row;
+              k = ((unsigned long long)(best[j] >> 16) << 32) |
+                  (unsigned long long)(0xFFFFFFFFu - (uint32_t)((int64_t)nb + args.vocab_offset));
+            }
+            k = dc_warp_max_u64(k);
+            if (lane == 0) red[q * BT + j] = k;
+          }
+        }
+        dc_epi_bar();
+        for (int j = e; j < mvalid; j += 128) {
+          unsigned long long v = red[j];
+          for (int w = 1; w < 4; ++w) v = red[w * BT + j] > v ? red[w * BT + j] : v;
+          if (v) atomicMax(args.packed + j, v);
+        }
+      }
+    }
+    if (args.y_tma && e == 0) ptx::bulk_wait_group_read0();
+    __syncwarp();
+  }
+
+  if (nsplit > 1) {
+    // ------------------------------------------------------------ cluster split-K reduction
+    __syncwarp();
+    ptx::cluster_sync();
+    if (warp >= 4 && have_acc) {
+      const int n0 = unit0 * DC_BN;
+      const uint32_t rank = ptx::cluster_ctarank();
+      const int w4 = warp - 4;
+      const int r0 = 4 * lane;
+      float sc4[4], bb4[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int ne = n0 + r0 + q;
+        sc4[q] = ne < args.N ? args.scales[ne] : 0.f;
+        bb4[q] = ne < args.N ? dc_load_bias(args.bias, args.bias_dtype, ne) : 0.f;
+      }
+      for (int jb = (int)rank + w4 * nsplit; jb < mvalid; jb += 4 * nsplit) {
+        const uint32_t loc = sbase + (uint32_t)((jb * DC_BN + r0) * 4);
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int sp = 0; sp < nsplit; ++sp) {  // fixed order: deterministic
+          const float4 p = ptx::ld_dsmem_f4(ptx::mapa_shared(loc, (uint32_t)sp));
+          acc.x += p.x;
+          acc.y += p.y;
+          acc.z += p.z;
+          acc.w += p.w;
+        }
+        const float xs = __ldg(args.xscale + jb);
+        const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+        if (ARGMAX) {
+          unsigned long long k = 0ull;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int nq = n0 + r0 + q;
+            const __half v = __float2half_rn(a4[q] * sc4[q] * xs);
+            if (nq < args.N && __half2float(v) > -FLT_MAX) {
+              const unsigned long long kq =
+                  ((unsigned long long)f16_order_key(v) << 32) |
+                  (unsigned long long)(0xFFFFFFFFu - (uint32_t)((int64_t)nq + args.vocab_offset));
+              k = kq > k ? kq : k;
+            }
+          }
+          k = dc_warp_max_u64(k);
+          if (lane == 0 && k) atomicMax(args.packed + jb, k);
+        } else {
+          __half* yrow = args.y + (size_t)jb * args.N;
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            if (n0 + r0 + q < args.N) yrow[n0 + r0 + q] = __float2half_rn(fmaf(a4[q] * sc4[q], xs, bb4[q]));
+        }
+      }
+    }
+    __syncwarp();
+    ptx::cluster_sync();
+  }
+
+  if (threadIdx.x == 128) trace_stamp(tr, 6);
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+  if (threadIdx.x == 0 && *abort_flag) record_device_error(DDQ_ERR_TIMEOUT);
+  if (threadIdx.x == 0) trace_stamp(tr, 7);
+}
+
+// ============================================================================
+// Host side
+// ============================================================================
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 dc_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+int dc_tmap(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner,
+            uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+            CUtensorMapSwizzle sw) {
+  auto enc = dc_encoder();
+  if (!enc) return DDQ_ERR_DEVICE;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? DDQ_OK : DDQ_ERR_ALIGNMENT;
+}
+
+template <int BT, int ST, bool ARGMAX>
+int launch_dec_t(const DecPlan& p, const uint8_t* wq, const uint8_t* planes, DcArgs a,
+                 cudaStream_t s) {
+  using Lay = DcLayout<BT, ST>;
+  auto kern = w8a16_dec_kernel<BT, ST, ARGMAX>;
+  const int dev = current_device();
+  if (dev < 0 || dev >= 64) return DDQ_ERR_DEVICE;
+  static bool attr_set[64] = {};
+  if (!attr_set[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::ALLOC) !=
+        cudaSuccess)
+      return DDQ_ERR_LAUNCH;
+    attr_set[dev] = true;
+  }
+  CUtensorMap tm_w, tm_x, tm_y;
+  int st = dc_tmap(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, (uint64_t)a.K, (uint64_t)a.N,
+                   (uint64_t)a.K, DC_BK, DC_BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st) return st;
+  st = dc_tmap(&tm_x, CU_TENSOR_MAP_DATA_TYPE_UINT8, planes, (uint64_t)a.K, (uint64_t)a.M * 3,
+               (uint64_t)a.K, DC_BK, BT, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st) return st;
+  a.y_tma = 0;
+  std::memset(&tm_y, 0, sizeof(tm_y));
+  if (!ARGMAX && p.splits == 1 && a.N % 8 == 0 && aligned16(a.y)) {
+    st = dc_tmap(&tm_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.y, (uint64_t)a.N, (uint64_t)a.M,
+                 (uint64_t)a.N * 2, DC_BN, Lay::CH, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st) return st;
+    a.y_tma = 1;
+  }
+  a.n_tiles = (a.N + DC_BN - 1) / DC_BN;
+  cudaLaunchConfig_t cfg = {};
+  if (p.splits > 1)
+    cfg.gridDim = dim3((unsigned)a.n_tiles, 1, (unsigned)p.splits);
+  else
+    cfg.gridDim = dim3((unsigned)(a.n_tiles < p.sms ? a.n_tiles : p.sms), 1, 1);
+  cfg.blockDim = dim3(DC_THREADS);
+  cfg.dynamicSmemBytes = Lay::ALLOC;
+  cfg.stream = s;
+  cudaLaunchAttribute attrs[2];
+  int na = 0;
+  attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[na].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  ++na;
+  if (p.splits > 1) {
+    attrs[na].id = cudaLaunchAttributeClusterDimension;
+    attrs[na].val.clusterDim.x = 1;
+    attrs[na].val.clusterDim.y = 1;
+    attrs[na].val.clusterDim.z = (unsigned)p.splits;
+    ++na;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = na;
+  if (cudaLaunchKernelEx(&cfg, kern, tm_w, tm_x, tm_y, a) != cudaSuccess) {
+    cudaGetLastError();
+    return DDQ_ERR_LAUNCH;
+  }
+  return check_launch();
+}
+
+}  // namespace
+
+DecPlan dec_plan(int64_t M, int64_t N, int64_t K, int sms) {
+  DecPlan p{};
+  p.sms = sms;
+  p.bt = M <= 16 ? 16 : M <= 32 ? 32 : 64;
+  const int64_t KS = (K + DC_BK - 1) / DC_BK;
+  const int64_t tiles = (N + DC_BN - 1) / DC_BN;
+  int64_t splits = 1, kps = KS;
+  if (sms > 0 && tiles * 2 <= sms) {
+    splits = sms / tiles;
+    if (splits > kMaxSplits) splits = kMaxSplits;
+    if (splits > KS) splits = KS;
+    if (splits < 1) splits = 1;
+    kps = (KS + splits - 1) / splits;
+    splits = (KS + kps - 1) / kps;
+  }
+  p.splits = (int)splits;
+  p.kps = (int)kps;
+  p.plane_bytes = (size_t)3 * M * K;
+  p.ws_bytes = ((p.plane_bytes + 255) & ~(size_t)255) + (size_t)M * sizeof(float);
+  return p;
+}
+
+int launch_dec(const __half* x, const uint8_t* wq, const float* scales, const void* bias,
+               int bias_dtype, __half* y, unsigned long long* packed, int64_t vocab_offset, int M,
+               int N, int K, void* ws, size_t ws_bytes, unsigned long long timeout_ns,
+               int debug_flags, cudaStream_t s) {
+  const int sms = device_sm_count(current_device());
+  if (sms <= 0) return DDQ_ERR_DEVICE;
+  if (M < 1 || M > 64) return DDQ_ERR_SHAPE;
+  const DecPlan p = dec_plan(M, N, K, sms);
+  if (!ws || ws_bytes < p.ws_bytes) return DDQ_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(ws) & 255u) return DDQ_ERR_ALIGNMENT;
+  uint8_t* planes = reinterpret_cast<uint8_t*>(ws);
+  float* xscale = reinterpret_cast<float*>(planes + ((p.plane_bytes + 255) & ~(size_t)255));
+  // 1) split the activations into three e4m3 planes (PDL: waits for the
+  //    producer of x, lets the GEMM launch early)
+  {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)M);
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute at;
+    at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at.val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = &at;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, xsplit_kernel, x, planes, xscale, M, K) != cudaSuccess) {
+      cudaGetLastError();
+      return DDQ_ERR_LAUNCH;
+    }
+  }
+  // 2) the GEMM on the e4m3 tensor cores
+  DcArgs a{};
+  a.scales = scales;
+  a.bias = bias;
+  a.bias_dtype = bias_dtype;
+  a.y = y;
+  a.packed = packed;
+  a.vocab_offset = vocab_offset;
+  a.xscale = xscale;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.kps = p.kps;
+  a.timeout_ns = timeout_ns;
+  a.debug_flags = debug_flags;
+  const bool am = packed != nullptr;
+#define DDQ_DC_CASE(BT_, ST_)                                                          \
+  case BT_:                                                                            \
+    return am ? launch_dec_t<BT_, ST_, true>(p, wq, planes, a, s)                      \
+              : launch_dec_t<BT_, ST_, false>(p, wq, planes, a, s);
+  switch (p.bt) {
+    DDQ_DC_CASE(16, 9)
+    DDQ_DC_CASE(32, 7)
+    DDQ_DC_CASE(64, 5)
+    default:
+      return DDQ_ERR_SHAPE;
+  }
+#undef DDQ_DC_CASE
+}
+
+}  // namespace ddq

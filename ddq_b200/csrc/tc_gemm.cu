@@ -692,7 +692,7 @@ int launch_tc_t(const TcPlan& p, const __half* x, const uint8_t* wq, TcArgs a, i
   cudaLaunchAttribute attrs[2];
   int na = 0;
   attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attrs[na].val.programmaticStreamSerializationAllowed = 1;
+  attrs[na].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   ++na;
   if (p.splits > 1) {
     attrs[na].id = cudaLaunchAttributeClusterDimension;

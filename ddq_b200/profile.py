@@ -36,6 +36,10 @@ def main(argv=None):
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--copies", type=int, default=0, help="distinct weight copies (0: > 2x L2)")
+    ap.add_argument("--chain", action="store_true",
+                    help="time --iters launches back to back (no events between) and report per launch")
+    ap.add_argument("--torch-fp16", action="store_true",
+                    help="time torch.matmul on an fp16 weight (cuBLAS, the reference engine's path)")
     ap.add_argument("--empty", action="store_true",
                     help="time a trivial one-thread kernel instead (launch + event floor)")
     ap.add_argument("--trace", action="store_true",
@@ -63,8 +67,15 @@ def main(argv=None):
 
     ids = torch.empty(M, dtype=torch.int64, device=dev)
 
+    w16 = None
+    if a.torch_fp16:
+        w16 = [torch.randn(N, K, generator=g, device=dev).half() * 0.02 for _ in range(copies)]
+
     def launch(i):
         wq, s = ws_list[i % copies]
+        if a.torch_fp16:
+            torch.matmul(x, w16[i % copies].t(), out=y)
+            return
         if a.empty:  # a trivial kernel of this library: the launch + event floor
             st = L.ddq_unpack_argmax(packed.data_ptr(), 1, ids.data_ptr(), stream.cuda_stream)
         elif a.lm_head:
@@ -87,10 +98,20 @@ def main(argv=None):
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(a.iters)]
     torch.cuda._sleep(int(2e8))  # ~0.1 s of GPU spin so every launch below is queued first
-    for i, (e0, e1) in enumerate(evs):
-        e0.record(stream)
-        launch(a.warmup + i)
-        e1.record(stream)
+    if a.chain:
+        c0, c1 = evs[0]
+        c0.record(stream)
+        for i in range(a.iters):
+            launch(a.warmup + i)
+        c1.record(stream)
+        torch.cuda.synchronize(dev)
+        per = c0.elapsed_time(c1) * 1e3 / a.iters
+        evs = [(c0, c1)]
+    else:
+        for i, (e0, e1) in enumerate(evs):
+            e0.record(stream)
+            launch(a.warmup + i)
+            e1.record(stream)
     torch.cuda.synchronize(dev)
     trace = None
     if a.trace:
@@ -115,10 +136,15 @@ def main(argv=None):
                 if len(col):
                     trace[nm] = [round(float(np.median(col)), 3), round(float(col.max()), 3)]
     t = sorted(e0.elapsed_time(e1) * 1e3 for e0, e1 in evs)
+    if a.chain:
+        t = [per]
     med = t[len(t) // 2]
     avg = sum(t) / len(t)
     nb = algorithmic_bytes(M, N, K, a.bias, a.lm_head)
+    if a.torch_fp16:
+        nb = 2 * N * K + 2 * M * K + 2 * M * N
     print(json.dumps({"M": M, "N": N, "K": K, "lm_head": a.lm_head, "copies": copies,
+                      "mode": ("torch_fp16" if a.torch_fp16 else "ddq") + ("_chain" if a.chain else ""),
                       "us_median": round(med, 3), "us_avg": round(avg, 3),
                       "us_min": round(t[0], 3), "bytes": nb,
                       "gbs_median": round(nb / (med * 1e-6) / 1e9, 1),
