@@ -738,4 +738,71 @@ int launch_dec(const __half* x, const uint8_t* wq, const float* scales, const vo
 #undef DDQ_DC_CASE
 }
 
+// ============================================================================
+// Allocation-free entry point
+// ============================================================================
+// Some callers cannot allocate device memory at the point where they call a
+// projection: a host that hands the library a fixed, pre-planned memory
+// budget and owns every allocation itself, a serving runtime that forbids
+// cudaMalloc on its request path (it synchronises the device and can fail
+// under fragmentation), or code that records its launches into a CUDA graph
+// and may not allocate while recording.  For them the decode-shape GEMM has a
+// variant whose scratch - the three activation planes and the token scales -
+// lives in this file-scope device array instead of a caller workspace.  Every
+// GPU that loads the library holds these 1 MiB until the process exits.
+constexpr size_t kNoAllocScratchBytes = (size_t)1 << 20;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64];  // device address of g_noalloc_scratch, per device
+
+// The array's name in host code is only a host-side stand-in; the device
+// address comes from cudaGetSymbolAddress, asked once per device with that
+// device current.
+int noalloc_scratch(int dev, void** out) {
+  if (dev < 0 || dev >= 64) return DDQ_ERR_DEVICE;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) {
+      cudaGetLastError();
+      return DDQ_ERR_DEVICE;
+    }
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return DDQ_OK;
+}
+}  // namespace
+
+size_t noalloc_scratch_bytes() { return kNoAllocScratchBytes; }
+
 }  // namespace ddq
+
+using namespace ddq;
+
+extern "C" int ddq_w8a16_gemm_noalloc(const void* x, const uint8_t* wq, const float* scales,
+                                      const void* bias, int bias_dtype, void* y, int64_t M,
+                                      int64_t N, int64_t K, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return DDQ_ERR_SHAPE;
+  if (bias_dtype != DDQ_DTYPE_NONE && bias_dtype != DDQ_DTYPE_F16 && bias_dtype != DDQ_DTYPE_F32)
+    return DDQ_ERR_INVALID_ARGUMENT;
+  if (bias_dtype != DDQ_DTYPE_NONE && !bias) return DDQ_ERR_INVALID_ARGUMENT;
+  if (M == 0 || N == 0) return DDQ_OK;
+  if (!x || !wq || !scales || !y) return DDQ_ERR_INVALID_ARGUMENT;
+  // decode shapes only: 1 <= M <= 64 tokens, K a multiple of 16
+  if (M > 64 || K == 0 || K % 16 != 0 || N > 0x7fffffff || K > 0x7fffffff) return DDQ_ERR_SHAPE;
+  if (!aligned16(x) || !aligned16(wq)) return DDQ_ERR_ALIGNMENT;
+  const int dev = current_device();
+  const int sms = device_sm_count(dev);
+  if (sms <= 0) return DDQ_ERR_DEVICE;
+  // 3*M*K plane bytes (rounded up to 256) + 4*M scale bytes must fit the array
+  if (dec_plan(M, N, K, sms).ws_bytes > kNoAllocScratchBytes) return DDQ_ERR_WORKSPACE;
+  void* scratch = nullptr;
+  const int st = noalloc_scratch(dev, &scratch);
+  if (st != DDQ_OK) return st;
+  return launch_dec(reinterpret_cast<const __half*>(x), wq, scales, bias, bias_dtype,
+                    reinterpret_cast<__half*>(y), nullptr, 0, (int)M, (int)N, (int)K, scratch,
+                    kNoAllocScratchBytes, 1000000000ull, 0, reinterpret_cast<cudaStream_t>(stream));
+}

@@ -96,6 +96,27 @@ int ddq_w8a16_gemm(const void* x, const uint8_t* wq, const float* scales,
                    void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Allocation-free variant of ddq_w8a16_gemm for decode shapes.  It has no
+ * counterpart in the reference; it exists for callers that cannot allocate
+ * device memory where they call a projection (a host that pre-plans and owns
+ * every allocation, a serving runtime that bans cudaMalloc on its request
+ * path, code recording a CUDA graph).  Same inputs, output and math as
+ * ddq_w8a16_gemm on the same shapes, but the scratch lives in a 1 MiB
+ * device array inside the library (held by every GPU that loads it, until
+ * the process exits) instead of a caller workspace.
+ * Limits: 1 <= M <= 64, K % 16 == 0, 16-byte aligned x and wq, and
+ * 3*M*K (rounded up to 256) + 4*M <= 1048576 bytes; larger sizes return
+ * DDQ_ERR_WORKSPACE (M > 64 or K % 16 != 0: DDQ_ERR_SHAPE).
+ * The first call on a device looks up the array's device address (with that
+ * device current); make that first call before any stream capture.  All
+ * calls share the array: calls that may overlap on the GPU (different
+ * streams, or several host threads) race - order them on one stream.
+ */
+int ddq_w8a16_gemm_noalloc(const void* x, const uint8_t* wq, const float* scales,
+                           const void* bias, int bias_dtype, void* y,
+                           int64_t M, int64_t N, int64_t K, void* stream);
+
+/*
  * Greedy argmax over fp16 logits [B, V] -> int64 [B]; ties go to the
  * lowest index.  Replaces: sampler_d.cu:10-70 (argmax_kernel + forward).
  */
