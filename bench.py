@@ -78,10 +78,14 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self._t = threading.Thread(target=self._read, daemon=True)
             self._t.start()
+            t0 = time.time()  # the timed region starts only once sampling has begun
+            while not self.lines and time.time() - t0 < 5.0 and self.proc.poll() is None:
+                time.sleep(0.01)
+            self._n0 = len(self.lines)
         except (FileNotFoundError, OSError):
             self.proc = None
         return self
@@ -101,7 +105,7 @@ class ClockSampler:
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in self.lines[getattr(self, "_n0", 0):]:
             p = [t.strip() for t in ln.split(",")]
             if len(p) < 8:
                 continue
@@ -214,6 +218,7 @@ def run_ours(args, rank, world, device):
 
     # ---- roofline of the dominant kernel: gate/up (58% of the bytes), per launch,
     # cold weights (24 distinct 8.7 MB matrices in turn), CUDA events on the launch stream
+    peaks = load_peaks()
     per_m = {}
     dom = None
     stream = torch.cuda.current_stream(device)
@@ -237,7 +242,6 @@ def run_ours(args, rank, world, device):
         if M == 64:
             dom = (nb, avg)
 
-    peaks = load_peaks()
     nb, avg = dom
     achieved = nb / (avg * 1e-3) / 1e9
     roofline = {"kernel": "w8a16_dec_kernel + xsplit_kernel (gate/up 896->9728, M=64)",
@@ -248,6 +252,15 @@ def run_ours(args, rank, world, device):
 
     # ---- e2e through the public API, host buffers, copies inside the timed region
     e2e = run_e2e(args, wl, device, world)
+
+    # ---- the other parts of the BASELINE metric: prefill TFLOP/s (config 3),
+    # the fused lm_head (config 4) and greedy generation tok/s (config 5)
+    n_gemms, n_launches = len(calls), launches_per_step(calls)
+    del wl, calls, graph
+    torch.cuda.empty_cache()
+    prefill = None if args.skip_extra else run_prefill(args, device, world, peaks)
+    lmhead = None if args.skip_extra else run_lm_head(args, device, world, peaks)
+    generation = None if args.skip_extra else run_generation(args, device, rank, world)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -262,18 +275,122 @@ def run_ours(args, rank, world, device):
                    "layers": LAYERS, "M": list(DECODE_M),
                    "shapes": [f"{n} {k}->{nn}" + ("+bias" if b else "") for n, k, nn, b in PROJS],
                    "qkv": "q 896->896, k 896->128, v 896->128 (+bias) stacked into one GEMM",
-                   "bytes_per_step": sbytes, "gemms_per_step": len(calls),
+                   "bytes_per_step": sbytes, "gemms_per_step": n_gemms,
                    "l2": "inputs larger than L2 (357.8 MB of weights per M pass > 126 MB)",
                    "timing": "CUDA graph of one step, replayed; CUDA events; max over ranks",
                    "parallelism": f"replicas x{world}"},
         "per_m_gate_up": per_m,
+        "prefill": prefill,
+        "lm_head": lmhead,
+        "generation": generation,
         "roofline": roofline,
         "e2e": e2e,
-        "gpu_launches": launches_per_step(calls) * args.steps,
+        "gpu_launches": n_launches * args.steps,
         "clocks": clk.summary(),
         "cpu_baseline": cpu,
     }
     return line
+
+
+def run_prefill(args, device, world, peaks):
+    """Config 3: the 24-layer projection set at M = 4096 tokens (8 x 512), TFLOP/s."""
+    from ddq_b200 import _lib, gemm_fp8
+    L = _lib.load()
+    M = 4096
+    g = torch.Generator(device=device).manual_seed(77)
+    mats = []
+    for _ in range(LAYERS):
+        for name, K, N, has_bias in PROJS:
+            wq, sc = gemm_fp8.quantize(torch.randn(N, K, generator=g, device=device) * 0.02)
+            b = torch.randn(N, generator=g, device=device) * 0.02 if has_bias else None
+            mats.append((wq, sc, b, K, N))
+    xs = {K: torch.randn(M, K, generator=g, device=device).half() for K in (HIDDEN, INTER)}
+    ys = {N: torch.empty(M, N, dtype=torch.float16, device=device) for _, _, N, _ in PROJS}
+    flops = 2 * M * sum(K * N for _, K, N, _ in PROJS) * LAYERS
+    stream = torch.cuda.current_stream(device)
+
+    def one():
+        for wq, sc, b, K, N in mats:
+            st = L.ddq_w8a16_gemm(xs[K].data_ptr(), wq.data_ptr(), sc.data_ptr(),
+                                  b.data_ptr() if b is not None else None,
+                                  _lib.DTYPE_F32 if b is not None else _lib.DTYPE_NONE,
+                                  ys[N].data_ptr(), M, N, K, None, 0, stream.cuda_stream)
+            _lib.check(st, "prefill gemm")
+    for _ in range(2):
+        one()
+    torch.cuda.synchronize(device)
+    reps = 5
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        one()
+    e1.record()
+    torch.cuda.synchronize(device)
+    ms = reduce_max(e0.elapsed_time(e1), world, device) / reps
+    tf = flops * world / (ms * 1e-3) / 1e12
+    per_gpu = flops / (ms * 1e-3) / 1e12
+    return {"workload": "config3: 24-layer projection set at M=4096 (q/k/v stacked)",
+            "tflops": round(tf, 1), "ms_per_pass": round(ms, 3), "flops_per_pass": flops,
+            "frac_of_bf16_peak_per_gpu": round(per_gpu / peaks["bf16_tflops"], 4),
+            "peak_tflops": peaks["bf16_tflops"], "peak_source": peaks["source"],
+            "kernel": "w8a16_tc_kernel (tcgen05 kind::f16, e4m3 tiles converted in smem)"}
+
+
+def run_lm_head(args, device, world, peaks):
+    """Config 4: fused lm_head 896 -> 151936 greedy argmax at M = 1, 16, 64 (one GPU's
+    full vocabulary; the vocab-sharded variant is exercised by the tests)."""
+    from ddq_b200 import gemm_fp8, lm_head
+    V = 151936
+    g = torch.Generator(device=device).manual_seed(88)
+    copies = [gemm_fp8.quantize(torch.randn(V, HIDDEN, generator=g, device=device) * 0.02)
+              for _ in range(2)]
+    out = {}
+    for M in (1, 16, 64):
+        x = torch.randn(M, HIDDEN, generator=g, device=device).half()
+        for i in range(3):
+            lm_head.lm_head_argmax(x, *copies[i % 2])
+        torch.cuda.synchronize(device)
+        reps = 10
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(reps):
+            lm_head.lm_head_argmax(x, *copies[i % 2])
+        e1.record()
+        torch.cuda.synchronize(device)
+        us = reduce_max(e0.elapsed_time(e1), world, device) * 1e3 / reps
+        nb = V * HIDDEN + 4 * V + 2 * M * HIDDEN + 8 * M
+        out[str(M)] = {"us": round(us, 2), "gbs": round(nb / (us * 1e-6) / 1e9, 1),
+                       "frac_of_hbm_peak": round(nb / (us * 1e-6) / 1e9 / peaks["hbm_gbs"], 4)}
+    del copies
+    return out
+
+
+def run_generation(args, device, rank, world):
+    """Config 5: greedy generation, 64 prompts x 512 random ids, 256 new tokens,
+    data-parallel replicas (64 / world prompts per GPU), random-init weights."""
+    from ddq_b200.engine import Config, Engine
+    cfg = Config()
+    eng = Engine.random(cfg, device, seed=99)
+    per = max(1, args.gen_prompts // world)
+    g = torch.Generator(device=device).manual_seed(1000 + rank)
+    prompts = torch.randint(0, cfg.vocab_size, (per, args.gen_prompt_len), generator=g, device=device)
+    eng.generate(prompts[:min(per, 8)], 4)           # warm-up (kernel attributes, graphs)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    toks = eng.generate(prompts, args.gen_new_tokens)
+    e1.record()
+    torch.cuda.synchronize(device)
+    ms = reduce_max(e0.elapsed_time(e1), world, device)
+    total = per * world * args.gen_new_tokens
+    del eng
+    torch.cuda.empty_cache()
+    return {"workload": f"config5: {per * world} prompts x {args.gen_prompt_len} random ids, "
+                        f"{args.gen_new_tokens} greedy tokens, replicas x{world}",
+            "tok_s": round(total / (ms * 1e-3), 1), "ms": round(ms, 1),
+            "tokens": int(total), "checksum": int(toks.sum().item()) % 1000003}
 
 
 def launches_per_step(calls):
@@ -426,12 +543,17 @@ def reduce_max(v, world, device):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--skip-extra", action="store_true",
+                    help="only the config-2 headline (no prefill / lm_head / generation)")
+    ap.add_argument("--gen-prompts", type=int, default=64)
+    ap.add_argument("--gen-prompt-len", type=int, default=512)
+    ap.add_argument("--gen-new-tokens", type=int, default=256)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

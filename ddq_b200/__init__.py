@@ -11,5 +11,6 @@ All compute goes through the C ABI of ``ddq_b200/lib/libddq_b200.so``
 (``include/ddq_b200.h``); build it with ``python -m ddq_b200.build``.
 """
 from . import gemm_fp8, sampler, lm_head  # noqa: F401
+from . import engine  # noqa: F401
 
-__all__ = ["gemm_fp8", "sampler", "lm_head"]
+__all__ = ["gemm_fp8", "sampler", "lm_head", "engine"]
