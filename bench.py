@@ -8,7 +8,7 @@ N(0, 0.02), fp16 activations from N(0, 1), fp32 biases, run at
 M in {1, 8, 32, 64}.  q, k and v run as one 896->1152 projection (their
 weights stacked at load time, as the engine does; the weight bytes are the
 same), so a layer is 4 dependent GEMMs.  One step = the 24-layer set at each
-of the four M (384 GEMMs).  `value` is algorithmic bytes (SURVEY 8d: weights + scales +
+of the four M (384 GEMMs).  `value` is algorithmic bytes (weights + scales +
 bias + activations in + outputs) per second over all ranks, in TB/s, with
 every input resident in HBM; the 357.8 MB of weights per pass exceed the
 126 MB L2, so every pass reads them from HBM.  The step is captured once in a

@@ -52,6 +52,34 @@ constexpr int DC_THREADS = 256;  // 8 warps
 // ----------------------------------------------------------------------------
 // Activation split pre-pass
 // ----------------------------------------------------------------------------
+// Split 8 fp32 values (already scaled by 2^e) into three e4m3 planes; the
+// bytes keep the element order (element 0 -> lowest byte).
+__device__ __forceinline__ void split8(const float* z, uint2& p1, uint2& p2, uint2& p3) {
+  uint32_t o1[2] = {0u, 0u}, o2[2] = {0u, 0u}, o3[2] = {0u, 0u};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float z0 = z[2 * i], z1 = z[2 * i + 1];
+    const uint16_t b1 = float2_to_e4m3x2(z0, z1);
+    const float2 d1 = e4m3x2_to_float2(b1);
+    const float r0 = z0 - d1.x, r1 = z1 - d1.y;  // exact (Sterbenz)
+    const uint16_t b2 = float2_to_e4m3x2(r0, r1);
+    const float2 d2 = e4m3x2_to_float2(b2);
+    const uint16_t b3 = float2_to_e4m3x2(r0 - d2.x, r1 - d2.y);
+    const int word = i >> 1, sh = (i & 1) * 16;
+    o1[word] |= (uint32_t)b1 << sh;
+    o2[word] |= (uint32_t)b2 << sh;
+    o3[word] |= (uint32_t)b3 << sh;
+  }
+  p1 = make_uint2(o1[0], o1[1]);
+  p2 = make_uint2(o2[0], o2[1]);
+  p3 = make_uint2(o3[0], o3[1]);
+}
+
+// One CTA (256 threads) per token row; the row's 16-byte chunks stay in
+// registers (CPT per thread), so x is read once: load, row max, scale, split,
+// store.  Rows longer than 256 * CPT * 8 elements use the CPT = 0 variant,
+// which reads the row twice.
+template <int CPT>
 __global__ void __launch_bounds__(256) xsplit_kernel(const __half* __restrict__ x,
                                                      uint8_t* __restrict__ planes,
                                                      float* __restrict__ xscale, int M, int K) {
@@ -61,60 +89,73 @@ __global__ void __launch_bounds__(256) xsplit_kernel(const __half* __restrict__ 
   ptx::pdl_launch_dependents();
   ptx::pdl_wait();
   const int m = blockIdx.x;
+  const int nch = K / 8;
   const __half* xr = x + (size_t)m * K;
-  __shared__ float red[8];
+  constexpr int R = CPT > 0 ? CPT : 1;
+  uint4 v[R];
   float amax = 0.f;
-  for (int c = threadIdx.x; c < K / 8; c += blockDim.x) {
-    const uint4 u = __ldg(reinterpret_cast<const uint4*>(xr) + c);
-    const __half2* h = reinterpret_cast<const __half2*>(&u);
+  if (CPT > 0) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 f = __half22float2(h[i]);
-      amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+    for (int j = 0; j < R; ++j) {
+      const int c = threadIdx.x + j * 256;
+      v[j] = c < nch ? __ldg(reinterpret_cast<const uint4*>(xr) + c) : make_uint4(0u, 0u, 0u, 0u);
+      const __half2* h = reinterpret_cast<const __half2*>(&v[j]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(h[i]);
+        amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+      }
+    }
+  } else {
+    for (int c = threadIdx.x; c < nch; c += 256) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(xr) + c);
+      const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(h[i]);
+        amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+      }
     }
   }
+  __shared__ float red[8];
   amax = warp_max(amax);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
   __syncthreads();
   amax = red[0];
-  for (int w = 1; w < (int)(blockDim.x >> 5); ++w) amax = fmaxf(amax, red[w]);
+#pragma unroll
+  for (int w = 1; w < 8; ++w) amax = fmaxf(amax, red[w]);
   int ex = 0;
-  if (amax > 0.f && amax <= FLT_MAX) frexpf(amax, &ex);  // amax = f * 2^ex, f in [0.5, 1)
-  const int e = (amax > 0.f && amax <= FLT_MAX) ? 8 - ex : 0;  // max |z| in [128, 256)
+  const bool finite = amax > 0.f && amax <= FLT_MAX;
+  if (finite) frexpf(amax, &ex);          // amax = f * 2^ex, f in [0.5, 1)
+  const int e = finite ? 8 - ex : 0;      // max |z| in [128, 256)
   const float up = ldexpf(1.f, e);
   if (threadIdx.x == 0) xscale[m] = ldexpf(1.f, -e);
   const size_t plane = (size_t)M * K;
   uint8_t* p1 = planes + (size_t)m * K;
-  uint8_t* p2 = p1 + plane;
-  uint8_t* p3 = p2 + plane;
-  for (int c = threadIdx.x; c < K / 8; c += blockDim.x) {
-    const uint4 u = __ldg(reinterpret_cast<const uint4*>(xr) + c);
+  auto emit = [&](int c, const uint4& u) {
     const __half2* h = reinterpret_cast<const __half2*>(&u);
-    uint32_t o1[2], o2[2], o3[2];
+    float z[8];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const float2 f = __half22float2(h[i]);
-      const float z0 = f.x * up, z1 = f.y * up;  // exact: power-of-two scale
-      const uint16_t b1 = float2_to_e4m3x2(z0, z1);
-      const float2 d1 = e4m3x2_to_float2(b1);
-      const float r0 = z0 - d1.x, r1 = z1 - d1.y;  // exact (Sterbenz)
-      const uint16_t b2 = float2_to_e4m3x2(r0, r1);
-      const float2 d2 = e4m3x2_to_float2(b2);
-      const uint16_t b3 = float2_to_e4m3x2(r0 - d2.x, r1 - d2.y);
-      const int word = i >> 1, sh = (i & 1) * 16;
-      if (sh == 0) {
-        o1[word] = b1;
-        o2[word] = b2;
-        o3[word] = b3;
-      } else {
-        o1[word] |= (uint32_t)b1 << 16;
-        o2[word] |= (uint32_t)b2 << 16;
-        o3[word] |= (uint32_t)b3 << 16;
-      }
+      z[2 * i] = f.x * up;                // exact: power-of-two scale
+      z[2 * i + 1] = f.y * up;
     }
-    *reinterpret_cast<uint2*>(p1 + (size_t)c * 8) = make_uint2(o1[0], o1[1]);
-    *reinterpret_cast<uint2*>(p2 + (size_t)c * 8) = make_uint2(o2[0], o2[1]);
-    *reinterpret_cast<uint2*>(p3 + (size_t)c * 8) = make_uint2(o3[0], o3[1]);
+    uint2 a, b, cc;
+    split8(z, a, b, cc);
+    *reinterpret_cast<uint2*>(p1 + (size_t)c * 8) = a;
+    *reinterpret_cast<uint2*>(p1 + plane + (size_t)c * 8) = b;
+    *reinterpret_cast<uint2*>(p1 + 2 * plane + (size_t)c * 8) = cc;
+  };
+  if (CPT > 0) {
+#pragma unroll
+    for (int j = 0; j < R; ++j) {
+      const int c = threadIdx.x + j * 256;
+      if (c < nch) emit(c, v[j]);
+    }
+  } else {
+    for (int c = threadIdx.x; c < nch; c += 256)
+      emit(c, __ldg(reinterpret_cast<const uint4*>(xr) + c));
   }
 }
 
@@ -123,7 +164,7 @@ __global__ void __launch_bounds__(256) xsplit_kernel(const __half* __restrict__ 
 // ----------------------------------------------------------------------------
 template <int BT, int ST>
 struct DcLayout {
-  static constexpr int CH = BT < 32 ? BT : 32;           // epilogue token chunk
+  static constexpr int CH = 16;                          // epilogue token chunk
   static constexpr int W_BYTES = DC_BN * DC_BK;          // 16 KB e4m3 weight stage
   static constexpr int XP_BYTES = BT * DC_BK;            // one activation plane tile
   static constexpr int X_BYTES = 3 * XP_BYTES;           // the three planes (B operand, N = 3 BT)
@@ -137,7 +178,8 @@ struct DcLayout {
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int OFF_RED = OFF_MISC + 16;
   static constexpr int RED_BYTES = 4 * BT * 8;
-  static constexpr int BYTES = OFF_RED + RED_BYTES;
+  static constexpr int OFF_XS = OFF_RED + RED_BYTES;  // token scales 2^-e [BT]
+  static constexpr int BYTES = OFF_XS + BT * 4;
   static constexpr int ALLOC = BYTES + 1024;
   static constexpr int ACC_COLS = 3 * BT <= 64 ? 64 : 3 * BT <= 128 ? 128 : 256;  // per buffer
   static_assert(S_BYTES % 1024 == 0, "stages keep 1024-B alignment");
@@ -382,6 +424,10 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
     const int q = warp & 3;
     const int row = q * 32 + lane;
     ptx::pdl_wait();
+    // token scales once into shared memory (written by the split pre-pass)
+    float* xs_s = reinterpret_cast<float*>(smem + L::OFF_XS);
+    if (e < BT) xs_s[e] = e < args.M ? __ldg(args.xscale + e) : 0.f;
+    dc_epi_bar();
     constexpr int NB = ARGMAX ? BT : 1;
     uint32_t best[NB];
 #pragma unroll
@@ -392,32 +438,32 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
       unit_k(kb, nk);
       const int n0 = u * DC_BN;
       const int b = it & 1;
+      // per-row weight scale and bias do not depend on the accumulator: load first
+      const int n = n0 + row;
+      const bool nok = n < args.N;
+      const float sc = nok ? args.scales[n] : 0.f;
+      const float bb = nok ? dc_load_bias(args.bias, args.bias_dtype, n) : 0.f;
       const bool got = nk > 0 && ptx::mbar_wait(bar_accfull + 8 * b, (uint32_t)(it >> 1) & 1u, tmo,
                                                 abort_flag);
       if (e == 0 && it == 0) trace_stamp(tr, 5);
       if (!got) break;
       ptx::tc_fence_after();
       const uint32_t taddr = tmem_base + (uint32_t)(b * ACC_COLS) + ((uint32_t)(q * 32) << 16);
-      const int n = n0 + row;
-      const bool nok = n < args.N;
-      const float sc = nok ? args.scales[n] : 0.f;
-      const float bb = nok ? dc_load_bias(args.bias, args.bias_dtype, n) : 0.f;
 
 #pragma unroll
       for (int c0 = 0; c0 < BT; c0 += CH) {
         if (c0 < mvalid) {
-          // the three plane blocks of these CH token columns, summed in order
+          // the three plane blocks of these CH token columns: three loads in
+          // flight, one wait, summed in plane order
           float acc[CH];
-          uint32_t r[32];
+          uint32_t r0[16], r1[16], r2[16];
+          ptx::tmem_ld_32x32b_x16(taddr + c0, r0);
+          ptx::tmem_ld_32x32b_x16(taddr + BT + c0, r1);
+          ptx::tmem_ld_32x32b_x16(taddr + 2 * BT + c0, r2);
+          ptx::tmem_ld_wait();
 #pragma unroll
-          for (int p = 0; p < 3; ++p) {
-            if (CH == 32) ptx::tmem_ld_32x32b_x32(taddr + p * BT + c0, r);
-            else ptx::tmem_ld_32x32b_x16(taddr + p * BT + c0, r);
-            ptx::tmem_ld_wait();
-#pragma unroll
-            for (int jj = 0; jj < CH; ++jj)
-              acc[jj] = p == 0 ? __uint_as_float(r[jj]) : acc[jj] + __uint_as_float(r[jj]);
-          }
+          for (int jj = 0; jj < CH; ++jj)
+            acc[jj] = (__uint_as_float(r0[jj]) + __uint_as_float(r1[jj])) + __uint_as_float(r2[jj]);
           if (c0 + CH >= mvalid && nsplit == 1) {
             ptx::tc_fence_before();
             __syncwarp();
@@ -430,8 +476,7 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
           } else if constexpr (ARGMAX) {
 #pragma unroll
             for (int jj = 0; jj < CH; ++jj) {
-              const float xs = __ldg(args.xscale + min(c0 + jj, args.M - 1));
-              const __half v = __float2half_rn(acc[jj] * sc * xs);
+              const __half v = __float2half_rn(acc[jj] * sc * xs_s[c0 + jj]);
               const uint32_t cand = (nok && c0 + jj < mvalid && __half2float(v) > -FLT_MAX)
                                         ? ((f16_order_key(v) << 16) | (0xFFFFu - (uint32_t)it))
                                         : 0u;
@@ -442,10 +487,8 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
             if (e == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
             dc_epi_bar();
 #pragma unroll
-            for (int jj = 0; jj < CH; ++jj) {
-              const float xs = __ldg(args.xscale + min(c0 + jj, args.M - 1));
-              stg[jj * DC_BN + row] = __float2half_rn(fmaf(acc[jj] * sc, xs, bb));
-            }
+            for (int jj = 0; jj < CH; ++jj)
+              stg[jj * DC_BN + row] = __float2half_rn(fmaf(acc[jj] * sc, xs_s[c0 + jj], bb));
             ptx::fence_proxy_async_smem();
             dc_epi_bar();
             if (e == 0) {
@@ -458,7 +501,7 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
             for (int jj = 0; jj < CH; ++jj)
               if (nok && c0 + jj < mvalid)
                 args.y[(size_t)(c0 + jj) * args.N + n] =
-                    __float2half_rn(fmaf(acc[jj] * sc, __ldg(args.xscale + c0 + jj), bb));
+                    __float2half_rn(fmaf(acc[jj] * sc, xs_s[c0 + jj], bb));
           }
         }
       }
@@ -522,7 +565,7 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
           acc.z += p.z;
           acc.w += p.w;
         }
-        const float xs = __ldg(args.xscale + jb);
+        const float xs = reinterpret_cast<const float*>(smem + L::OFF_XS)[jb];
         const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
         if (ARGMAX) {
           unsigned long long k = 0ull;
@@ -703,7 +746,14 @@ int launch_dec(const __half* x, const uint8_t* wq, const float* scales, const vo
     at.val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
     cfg.attrs = &at;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, xsplit_kernel, x, planes, xscale, M, K) != cudaSuccess) {
+    const int nch = K / 8;
+    cudaError_t le;
+    if (nch <= 256) le = cudaLaunchKernelEx(&cfg, xsplit_kernel<1>, x, planes, xscale, M, K);
+    else if (nch <= 512) le = cudaLaunchKernelEx(&cfg, xsplit_kernel<2>, x, planes, xscale, M, K);
+    else if (nch <= 768) le = cudaLaunchKernelEx(&cfg, xsplit_kernel<3>, x, planes, xscale, M, K);
+    else if (nch <= 1024) le = cudaLaunchKernelEx(&cfg, xsplit_kernel<4>, x, planes, xscale, M, K);
+    else le = cudaLaunchKernelEx(&cfg, xsplit_kernel<0>, x, planes, xscale, M, K);
+    if (le != cudaSuccess) {
       cudaGetLastError();
       return DDQ_ERR_LAUNCH;
     }
