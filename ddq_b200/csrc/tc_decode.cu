@@ -28,9 +28,10 @@
 //     warp 1     MMA issuer (4 MMAs of K = 32 per stage, double-buffered TMEM
 //                accumulator)
 //     warp 2     TMA producer of the activation planes (after the grid wait)
-//     warps 4-7  epilogue: tcgen05.ld of the three blocks -> sum -> weight and
-//                token scales, bias, fp16 -> TMA tile store; or the fused
-//                lm_head's running greedy key.
+//     warps 4-7  epilogue: tcgen05.ld of the three blocks (the next chunk's
+//                loads in flight while this one is stored) -> sum -> weight
+//                and token scales, bias, fp16 -> a TMA store of each warp's
+//                32 x 16 tile; or the fused lm_head's running greedy key.
 // Every mbarrier wait is bounded (see sm100_ptx.cuh); on timeout the CTA
 // records DDQ_ERR_TIMEOUT, drains its copies and MMAs, frees TMEM and exits.
 #include <cudaTypedefs.h>
@@ -47,7 +48,7 @@ namespace ddq {
 
 constexpr int DC_BN = 128;       // weight rows per tile (MMA M)
 constexpr int DC_BK = 128;       // K elements (= bytes) per stage
-constexpr int DC_THREADS = 256;  // 8 warps
+constexpr int DC_THREADS = 384;  // 12 warps
 
 // ----------------------------------------------------------------------------
 // Activation split pre-pass
@@ -169,11 +170,11 @@ struct DcLayout {
   static constexpr int XP_BYTES = BT * DC_BK;            // one activation plane tile
   static constexpr int X_BYTES = 3 * XP_BYTES;           // the three planes (B operand, N = 3 BT)
   static constexpr int S_BYTES = W_BYTES + X_BYTES;
-  static constexpr int O_BYTES = CH * DC_BN * 2;         // output staging chunk
   static constexpr int OFF_S = 0;
-  static constexpr int OFF_O = ST * S_BYTES;
   static constexpr int P_BYTES = DC_BN * BT * 4;         // split-K partial (ring reused)
-  static constexpr int OFF_BAR = OFF_O + 2 * O_BYTES;
+  static constexpr int OW_BYTES = CH * 32 * 2;          // one warp's output staging chunk
+  static constexpr int OFF_O = ST * S_BYTES;             // 8 warps x 2 staging buffers
+  static constexpr int OFF_BAR = OFF_O + 16 * OW_BYTES;
   static constexpr int NBAR = 3 * ST + 4 + 1;            // wfull, xfull, empty; acc x2 x2; drain
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int OFF_RED = OFF_MISC + 16;
@@ -183,7 +184,8 @@ struct DcLayout {
   static constexpr int ALLOC = BYTES + 1024;
   static constexpr int ACC_COLS = 3 * BT <= 64 ? 64 : 3 * BT <= 128 ? 128 : 256;  // per buffer
   static_assert(S_BYTES % 1024 == 0, "stages keep 1024-B alignment");
-  static_assert(P_BYTES <= OFF_O, "split-K partial must fit in the ring");
+  static_assert(OFF_XS % 16 == 0, "token scales are read as float4");
+  static_assert(P_BYTES <= ST * S_BYTES, "split-K partial must fit in the ring");
   static_assert(ALLOC <= 232448, "shared memory budget");
   static_assert(3 * BT <= 256, "N = 3 BT must fit one MMA");
 };
@@ -218,7 +220,28 @@ __device__ __forceinline__ unsigned long long dc_warp_max_u64(unsigned long long
   return v;
 }
 
-__device__ __forceinline__ void dc_epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// The three plane blocks (columns c, BT + c, 2 BT + c) of CH = 16 token columns.
+template <int BT>
+__device__ __forceinline__ void dc_ld_chunk_t(uint32_t taddr, int c, uint32_t (&r)[3][16]) {
+  ptx::tmem_ld_32x32b_x16(taddr + (uint32_t)c, r[0]);
+  ptx::tmem_ld_32x32b_x16(taddr + (uint32_t)(BT + c), r[1]);
+  ptx::tmem_ld_32x32b_x16(taddr + (uint32_t)(2 * BT + c), r[2]);
+}
+#define dc_ld_chunk(taddr, c, r) dc_ld_chunk_t<BT>(taddr, c, r)
+
+// Ties the loaded registers to the preceding tcgen05.wait::ld: no use of them
+// can be scheduled above the wait.
+__device__ __forceinline__ void dc_reg_fence(uint32_t (&r)[3][16]) {
+#pragma unroll
+  for (int p = 0; p < 3; ++p)
+    asm volatile(""
+                 : "+r"(r[p][0]), "+r"(r[p][1]), "+r"(r[p][2]), "+r"(r[p][3]), "+r"(r[p][4]),
+                   "+r"(r[p][5]), "+r"(r[p][6]), "+r"(r[p][7]), "+r"(r[p][8]), "+r"(r[p][9]),
+                   "+r"(r[p][10]), "+r"(r[p][11]), "+r"(r[p][12]), "+r"(r[p][13]),
+                   "+r"(r[p][14]), "+r"(r[p][15])::"memory");
+}
+
+__device__ __forceinline__ void dc_epi_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 __device__ __forceinline__ bool dc_wait_drain(uint32_t bar, uint32_t parity, uint64_t timeout_ns) {
   const long long t0 = clock64();
@@ -290,7 +313,7 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(bar_accfull + 8 * b, 1);
-      ptx::mbar_init(bar_accempty + 8 * b, 4);
+      ptx::mbar_init(bar_accempty + 8 * b, 8);
     }
     ptx::mbar_init(bar_drain, 1);
     *abort_flag = 0;
@@ -420,15 +443,22 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
     __syncwarp();
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue
+    // Two groups of four warps (two warps per SM sub-partition, so one
+    // group's TMEM loads and stores overlap the other's arithmetic); group g
+    // takes the CH-token chunks ci with ci % 2 == g.  Warp w reads TMEM lanes
+    // 32 (w % 4) .. 32 (w % 4) + 31, so both groups cover all 128 rows.
     const int e = threadIdx.x - 128;
     const int q = warp & 3;
+    const int grp = (warp - 4) >> 2;
     const int row = q * 32 + lane;
     ptx::pdl_wait();
     // token scales once into shared memory (written by the split pre-pass)
     float* xs_s = reinterpret_cast<float*>(smem + L::OFF_XS);
     if (e < BT) xs_s[e] = e < args.M ? __ldg(args.xscale + e) : 0.f;
     dc_epi_bar();
-    constexpr int NB = ARGMAX ? BT : 1;
+    constexpr int NCH = BT / CH;                // chunks per tile
+    constexpr int NCG = (NCH + 1) / 2;          // chunks per group (at most)
+    constexpr int NB = ARGMAX ? NCG * CH : 1;   // running best per owned token
     uint32_t best[NB];
 #pragma unroll
     for (int j = 0; j < NB; ++j) best[j] = 0u;
@@ -449,26 +479,33 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
       if (!got) break;
       ptx::tc_fence_after();
       const uint32_t taddr = tmem_base + (uint32_t)(b * ACC_COLS) + ((uint32_t)(q * 32) << 16);
-
+      const int nch = (mvalid + CH - 1) / CH;
 #pragma unroll
-      for (int c0 = 0; c0 < BT; c0 += CH) {
-        if (c0 < mvalid) {
-          // the three plane blocks of these CH token columns: three loads in
-          // flight, one wait, summed in plane order
-          float acc[CH];
-          uint32_t r0[16], r1[16], r2[16];
-          ptx::tmem_ld_32x32b_x16(taddr + c0, r0);
-          ptx::tmem_ld_32x32b_x16(taddr + BT + c0, r1);
-          ptx::tmem_ld_32x32b_x16(taddr + 2 * BT + c0, r2);
+      for (int cl = 0; cl < NCG; ++cl) {
+        const int ci = 2 * cl + grp;
+        if (ci < nch) {
+          const int c0 = ci * CH;
+          // token scales 2^-e of these columns, into registers before the
+          // stores (read between them they would be ordered behind each one)
+          float xsr[CH];
+#pragma unroll
+          for (int j4 = 0; j4 < CH / 4; ++j4) {
+            const float4 v = reinterpret_cast<const float4*>(xs_s + c0)[j4];
+            xsr[4 * j4] = v.x;
+            xsr[4 * j4 + 1] = v.y;
+            xsr[4 * j4 + 2] = v.z;
+            xsr[4 * j4 + 3] = v.w;
+          }
+          uint32_t rr[3][16];
+          dc_ld_chunk(taddr, c0, rr);
           ptx::tmem_ld_wait();
+          dc_reg_fence(rr);
+          // the three plane blocks summed in plane order
+          float acc[CH];
 #pragma unroll
           for (int jj = 0; jj < CH; ++jj)
-            acc[jj] = (__uint_as_float(r0[jj]) + __uint_as_float(r1[jj])) + __uint_as_float(r2[jj]);
-          if (c0 + CH >= mvalid && nsplit == 1) {
-            ptx::tc_fence_before();
-            __syncwarp();
-            if (lane == 0) ptx::mbar_arrive(bar_accempty + 8 * b);
-          }
+            acc[jj] = (__uint_as_float(rr[0][jj]) + __uint_as_float(rr[1][jj])) +
+                      __uint_as_float(rr[2][jj]);
           if (nsplit > 1) {
             float* part = reinterpret_cast<float*>(smem);
 #pragma unroll
@@ -476,32 +513,36 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
           } else if constexpr (ARGMAX) {
 #pragma unroll
             for (int jj = 0; jj < CH; ++jj) {
-              const __half v = __float2half_rn(acc[jj] * sc * xs_s[c0 + jj]);
+              const __half v = __float2half_rn(acc[jj] * sc * xsr[jj]);
               const uint32_t cand = (nok && c0 + jj < mvalid && __half2float(v) > -FLT_MAX)
                                         ? ((f16_order_key(v) << 16) | (0xFFFFu - (uint32_t)it))
                                         : 0u;
-              best[c0 + jj] = cand > best[c0 + jj] ? cand : best[c0 + jj];
+              uint32_t& bj = best[cl * CH + jj];
+              bj = cand > bj ? cand : bj;
             }
           } else if (args.y_tma) {
-            __half* stg = reinterpret_cast<__half*>(smem + L::OFF_O + ostage * L::O_BYTES);
-            if (e == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-            dc_epi_bar();
+            // each warp stages its 32 rows x CH tokens and stores them with its
+            // own TMA store: no barrier across the epilogue warps
+            __half* stg = reinterpret_cast<__half*>(smem + L::OFF_O +
+                                                    (2 * (warp - 4) + ostage) * L::OW_BYTES);
+            if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+            __syncwarp();
 #pragma unroll
             for (int jj = 0; jj < CH; ++jj)
-              stg[jj * DC_BN + row] = __float2half_rn(fmaf(acc[jj] * sc, xs_s[c0 + jj], bb));
+              stg[jj * 32 + lane] = __float2half_rn(fmaf(acc[jj] * sc, xsr[jj], bb));
             ptx::fence_proxy_async_smem();
-            dc_epi_bar();
-            if (e == 0) {
-              ptx::tma_store_2d(&tm_y, ptx::smem_u32(stg), n0, c0);
+            __syncwarp();
+            if (lane == 0 && n0 + q * 32 < args.N) {
+              ptx::tma_store_2d(&tm_y, ptx::smem_u32(stg), n0 + q * 32, c0);
               ptx::bulk_commit_group();
             }
             ostage ^= 1;
           } else {
+            __half* yp = args.y + (size_t)c0 * args.N + n;
 #pragma unroll
             for (int jj = 0; jj < CH; ++jj)
               if (nok && c0 + jj < mvalid)
-                args.y[(size_t)(c0 + jj) * args.N + n] =
-                    __float2half_rn(fmaf(acc[jj] * sc, xs_s[c0 + jj], bb));
+                yp[(size_t)jj * args.N] = __float2half_rn(fmaf(acc[jj] * sc, xsr[jj], bb));
           }
         }
       }
@@ -509,33 +550,42 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
         have_acc = true;
         break;  // one unit per CTA in split mode
       }
+      // every epilogue warp releases the accumulator once its TMEM loads are done
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(bar_accempty + 8 * b);
     }
+    if (args.y_tma && lane == 0) ptx::bulk_wait_group_read0();
     if constexpr (ARGMAX) {
       if (nsplit == 1) {
         unsigned long long* red = reinterpret_cast<unsigned long long*>(smem + L::OFF_RED);
 #pragma unroll
-        for (int j = 0; j < BT; ++j) {
-          if (j < mvalid) {
-            unsigned long long k = 0ull;
-            if (best[j]) {
-              const int itb = 0xFFFF - (int)(best[j] & 0xFFFFu);
-              const int nb = (unit0 + itb * ustride) * DC_BN + row;
-              k = ((unsigned long long)(best[j] >> 16) << 32) |
-                  (unsigned long long)(0xFFFFFFFFu - (uint32_t)((int64_t)nb + args.vocab_offset));
+        for (int cl = 0; cl < NCG; ++cl) {
+#pragma unroll
+          for (int jj = 0; jj < CH; ++jj) {
+            const int j = (2 * cl + grp) * CH + jj;
+            if (j < mvalid) {
+              const uint32_t bj = best[cl * CH + jj];
+              unsigned long long k = 0ull;
+              if (bj) {
+                const int itb = 0xFFFF - (int)(bj & 0xFFFFu);
+                const int nb = (unit0 + itb * ustride) * DC_BN + row;
+                k = ((unsigned long long)(bj >> 16) << 32) |
+                    (unsigned long long)(0xFFFFFFFFu - (uint32_t)((int64_t)nb + args.vocab_offset));
+              }
+              k = dc_warp_max_u64(k);
+              if (lane == 0) red[q * BT + j] = k;
             }
-            k = dc_warp_max_u64(k);
-            if (lane == 0) red[q * BT + j] = k;
           }
         }
         dc_epi_bar();
-        for (int j = e; j < mvalid; j += 128) {
+        for (int j = e; j < mvalid; j += 256) {
           unsigned long long v = red[j];
           for (int w = 1; w < 4; ++w) v = red[w * BT + j] > v ? red[w * BT + j] : v;
           if (v) atomicMax(args.packed + j, v);
         }
       }
     }
-    if (args.y_tma && e == 0) ptx::bulk_wait_group_read0();
     __syncwarp();
   }
 
@@ -546,7 +596,7 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
     if (warp >= 4 && have_acc) {
       const int n0 = unit0 * DC_BN;
       const uint32_t rank = ptx::cluster_ctarank();
-      const int w4 = warp - 4;
+      const int w8 = warp - 4;
       const int r0 = 4 * lane;
       float sc4[4], bb4[4];
 #pragma unroll
@@ -555,7 +605,7 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
         sc4[q] = ne < args.N ? args.scales[ne] : 0.f;
         bb4[q] = ne < args.N ? dc_load_bias(args.bias, args.bias_dtype, ne) : 0.f;
       }
-      for (int jb = (int)rank + w4 * nsplit; jb < mvalid; jb += 4 * nsplit) {
+      for (int jb = (int)rank + w8 * nsplit; jb < mvalid; jb += 8 * nsplit) {
         const uint32_t loc = sbase + (uint32_t)((jb * DC_BN + r0) * 4);
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int sp = 0; sp < nsplit; ++sp) {  // fixed order: deterministic
@@ -664,7 +714,7 @@ int launch_dec_t(const DecPlan& p, const uint8_t* wq, const uint8_t* planes, DcA
   std::memset(&tm_y, 0, sizeof(tm_y));
   if (!ARGMAX && p.splits == 1 && a.N % 8 == 0 && aligned16(a.y)) {
     st = dc_tmap(&tm_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.y, (uint64_t)a.N, (uint64_t)a.M,
-                 (uint64_t)a.N * 2, DC_BN, Lay::CH, CU_TENSOR_MAP_SWIZZLE_NONE);
+                 (uint64_t)a.N * 2, 32, Lay::CH, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (st) return st;
     a.y_tma = 1;
   }
