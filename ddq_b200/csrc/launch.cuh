@@ -34,7 +34,7 @@ int launch_tc(const __half* x, const uint8_t* wq, const float* scales, const voi
 struct DecPlan {
   int bt;             // token tile: 16, 32 or 64
   int splits;         // split-K factor (cluster size)
-  int kps;            // 128-wide K stages per split
+  int kps;            // K stages (dc_stage_k(bt) bytes each) per split
   int sms;
   size_t plane_bytes; // 3 * M * K
   size_t ws_bytes;    // planes + per-token scales

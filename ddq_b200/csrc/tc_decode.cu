@@ -47,8 +47,12 @@
 namespace ddq {
 
 constexpr int DC_BN = 128;       // weight rows per tile (MMA M)
-constexpr int DC_BK = 128;       // K elements (= bytes) per stage
+constexpr int DC_AK = 128;       // K bytes per 128-byte swizzle atom (one TMA box)
 constexpr int DC_THREADS = 384;  // 12 warps
+
+// K bytes per pipeline stage: two swizzle atoms (8 MMAs per barrier round
+// trip) where the ring still holds enough stages, one for the 64-token tile.
+__host__ __device__ constexpr int dc_stage_k(int bt) { return bt <= 32 ? 256 : 128; }
 
 // ----------------------------------------------------------------------------
 // Activation split pre-pass
@@ -163,27 +167,32 @@ __global__ void __launch_bounds__(256) xsplit_kernel(const __half* __restrict__ 
 // ----------------------------------------------------------------------------
 // Decode GEMM
 // ----------------------------------------------------------------------------
-template <int BT, int ST>
+// A stage holds KB bytes of K (NA = KB / 128 swizzle atoms) of the weight
+// tile and of the three activation planes.
+template <int BT, int ST, int KB>
 struct DcLayout {
   static constexpr int CH = 16;                          // epilogue token chunk
-  static constexpr int W_BYTES = DC_BN * DC_BK;          // 16 KB e4m3 weight stage
-  static constexpr int XP_BYTES = BT * DC_BK;            // one activation plane tile
-  static constexpr int X_BYTES = 3 * XP_BYTES;           // the three planes (B operand, N = 3 BT)
+  static constexpr int NA = KB / DC_AK;                  // atoms per stage
+  static constexpr int WA_BYTES = DC_BN * DC_AK;         // 16 KB: one weight atom
+  static constexpr int XA_BYTES = 3 * BT * DC_AK;        // one atom of the three planes
+  static constexpr int W_BYTES = NA * WA_BYTES;
+  static constexpr int X_BYTES = NA * XA_BYTES;          // B operand rows: plane p, token m -> p BT + m
   static constexpr int S_BYTES = W_BYTES + X_BYTES;
   static constexpr int OFF_S = 0;
   static constexpr int P_BYTES = DC_BN * BT * 4;         // split-K partial (ring reused)
   static constexpr int OW_BYTES = CH * 32 * 2;          // one warp's output staging chunk
   static constexpr int OFF_O = ST * S_BYTES;             // 8 warps x 2 staging buffers
   static constexpr int OFF_BAR = OFF_O + 16 * OW_BYTES;
-  static constexpr int NBAR = 3 * ST + 4 + 1;            // wfull, xfull, empty; acc x2 x2; drain
-  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int NBAR = 2 * ST + 4 + 1;            // full, empty; acc x2 x2; drain
+  static constexpr int OFF_MISC = (OFF_BAR + NBAR * 8 + 15) & ~15;
   static constexpr int OFF_RED = OFF_MISC + 16;
   static constexpr int RED_BYTES = 4 * BT * 8;
   static constexpr int OFF_XS = OFF_RED + RED_BYTES;  // token scales 2^-e [BT]
   static constexpr int BYTES = OFF_XS + BT * 4;
   static constexpr int ALLOC = BYTES + 1024;
   static constexpr int ACC_COLS = 3 * BT <= 64 ? 64 : 3 * BT <= 128 ? 128 : 256;  // per buffer
-  static_assert(S_BYTES % 1024 == 0, "stages keep 1024-B alignment");
+  static_assert(S_BYTES % 1024 == 0 && XA_BYTES % 1024 == 0, "atoms keep 1024-B alignment");
+  static_assert(KB == 128 || KB == 256, "stage K bytes");
   static_assert(OFF_XS % 16 == 0, "token scales are read as float4");
   static_assert(P_BYTES <= ST * S_BYTES, "split-K partial must fit in the ring");
   static_assert(ALLOC <= 232448, "shared memory budget");
@@ -198,7 +207,7 @@ struct DcArgs {
   unsigned long long* packed;
   int64_t vocab_offset;
   const float* xscale;  // 2^-e per token row
-  int M, N, K, kps;     // kps in 128-wide stages
+  int M, N, K, kps;     // kps in stages of KB bytes of K
   int n_tiles;
   int y_tma;
   unsigned long long timeout_ns;
@@ -268,12 +277,12 @@ __device__ __forceinline__ void mma_f8_ss(uint32_t d_tmem, uint64_t a_desc, uint
       : "memory");
 }
 
-template <int BT, int ST, bool ARGMAX>
+template <int BT, int ST, int KB, bool ARGMAX>
 __global__ void __launch_bounds__(DC_THREADS, 1)
     w8a16_dec_kernel(const __grid_constant__ CUtensorMap tm_w,
                      const __grid_constant__ CUtensorMap tm_x,
                      const __grid_constant__ CUtensorMap tm_y, const DcArgs args) {
-  using L = DcLayout<BT, ST>;
+  using L = DcLayout<BT, ST, KB>;
   constexpr int CH = L::CH;
   constexpr uint32_t ACC_COLS = L::ACC_COLS;
   constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
@@ -283,7 +292,7 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
   const uint32_t sbase = ptx::smem_u32(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nsplit = gridDim.z;
-  const int KS = (args.K + DC_BK - 1) / DC_BK;
+  const int KS = (args.K + KB - 1) / KB;
   const uint64_t tmo = args.timeout_ns;
   const bool tr = (args.debug_flags & 2) != 0;
   const int units = args.n_tiles;  // one token tile (M <= BT)
@@ -295,9 +304,9 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
     nk = max(0, min(args.kps, KS - kb));
   };
 
-  const uint32_t bar_wfull = sbase + L::OFF_BAR;
-  const uint32_t bar_xfull = bar_wfull + 8 * ST;
-  const uint32_t bar_empty = bar_xfull + 8 * ST;
+  // full[s]: both producers arrive (expect_tx) and their TMA bytes land
+  const uint32_t bar_full = sbase + L::OFF_BAR;
+  const uint32_t bar_empty = bar_full + 8 * ST;
   const uint32_t bar_accfull = bar_empty + 8 * ST;   // [2]
   const uint32_t bar_accempty = bar_accfull + 16;    // [2]
   const uint32_t bar_drain = bar_accempty + 16;
@@ -307,8 +316,7 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
   if (threadIdx.x == 0) trace_stamp(tr, 0);
   if (threadIdx.x == 0) {
     for (int s = 0; s < ST; ++s) {
-      ptx::mbar_init(bar_wfull + 8 * s, 1);
-      ptx::mbar_init(bar_xfull + 8 * s, 1);
+      ptx::mbar_init(bar_full + 8 * s, 2);
       ptx::mbar_init(bar_empty + 8 * s, 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -333,10 +341,24 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
   if (threadIdx.x == 0) trace_stamp(tr, 1);
   if (threadIdx.x == 0) ptx::pdl_launch_dependents();
 
+  // K atoms of stage index ks that hold data (the last stage may be short)
+  auto stage_atoms = [&](int ks) {
+    const int rem = args.K - ks * KB;
+    return rem >= KB ? L::NA : (rem + DC_AK - 1) / DC_AK;
+  };
+
   bool have_acc = false;
   if (warp == 0) {
     // ------------------------------------------------------------ weight producer
     if (lane == 0) {
+      auto issue_w = [&](int s, int ks, int n0) {
+        const int na = stage_atoms(ks);
+        const uint32_t full = bar_full + 8 * s;
+        ptx::mbar_arrive_expect_tx(full, (uint32_t)(na * L::WA_BYTES));
+        for (int a = 0; a < na; ++a)
+          ptx::tma_load_2d(sbase + L::OFF_S + s * L::S_BYTES + a * L::WA_BYTES, &tm_w,
+                           ks * KB + a * DC_AK, n0, full);
+      };
       int g = 0;
       bool ok = true, waited = false;
       for (int u = unit0; u < units && ok; u += ustride) {
@@ -346,12 +368,10 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
         int i = 0;
         if (!waited) {
           const int pre = nk < ST ? nk : ST;
-          for (; i < pre; ++i, ++g) {  // fresh stages: no wait
-            ptx::mbar_arrive_expect_tx(bar_wfull + 8 * g, L::W_BYTES);
-            ptx::tma_load_2d(sbase + L::OFF_S + g * L::S_BYTES, &tm_w, (kb + i) * DC_BK, n0,
-                             bar_wfull + 8 * g);
-          }
-          for (int i2 = ST; i2 < nk; ++i2) ptx::tma_prefetch_l2_2d(&tm_w, (kb + i2) * DC_BK, n0);
+          for (; i < pre; ++i, ++g) issue_w(g, kb + i, n0);  // fresh stages: no wait
+          for (int i2 = ST; i2 < nk; ++i2)
+            for (int a = 0; a < stage_atoms(kb + i2); ++a)
+              ptx::tma_prefetch_l2_2d(&tm_w, (kb + i2) * KB + a * DC_AK, n0);
           trace_stamp(tr, 2);
           ptx::pdl_wait();
           waited = true;
@@ -362,20 +382,20 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
             ok = false;
             break;
           }
-          ptx::mbar_arrive_expect_tx(bar_wfull + 8 * s, L::W_BYTES);
-          ptx::tma_load_2d(sbase + L::OFF_S + s * L::S_BYTES, &tm_w, (kb + i) * DC_BK, n0,
-                           bar_wfull + 8 * s);
+          issue_w(s, kb + i, n0);
         }
       }
       if (!waited) ptx::pdl_wait();
       if (*abort_flag) {
         for (int i = g > ST ? g - ST : 0; i < g; ++i)
-          dc_wait_drain(bar_wfull + 8 * (i % ST), (uint32_t)(i / ST) & 1u, tmo);
+          dc_wait_drain(bar_full + 8 * (i % ST), (uint32_t)(i / ST) & 1u, tmo);
       }
     }
     __syncwarp();
   } else if (warp == 2) {
     // ------------------------------------------------------------ activation-plane producer
+    // one 3-D box {128 B of K, BT tokens, 3 planes} per atom: the B operand
+    // rows p BT + m, tokens m >= M zero-filled
     if (lane == 0) {
       ptx::pdl_wait();  // the planes come from the split pre-pass
       int g = 0;
@@ -389,17 +409,17 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
             ok = false;
             break;
           }
-          ptx::mbar_arrive_expect_tx(bar_xfull + 8 * s, L::X_BYTES);
+          const int na = stage_atoms(kb + i);
+          const uint32_t full = bar_full + 8 * s;
+          ptx::mbar_arrive_expect_tx(full, (uint32_t)(na * L::XA_BYTES));
           const uint32_t dst = sbase + L::OFF_S + s * L::S_BYTES + L::W_BYTES;
-#pragma unroll
-          for (int p = 0; p < 3; ++p)
-            ptx::tma_load_2d(dst + p * L::XP_BYTES, &tm_x, (kb + i) * DC_BK, p * args.M,
-                             bar_xfull + 8 * s);
+          for (int a = 0; a < na; ++a)
+            ptx::tma_load_3d(dst + a * L::XA_BYTES, &tm_x, (kb + i) * KB + a * DC_AK, 0, 0, full);
         }
       }
       if (*abort_flag) {
         for (int i = g > ST ? g - ST : 0; i < g; ++i)
-          dc_wait_drain(bar_xfull + 8 * (i % ST), (uint32_t)(i / ST) & 1u, tmo);
+          dc_wait_drain(bar_full + 8 * (i % ST), (uint32_t)(i / ST) & 1u, tmo);
       }
     }
     __syncwarp();
@@ -407,6 +427,9 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_e4m3_f32(DC_BN, 3 * BT);
+      // descriptor of stage 0's weight atom 0; other atoms and K steps are
+      // offsets in the 16-byte address field
+      const uint64_t desc0 = ptx::smem_desc_sw128(sbase + L::OFF_S);
       ptx::pdl_wait();
       bool ok = true;
       int g = 0, it = 0;
@@ -420,17 +443,21 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
         ptx::tc_fence_after();
         for (int i = 0; i < nk; ++i, ++g) {
           const int s = g % ST;
-          const uint32_t ph = (uint32_t)(g / ST) & 1u;
-          ok = ptx::mbar_wait(bar_wfull + 8 * s, ph, tmo, abort_flag) &&
-               ptx::mbar_wait(bar_xfull + 8 * s, ph, tmo, abort_flag);
+          ok = ptx::mbar_wait(bar_full + 8 * s, (uint32_t)(g / ST) & 1u, tmo, abort_flag);
           if (!ok) break;
           ptx::tc_fence_after();
-          const uint32_t a0 = sbase + L::OFF_S + s * L::S_BYTES;
-          const uint32_t b0 = a0 + L::W_BYTES;
+          const int rem = args.K - (kb + i) * KB;
+          const int nkk = rem >= KB ? KB / 32 : (rem + 31) / 32;  // 32-byte K steps with data
+          const uint64_t dw = desc0 + (uint64_t)((s * L::S_BYTES) >> 4);
+          const uint64_t dx = dw + (uint64_t)(L::W_BYTES >> 4);
 #pragma unroll
-          for (int kk = 0; kk < DC_BK / 32; ++kk)
-            mma_f8_ss(tmem_d, ptx::smem_desc_sw128(a0 + 32 * kk), ptx::smem_desc_sw128(b0 + 32 * kk),
-                      idesc, (i | kk) != 0 ? 1u : 0u);
+          for (int a = 0; a < L::NA; ++a)
+#pragma unroll
+            for (int kk = 0; kk < DC_AK / 32; ++kk)
+              if (a * (DC_AK / 32) + kk < nkk)
+                mma_f8_ss(tmem_d, dw + (uint64_t)((a * L::WA_BYTES + 32 * kk) >> 4),
+                          dx + (uint64_t)((a * L::XA_BYTES + 32 * kk) >> 4), idesc,
+                          (i | a | kk) != 0 ? 1u : 0u);
           ptx::mma_commit(bar_empty + 8 * s);
         }
         if (!ok) break;
@@ -689,11 +716,26 @@ int dc_tmap(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t i
   return r == CUDA_SUCCESS ? DDQ_OK : DDQ_ERR_ALIGNMENT;
 }
 
-template <int BT, int ST, bool ARGMAX>
+// The activation planes [3][M][K] e4m3 as a 3-D tensor {K, M, 3}; a box
+// {128, BT, 3} lands as the B operand rows p BT + m, tokens m >= M zero.
+int dc_tmap_planes(CUtensorMap* m, const void* base, uint64_t K, uint64_t M, uint32_t bt) {
+  auto enc = dc_encoder();
+  if (!enc) return DDQ_ERR_DEVICE;
+  cuuint64_t dims[3] = {K, M, 3};
+  cuuint64_t strides[2] = {K, K * M};
+  cuuint32_t box[3] = {(cuuint32_t)DC_AK, bt, 3};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box,
+                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? DDQ_OK : DDQ_ERR_ALIGNMENT;
+}
+
+template <int BT, int ST, int KB, bool ARGMAX>
 int launch_dec_t(const DecPlan& p, const uint8_t* wq, const uint8_t* planes, DcArgs a,
                  cudaStream_t s) {
-  using Lay = DcLayout<BT, ST>;
-  auto kern = w8a16_dec_kernel<BT, ST, ARGMAX>;
+  using Lay = DcLayout<BT, ST, KB>;
+  auto kern = w8a16_dec_kernel<BT, ST, KB, ARGMAX>;
   const int dev = current_device();
   if (dev < 0 || dev >= 64) return DDQ_ERR_DEVICE;
   static bool attr_set[64] = {};
@@ -705,10 +747,9 @@ int launch_dec_t(const DecPlan& p, const uint8_t* wq, const uint8_t* planes, DcA
   }
   CUtensorMap tm_w, tm_x, tm_y;
   int st = dc_tmap(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, (uint64_t)a.K, (uint64_t)a.N,
-                   (uint64_t)a.K, DC_BK, DC_BN, CU_TENSOR_MAP_SWIZZLE_128B);
+                   (uint64_t)a.K, DC_AK, DC_BN, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st) return st;
-  st = dc_tmap(&tm_x, CU_TENSOR_MAP_DATA_TYPE_UINT8, planes, (uint64_t)a.K, (uint64_t)a.M * 3,
-               (uint64_t)a.K, DC_BK, BT, CU_TENSOR_MAP_SWIZZLE_128B);
+  st = dc_tmap_planes(&tm_x, planes, (uint64_t)a.K, (uint64_t)a.M, (uint32_t)BT);
   if (st) return st;
   a.y_tma = 0;
   std::memset(&tm_y, 0, sizeof(tm_y));
@@ -754,7 +795,7 @@ DecPlan dec_plan(int64_t M, int64_t N, int64_t K, int sms) {
   DecPlan p{};
   p.sms = sms;
   p.bt = M <= 16 ? 16 : M <= 32 ? 32 : 64;
-  const int64_t KS = (K + DC_BK - 1) / DC_BK;
+  const int64_t KS = (K + dc_stage_k(p.bt) - 1) / dc_stage_k(p.bt);
   const int64_t tiles = (N + DC_BN - 1) / DC_BN;
   int64_t splits = 1, kps = KS;
   if (sms > 0 && tiles * 2 <= sms) {
@@ -826,11 +867,11 @@ int launch_dec(const __half* x, const uint8_t* wq, const float* scales, const vo
   const bool am = packed != nullptr;
 #define DDQ_DC_CASE(BT_, ST_)                                                          \
   case BT_:                                                                            \
-    return am ? launch_dec_t<BT_, ST_, true>(p, wq, planes, a, s)                      \
-              : launch_dec_t<BT_, ST_, false>(p, wq, planes, a, s);
+    return am ? launch_dec_t<BT_, ST_, dc_stage_k(BT_), true>(p, wq, planes, a, s)     \
+              : launch_dec_t<BT_, ST_, dc_stage_k(BT_), false>(p, wq, planes, a, s);
   switch (p.bt) {
-    DDQ_DC_CASE(16, 9)
-    DDQ_DC_CASE(32, 7)
+    DDQ_DC_CASE(16, 4)
+    DDQ_DC_CASE(32, 3)
     DDQ_DC_CASE(64, 5)
     default:
       return DDQ_ERR_SHAPE;
