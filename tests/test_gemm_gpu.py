@@ -209,3 +209,25 @@ def test_e4m3_all_codes_decode_exactly(g):
     want = o.e4m3fn_decode(codes).astype(np.float16).astype(np.float32)
     for r in range(4):
         np.testing.assert_array_equal(y[r], want)
+
+
+def test_decode_calls_of_many_shapes_share_one_workspace(g):
+    """Decode-shape calls of different shapes, twice over, through one caller
+    workspace sized for the largest: each matches the oracle."""
+    from ddq_b200 import _lib
+    lib = _lib.load()
+    shapes = [(16, 1152, 896), (64, 896, 4864), (1, 9728, 896), (37, 256, 48), (64, 896, 896)]
+    need = max(lib.ddq_w8a16_gemm_workspace_size(M, N, K) for M, N, K in shapes)
+    ws = torch.zeros(need, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    for i, (M, N, K) in enumerate(shapes * 2):
+        x, w, b = gen(M, N, K, seed=100 + i)
+        wq, s = o.quantize(w)
+        y = torch.full((M, N), float("nan"), dtype=torch.float16, device="cuda")
+        xd, wqd, sd, bd = dev(x), dev(wq), dev(s), dev(b)
+        st = lib.ddq_w8a16_gemm(xd.data_ptr(), wqd.data_ptr(), sd.data_ptr(), bd.data_ptr(),
+                                _lib.DTYPE_F32, y.data_ptr(), M, N, K, ws.data_ptr(), need, stream)
+        assert st == 0, _lib.status_string(st)
+        torch.cuda.synchronize()
+        err = o.normwise_rel_err(y.cpu().numpy(), o.f8_forward(x, wq, s, b))
+        assert err <= TIGHT, (M, N, K, err)
