@@ -57,6 +57,18 @@ int tc_min_m() {
 }
 constexpr int64_t kDecodeMaxM = 64;
 
+// From this many tokens on, a GEMM expands the weights to fp16 once and runs
+// the fp16 tensor-core GEMM (tc_prefill.cu); between kDecodeMaxM and this the
+// in-kernel conversion of tc_gemm.cu is cheaper.  DDQ_PF_MIN_M overrides.
+int64_t pf_min_m() {
+  static const int64_t v = [] {
+    const char* e = std::getenv("DDQ_PF_MIN_M");
+    return e ? (int64_t)std::atoll(e) : (int64_t)128;
+  }();
+  return v;
+}
+bool pf_shape(int64_t M, int64_t N) { return M > kDecodeMaxM && M >= pf_min_m() && N % 8 == 0; }
+
 // Test hooks (ddq_set_debug): bounded-wait limit and fault-injection flags.
 unsigned long long g_wait_timeout_ns = 1000000000ull;  // 1 s
 int g_debug_flags = 0;
@@ -91,6 +103,7 @@ extern "C" size_t ddq_w8a16_gemm_workspace_size(int64_t M, int64_t N, int64_t K)
   const int dev = current_device();
   const int sms = dev >= 0 ? device_sm_count(dev) : -1;
   if (M <= kDecodeMaxM) return dec_plan(M, N, K, sms > 0 ? sms : 148).ws_bytes;
+  if (pf_shape(M, N)) return pf_workspace_bytes(N, K);
   return tc_plan(M, N, K, sms > 0 ? sms : 148).ws_bytes;
 }
 
@@ -112,6 +125,10 @@ extern "C" int ddq_w8a16_gemm(const void* x, const uint8_t* wq, const float* sca
     if (M <= kDecodeMaxM)
       return launch_dec(xh, wq, scales, bias, bias_dtype, yh, nullptr, 0, (int)M, (int)N, (int)K,
                         workspace, workspace_bytes, g_wait_timeout_ns, g_debug_flags, s);
+    if (pf_shape(M, N) && aligned16(y) && workspace &&
+        workspace_bytes >= pf_workspace_bytes(N, K))
+      return launch_pf(xh, wq, scales, bias, bias_dtype, yh, (int)M, (int)N, (int)K, workspace,
+                       workspace_bytes, g_wait_timeout_ns, g_debug_flags, s);
     return launch_tc(xh, wq, scales, bias, bias_dtype, yh, nullptr, 0, (int)M, (int)N, (int)K,
                      workspace, workspace_bytes, g_wait_timeout_ns, g_debug_flags, s);
   }

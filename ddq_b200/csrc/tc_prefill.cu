@@ -1,0 +1,441 @@
+// tc_prefill.cu - the prefill-shape (large M) W8A16 GEMM: an exact e4m3 -> fp16
+// expansion of the weight matrix, then an fp16 tcgen05 GEMM at tensor rate.
+//
+// With hundreds of tokens per weight tile the GEMM is tensor-bound, and
+// converting the e4m3 weight tile in shared memory for every token block
+// (the in-kernel conversion of tc_gemm.cu) costs more SM issue slots than the
+// MMAs themselves.  Here the conversion runs once per call instead:
+//   e4m3_to_f16_kernel   w16[n, k] = fp16(e4m3(wq[n, k]))  (exact: every e4m3
+//                        value is an fp16 value), HBM-bound, 1 byte in -> 2 out
+//   w8a16_pf_kernel      D[m, n] = sum_k x[m, k] * w16[n, k]   (fp32 in TMEM)
+//                        y[m, n] = fp16( D[m, n] * scale[n] + bias[n] )
+// so the per-row weight scale is applied to the fp32 sum, as in the
+// reference's dequantize-then-multiply semantics (gemm_FP8_d.cu:94-146).
+//
+// w8a16_pf_kernel: persistent, one CTA per SM, 384 threads; output tile =
+// 128 tokens (the MMA M, TMEM lanes) x 256 weight rows (the MMA N, TMEM
+// columns), K in stages of 64 (one 128-byte swizzle atom of fp16):
+//   warp 0      TMA producer: the x tile (128 x 64) and the w16 tile (256 x 64)
+//               of each stage on one full barrier (48 KB per stage)
+//   warp 1      MMA issuer: 4 x tcgen05.mma kind::f16 (K = 16) per stage into
+//               one of two 256-column TMEM accumulators (double buffered, so a
+//               tile's epilogue overlaps the next tile's MMAs)
+//   warps 4-11  epilogue, two groups of four over alternate 32-column chunks:
+//               tcgen05.ld -> scale, bias -> fp16 -> 64-byte-swizzled staging ->
+//               one TMA store per warp and chunk (32 tokens x 32 columns)
+// Tiles run token-tile-major across the grid (consecutive CTAs share an x
+// tile; the 2-byte weights of a 9728 x 896 projection, 17 MB, stay in L2).
+// Every mbarrier wait is bounded; on timeout the CTA records DDQ_ERR_TIMEOUT,
+// drains its copies and MMAs, frees TMEM and exits.
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "launch.cuh"
+#include "sm100_ptx.cuh"
+
+namespace ddq {
+
+constexpr int PF_BM = 128;       // tokens per tile (MMA M, TMEM lanes)
+constexpr int PF_BN = 256;       // weight rows per tile (MMA N, TMEM columns)
+constexpr int PF_BK = 64;        // K elements per stage (128 B of fp16)
+constexpr int PF_ST = 4;         // ring stages
+constexpr int PF_THREADS = 384;  // 12 warps
+constexpr int PF_CH = 32;        // epilogue column chunk
+
+struct PfLayout {
+  static constexpr int A_BYTES = PF_BM * PF_BK * 2;   // 16 KB x tile
+  static constexpr int B_BYTES = PF_BN * PF_BK * 2;   // 32 KB w16 tile
+  static constexpr int S_BYTES = A_BYTES + B_BYTES;
+  static constexpr int OW_BYTES = 32 * PF_CH * 2;     // one warp's staging (32 x 32 fp16)
+  static constexpr int OFF_O = PF_ST * S_BYTES;       // 8 warps x 1 staging buffer
+  static constexpr int OFF_SB = OFF_O + 8 * OW_BYTES;   // [2 tiles][scale 256 | bias 256] fp32
+  static constexpr int OFF_BAR = OFF_SB + 2 * 2 * PF_BN * 4;
+  static constexpr int NBAR = 2 * PF_ST + 4 + 1;      // full, empty; acc x2 x2; drain
+  static constexpr int OFF_MISC = (OFF_BAR + NBAR * 8 + 15) & ~15;
+  static constexpr int BYTES = OFF_MISC + 16;
+  static constexpr int ALLOC = BYTES + 1024;
+  static_assert(S_BYTES % 1024 == 0 && A_BYTES % 1024 == 0, "1024-B aligned operand tiles");
+  static_assert(ALLOC <= 232448, "shared memory budget");
+};
+
+struct PfArgs {
+  const float* scales;
+  const void* bias;
+  int bias_dtype;
+  int M, N, K;
+  int tiles_m, tiles_n;
+  unsigned long long timeout_ns;
+  int debug_flags;
+};
+
+__device__ __forceinline__ float pf_load_bias(const void* bias, int bias_dtype, int n) {
+  if (bias_dtype == DDQ_DTYPE_F16) return __half2float(reinterpret_cast<const __half*>(bias)[n]);
+  if (bias_dtype == DDQ_DTYPE_F32) return reinterpret_cast<const float*>(bias)[n];
+  return 0.f;
+}
+
+__device__ __forceinline__ bool pf_wait_drain(uint32_t bar, uint32_t parity, uint64_t timeout_ns) {
+  const long long t0 = clock64();
+  const long long limit = (long long)(timeout_ns * 2ull);
+  while (!ptx::mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > limit) return false;
+  }
+  return true;
+}
+
+__device__ __forceinline__ void pf_reg_fence(uint32_t (&r)[32]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])::"memory");
+  asm volatile(""
+               : "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]),
+                 "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])::"memory");
+}
+
+// Exact expansion e4m3 -> fp16, 16 bytes in, 32 bytes out per thread step.
+__global__ void __launch_bounds__(256) e4m3_to_f16_kernel(const uint8_t* __restrict__ wq,
+                                                          __half* __restrict__ w16, size_t n16) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();  // w16 may still be read by the previous GEMM
+  const uint4* src = reinterpret_cast<const uint4*>(wq);
+  uint4* dst = reinterpret_cast<uint4*>(w16);
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const uint4 v = __ldcs(src + i);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t h[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      h[2 * j] = e4m3x2_to_half2_bits((uint16_t)(w[j] & 0xFFFFu));
+      h[2 * j + 1] = e4m3x2_to_half2_bits((uint16_t)(w[j] >> 16));
+    }
+    dst[2 * i] = make_uint4(h[0], h[1], h[2], h[3]);
+    dst[2 * i + 1] = make_uint4(h[4], h[5], h[6], h[7]);
+  }
+}
+
+__global__ void __launch_bounds__(PF_THREADS, 1)
+    w8a16_pf_kernel(const __grid_constant__ CUtensorMap tm_x,
+                    const __grid_constant__ CUtensorMap tm_w,
+                    const __grid_constant__ CUtensorMap tm_y, const PfArgs args) {
+  using L = PfLayout;
+  constexpr uint32_t ACC_COLS = PF_BN;
+  constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = ptx::smem_u32(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int KS = (args.K + PF_BK - 1) / PF_BK;
+  const int units = args.tiles_m * args.tiles_n;
+  const uint64_t tmo = args.timeout_ns;
+  const bool tr = (args.debug_flags & 2) != 0;
+
+  const uint32_t bar_full = sbase + L::OFF_BAR;
+  const uint32_t bar_empty = bar_full + 8 * PF_ST;
+  const uint32_t bar_accfull = bar_empty + 8 * PF_ST;  // [2]
+  const uint32_t bar_accempty = bar_accfull + 16;      // [2]
+  const uint32_t bar_drain = bar_accempty + 16;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
+
+  if (threadIdx.x == 0) trace_stamp(tr, 0);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PF_ST; ++s) {
+      ptx::mbar_init(bar_full + 8 * s, 1);
+      ptx::mbar_init(bar_empty + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(bar_accfull + 8 * b, 1);
+      ptx::mbar_init(bar_accempty + 8 * b, 8);
+    }
+    ptx::mbar_init(bar_drain, 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+    ptx::prefetch_tmap(&tm_x);
+    ptx::prefetch_tmap(&tm_w);
+    ptx::prefetch_tmap(&tm_y);
+  }
+  if (warp == 0) {
+    ptx::tmem_alloc(ptx::smem_u32(tmem_holder), TMEM_COLS);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  if (threadIdx.x == 0) trace_stamp(tr, 1);
+  if (threadIdx.x == 0) ptx::pdl_launch_dependents();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      ptx::pdl_wait();  // x and w16 come from earlier kernels
+      int g = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const int m0 = (u / args.tiles_n) * PF_BM, n0 = (u % args.tiles_n) * PF_BN;
+        for (int ks = 0; ks < KS; ++ks, ++g) {
+          const int s = g % PF_ST;
+          if (!ptx::mbar_wait(bar_empty + 8 * s, ((uint32_t)(g / PF_ST) & 1u) ^ 1u, tmo,
+                              abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t full = bar_full + 8 * s;
+          const uint32_t dst = sbase + s * L::S_BYTES;
+          ptx::mbar_arrive_expect_tx(full, (uint32_t)L::S_BYTES);
+          ptx::tma_load_2d(dst, &tm_x, ks * PF_BK, m0, full);
+          ptx::tma_load_2d(dst + L::A_BYTES, &tm_w, ks * PF_BK, n0, full);
+        }
+      }
+      if (*abort_flag) {
+        for (int i = g > PF_ST ? g - PF_ST : 0; i < g; ++i)
+          pf_wait_drain(bar_full + 8 * (i % PF_ST), (uint32_t)(i / PF_ST) & 1u, tmo);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = ptx::idesc_f16_f32(PF_BM, PF_BN);
+      const uint64_t desc0 = ptx::smem_desc_sw128(sbase);
+      ptx::pdl_wait();
+      bool ok = true;
+      int g = 0, it = 0;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++it) {
+        const int b = it & 1;
+        const uint32_t tmem_d = tmem_base + (uint32_t)(b * ACC_COLS);
+        ok = ptx::mbar_wait(bar_accempty + 8 * b, ((uint32_t)(it >> 1) & 1u) ^ 1u, tmo, abort_flag);
+        if (!ok) break;
+        ptx::tc_fence_after();
+        for (int ks = 0; ks < KS; ++ks, ++g) {
+          const int s = g % PF_ST;
+          ok = ptx::mbar_wait(bar_full + 8 * s, (uint32_t)(g / PF_ST) & 1u, tmo, abort_flag);
+          if (!ok) break;
+          ptx::tc_fence_after();
+          const uint64_t da = desc0 + (uint64_t)((s * L::S_BYTES) >> 4);
+          const uint64_t db = da + (uint64_t)(L::A_BYTES >> 4);
+#pragma unroll
+          for (int kk = 0; kk < PF_BK / 16; ++kk)  // 32 bytes of K per MMA
+            ptx::mma_f16_ss(tmem_d, da + (uint64_t)(2 * kk), db + (uint64_t)(2 * kk), idesc,
+                            (ks | kk) != 0 ? 1u : 0u);
+          ptx::mma_commit(bar_empty + 8 * s);
+        }
+        if (!ok) break;
+        ptx::mma_commit(bar_accfull + 8 * b);
+      }
+      trace_stamp(tr, 4);
+      ptx::mma_commit(bar_drain);
+      pf_wait_drain(bar_drain, 0, tmo);
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;              // TMEM lanes 32 q .. 32 q + 31 = tokens
+    const int grp = (warp - 4) >> 2;     // column chunks grp, grp + 2, ...
+    const uint32_t stg = sbase + L::OFF_O + (uint32_t)((warp - 4) * L::OW_BYTES);
+    const int e = threadIdx.x - 128;     // 0..255: one column's scale and bias per tile
+    ptx::pdl_wait();
+    int it = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++it) {
+      const int m0 = (u / args.tiles_n) * PF_BM, n0 = (u % args.tiles_n) * PF_BN;
+      const int b = it & 1;
+      // the tile's weight scales and biases, once, into shared memory (two
+      // buffers by tile parity: the barrier below keeps every warp within one
+      // tile of the others)
+      float* sb = reinterpret_cast<float*>(smem + L::OFF_SB) + b * 2 * PF_BN;
+      {
+        const int n = n0 + e;
+        sb[e] = n < args.N ? __ldg(args.scales + n) : 0.f;
+        sb[PF_BN + e] = n < args.N ? pf_load_bias(args.bias, args.bias_dtype, n) : 0.f;
+      }
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (!ptx::mbar_wait(bar_accfull + 8 * b, (uint32_t)(it >> 1) & 1u, tmo, abort_flag)) break;
+      if (warp == 4 && lane == 0 && it == 0) trace_stamp(tr, 5);
+      ptx::tc_fence_after();
+      const uint32_t taddr = tmem_base + (uint32_t)(b * ACC_COLS) + ((uint32_t)(q * 32) << 16);
+#pragma unroll 1
+      for (int c = grp; c < PF_BN / PF_CH; c += 2) {
+        const int col0 = c * PF_CH;
+        if (n0 + col0 >= args.N) break;
+        uint32_t r[32];
+        ptx::tmem_ld_32x32b_x32(taddr + (uint32_t)col0, r);
+        // this chunk's 32 weight scales and biases (shared-memory broadcasts)
+        float sc[PF_CH], bb[PF_CH];
+#pragma unroll
+        for (int j4 = 0; j4 < PF_CH / 4; ++j4) {
+          const float4 s4 = reinterpret_cast<const float4*>(sb + col0)[j4];
+          const float4 b4 = reinterpret_cast<const float4*>(sb + PF_BN + col0)[j4];
+          sc[4 * j4] = s4.x; sc[4 * j4 + 1] = s4.y; sc[4 * j4 + 2] = s4.z; sc[4 * j4 + 3] = s4.w;
+          bb[4 * j4] = b4.x; bb[4 * j4 + 1] = b4.y; bb[4 * j4 + 2] = b4.z; bb[4 * j4 + 3] = b4.w;
+        }
+        ptx::tmem_ld_wait();
+        pf_reg_fence(r);
+        uint32_t h[PF_CH / 2];
+#pragma unroll
+        for (int j = 0; j < PF_CH / 2; ++j) {
+          const float v0 = fmaf(__uint_as_float(r[2 * j]), sc[2 * j], bb[2 * j]);
+          const float v1 = fmaf(__uint_as_float(r[2 * j + 1]), sc[2 * j + 1], bb[2 * j + 1]);
+          const __half2 hv = __floats2half2_rn(v0, v1);
+          h[j] = *reinterpret_cast<const uint32_t*>(&hv);
+        }
+        // staging: 32 rows (tokens) x 64 B, 64-byte swizzle (16-byte chunk
+        // j of row r at chunk j ^ ((r >> 1) & 3)), matching the store map
+        if (lane == 0) ptx::bulk_wait_group_read0();
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t a = stg + (uint32_t)(lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4));
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(h[4 * j]),
+                       "r"(h[4 * j + 1]), "r"(h[4 * j + 2]), "r"(h[4 * j + 3])
+                       : "memory");
+        }
+        ptx::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && m0 + q * 32 < args.M) {
+          ptx::tma_store_2d(&tm_y, stg, n0 + col0, m0 + q * 32);
+          ptx::bulk_commit_group();
+        }
+      }
+      // release the accumulator once this warp's TMEM loads are done
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(bar_accempty + 8 * b);
+    }
+    if (lane == 0) ptx::bulk_wait_group0();
+    __syncwarp();
+  }
+
+  if (threadIdx.x == 128) trace_stamp(tr, 6);
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+  if (threadIdx.x == 0 && *abort_flag) record_device_error(DDQ_ERR_TIMEOUT);
+  if (threadIdx.x == 0) trace_stamp(tr, 7);
+}
+
+// ============================================================================
+// Host side
+// ============================================================================
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 pf_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+int pf_tmap(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint32_t box_inner,
+            uint32_t box_outer, CUtensorMapSwizzle sw) {
+  auto enc = pf_encoder();
+  if (!enc) return DDQ_ERR_DEVICE;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {inner * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? DDQ_OK : DDQ_ERR_ALIGNMENT;
+}
+
+cudaLaunchAttribute pdl_attr() {
+  cudaLaunchAttribute at;
+  at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at.val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  return at;
+}
+
+}  // namespace
+
+size_t pf_workspace_bytes(int64_t N, int64_t K) { return (size_t)N * (size_t)K * 2; }
+
+int launch_pf(const __half* x, const uint8_t* wq, const float* scales, const void* bias,
+              int bias_dtype, __half* y, int M, int N, int K, void* ws, size_t ws_bytes,
+              unsigned long long timeout_ns, int debug_flags, cudaStream_t s) {
+  const int dev = current_device();
+  const int sms = device_sm_count(dev);
+  if (sms <= 0 || dev < 0 || dev >= 64) return DDQ_ERR_DEVICE;
+  if (M < 1 || N < 1 || K < 16 || K % 16 != 0) return DDQ_ERR_SHAPE;
+  if (!ws || ws_bytes < pf_workspace_bytes(N, K)) return DDQ_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(ws) & 255u) || !aligned16(x) || !aligned16(y) ||
+      (N % 8) != 0)
+    return DDQ_ERR_ALIGNMENT;
+  __half* w16 = reinterpret_cast<__half*>(ws);
+  // 1) exact e4m3 -> fp16 expansion of the weights
+  {
+    const size_t n16 = (size_t)N * (size_t)K / 16;
+    cudaLaunchConfig_t cfg = {};
+    const size_t want = (n16 + 255) / 256;
+    const size_t cap = (size_t)sms * 8;
+    cfg.gridDim = dim3((unsigned)(want < cap ? want : cap));
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute at = pdl_attr();
+    cfg.attrs = &at;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, e4m3_to_f16_kernel, wq, w16, n16) != cudaSuccess) {
+      cudaGetLastError();
+      return DDQ_ERR_LAUNCH;
+    }
+  }
+  // 2) the fp16 GEMM
+  static bool attr_set[64] = {};
+  if (!attr_set[dev]) {
+    if (cudaFuncSetAttribute(w8a16_pf_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             PfLayout::ALLOC) != cudaSuccess)
+      return DDQ_ERR_LAUNCH;
+    attr_set[dev] = true;
+  }
+  CUtensorMap tm_x, tm_w, tm_y;
+  int st = pf_tmap(&tm_x, x, (uint64_t)K, (uint64_t)M, PF_BK, PF_BM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st) return st;
+  st = pf_tmap(&tm_w, w16, (uint64_t)K, (uint64_t)N, PF_BK, PF_BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st) return st;
+  st = pf_tmap(&tm_y, y, (uint64_t)N, (uint64_t)M, PF_CH, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+  if (st) return st;
+  PfArgs a{};
+  a.scales = scales;
+  a.bias = bias;
+  a.bias_dtype = bias_dtype;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.tiles_m = (M + PF_BM - 1) / PF_BM;
+  a.tiles_n = (N + PF_BN - 1) / PF_BN;
+  a.timeout_ns = timeout_ns;
+  a.debug_flags = debug_flags;
+  const int units = a.tiles_m * a.tiles_n;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(units < sms ? units : sms));
+  cfg.blockDim = dim3(PF_THREADS);
+  cfg.dynamicSmemBytes = PfLayout::ALLOC;
+  cfg.stream = s;
+  cudaLaunchAttribute at = pdl_attr();
+  cfg.attrs = &at;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, w8a16_pf_kernel, tm_x, tm_w, tm_y, a) != cudaSuccess) {
+    cudaGetLastError();
+    return DDQ_ERR_LAUNCH;
+  }
+  return check_launch();
+}
+
+}  // namespace ddq

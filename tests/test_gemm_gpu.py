@@ -70,8 +70,8 @@ def test_f8_forward_decode_shapes(g, M, N, K):
     assert err <= TIGHT, err
 
 
-@pytest.mark.parametrize("M", [100, 512, 1000])
-@pytest.mark.parametrize("N,K", [(896, 896), (1152, 896), (896, 4864)])
+@pytest.mark.parametrize("M", [100, 129, 512, 1000])
+@pytest.mark.parametrize("N,K", [(896, 896), (1152, 896), (896, 4864), (9728, 896), (1000, 136)])
 def test_f8_forward_larger_m(g, M, N, K):
     x, w, b = gen(M, N, K, seed=M + N + K)
     wq, s = o.quantize(w)
@@ -99,9 +99,10 @@ def test_unaligned_activation_pointer_uses_generic_path(g):
     assert o.normwise_rel_err(y.cpu().numpy(), o.f8_forward(x, wq, s, b)) <= TIGHT
 
 
+@pytest.mark.parametrize("M", [8, 700])
 @pytest.mark.parametrize("bias_kind", ["none", "empty", "f16", "f32"])
-def test_bias_variants(g, bias_kind):
-    x, w, b = gen(8, 896, 896, seed=13)
+def test_bias_variants(g, bias_kind, M):
+    x, w, b = gen(M, 896, 896, seed=13)
     wq, s = o.quantize(w)
     if bias_kind == "none":
         bt, bref = None, None
