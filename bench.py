@@ -325,13 +325,16 @@ def run_prefill(args, device, world, peaks):
     ys = {N: torch.empty(M, N, dtype=torch.float16, device=device) for _, _, N, _ in PROJS}
     flops = 2 * M * sum(K * N for _, K, N, _ in PROJS) * LAYERS
     stream = torch.cuda.current_stream(device)
+    nws = max(L.ddq_w8a16_gemm_workspace_size(M, N, K) for _, K, N, _ in PROJS)
+    ws = gemm_fp8.workspace(device, nws) if nws else None
+    ws_ptr, ws_bytes = (ws.data_ptr(), ws.numel()) if ws is not None else (None, 0)
 
     def one():
         for wq, sc, b, K, N in mats:
             st = L.ddq_w8a16_gemm(xs[K].data_ptr(), wq.data_ptr(), sc.data_ptr(),
                                   b.data_ptr() if b is not None else None,
                                   _lib.DTYPE_F32 if b is not None else _lib.DTYPE_NONE,
-                                  ys[N].data_ptr(), M, N, K, None, 0, stream.cuda_stream)
+                                  ys[N].data_ptr(), M, N, K, ws_ptr, ws_bytes, stream.cuda_stream)
             _lib.check(st, "prefill gemm")
     for _ in range(2):
         one()
@@ -350,7 +353,7 @@ def run_prefill(args, device, world, peaks):
             "tflops": round(tf, 1), "ms_per_pass": round(ms, 3), "flops_per_pass": flops,
             "frac_of_bf16_peak_per_gpu": round(per_gpu / peaks["bf16_tflops"], 4),
             "peak_tflops": peaks["bf16_tflops"], "peak_source": peaks["source"],
-            "kernel": "w8a16_tc_kernel (tcgen05 kind::f16, e4m3 tiles converted in smem)"}
+            "kernel": "e4m3_to_f16_kernel + w8a16_pf_kernel (exact weight expansion, tcgen05 kind::f16)"}
 
 
 def run_lm_head(args, device, world, peaks):
@@ -401,18 +404,26 @@ def run_generation(args, device, rank, world):
     e1.record()
     torch.cuda.synchronize(device)
     ms = reduce_max(e0.elapsed_time(e1), world, device)
+    # the prefill share of that time: the same prompts, first token only
+    e0.record()
+    eng.generate(prompts, 1)
+    e1.record()
+    torch.cuda.synchronize(device)
+    prefill_ms = reduce_max(e0.elapsed_time(e1), world, device)
     total = per * world * args.gen_new_tokens
     del eng
     torch.cuda.empty_cache()
     return {"workload": f"config5: {per * world} prompts x {args.gen_prompt_len} random ids, "
                         f"{args.gen_new_tokens} greedy tokens, replicas x{world}",
             "tok_s": round(total / (ms * 1e-3), 1), "ms": round(ms, 1),
+            "prefill_ms": round(prefill_ms, 1),
+            "decode_ms_per_step": round((ms - prefill_ms) / max(1, args.gen_new_tokens - 1), 3),
             "tokens": int(total), "checksum": int(toks.sum().item()) % 1000003}
 
 
 def launches_per_step(calls):
     """Kernels of this library per step: a decode-shape GEMM (M <= 64) is the
-    activation-split pre-pass plus the GEMM; larger M is one kernel."""
+    activation-split pre-pass plus the GEMM."""
     return sum(2 if c[6] <= 64 else 1 for c in calls)
 
 

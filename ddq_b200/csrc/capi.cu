@@ -137,6 +137,39 @@ extern "C" int ddq_w8a16_gemm(const void* x, const uint8_t* wq, const float* sca
   return launch_skinny(xh, wq, scales, bias, bias_dtype, yh, (int)M, (int)N, (int)K, s);
 }
 
+extern "C" size_t ddq_w8a16_gemm_swiglu_workspace_size(int64_t M, int64_t I, int64_t K) {
+  if (M <= 0 || I <= 0 || K <= 0 || K % 16 != 0 || I % 16 != 0) return 0;
+  const int dev = current_device();
+  const int sms = dev >= 0 ? device_sm_count(dev) : -1;
+  if (M <= kDecodeMaxM) return dec_plan(M, 2 * I, K, sms > 0 ? sms : 148, true).ws_bytes;
+  return pf_workspace_bytes(2 * I, K);
+}
+
+extern "C" int ddq_w8a16_gemm_swiglu(const void* x, const uint8_t* wq_gu, const float* scales_gu,
+                                     const void* bias, int bias_dtype, void* z, int64_t M,
+                                     int64_t I, int64_t K, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+  if (M < 0 || I < 0 || K < 0) return DDQ_ERR_SHAPE;
+  if (bias_dtype != DDQ_DTYPE_NONE && bias_dtype != DDQ_DTYPE_F16 && bias_dtype != DDQ_DTYPE_F32)
+    return DDQ_ERR_INVALID_ARGUMENT;
+  if (bias_dtype != DDQ_DTYPE_NONE && !bias) return DDQ_ERR_INVALID_ARGUMENT;
+  if (M == 0 || I == 0) return DDQ_OK;
+  if (!x || !wq_gu || !scales_gu || !z) return DDQ_ERR_INVALID_ARGUMENT;
+  if (I % 16 != 0 || K == 0 || K % 16 != 0 || M > 0x7fffffff || 2 * I > 0x7fffffff ||
+      K > 0x7fffffff)
+    return DDQ_ERR_SHAPE;
+  if (!aligned16(x) || !aligned16(wq_gu) || !aligned16(z)) return DDQ_ERR_ALIGNMENT;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const __half* xh = reinterpret_cast<const __half*>(x);
+  __half* zh = reinterpret_cast<__half*>(z);
+  if (M <= kDecodeMaxM)
+    return launch_dec(xh, wq_gu, scales_gu, bias, bias_dtype, zh, nullptr, 0, (int)M, (int)(2 * I),
+                      (int)K, workspace, workspace_bytes, g_wait_timeout_ns, g_debug_flags, s,
+                      true);
+  return launch_pf(xh, wq_gu, scales_gu, bias, bias_dtype, zh, (int)M, (int)(2 * I), (int)K,
+                   workspace, workspace_bytes, g_wait_timeout_ns, g_debug_flags, s, true);
+}
+
 extern "C" int ddq_argmax_f16(const void* logits, int64_t B, int64_t V, int64_t* out,
                               void* stream) {
   if (B < 0 || V < 0) return DDQ_ERR_SHAPE;

@@ -39,17 +39,18 @@ struct DecPlan {
   size_t plane_bytes; // 3 * M * K
   size_t ws_bytes;    // planes + per-token scales
 };
-DecPlan dec_plan(int64_t M, int64_t N, int64_t K, int sms);
+DecPlan dec_plan(int64_t M, int64_t N, int64_t K, int sms, bool no_split = false);
 int launch_dec(const __half* x, const uint8_t* wq, const float* scales, const void* bias,
                int bias_dtype, __half* y, unsigned long long* packed, int64_t vocab_offset, int M,
                int N, int K, void* ws, size_t ws_bytes, unsigned long long timeout_ns,
-               int debug_flags, cudaStream_t s);
+               int debug_flags, cudaStream_t s, bool swiglu = false);
 // Prefill shapes: exact e4m3 -> fp16 weight expansion into the workspace
 // (N * K * 2 bytes), then the fp16 tensor-core GEMM (tc_prefill.cu).
 size_t pf_workspace_bytes(int64_t N, int64_t K);
 int launch_pf(const __half* x, const uint8_t* wq, const float* scales, const void* bias,
               int bias_dtype, __half* y, int M, int N, int K, void* ws, size_t ws_bytes,
-              unsigned long long timeout_ns, int debug_flags, cudaStream_t s);
+              unsigned long long timeout_ns, int debug_flags, cudaStream_t s,
+              bool swiglu = false);
 int launch_unpack_argmax(const unsigned long long* packed, int64_t M, int64_t* ids, cudaStream_t s);
 
 }  // namespace ddq

@@ -209,6 +209,7 @@ struct DcArgs {
   const float* xscale;  // 2^-e per token row
   int M, N, K, kps;     // kps in stages of KB bytes of K
   int n_tiles;
+  int out_n;            // output row length: N, or N / 2 for the SwiGLU epilogue
   int y_tma;
   unsigned long long timeout_ns;
   int debug_flags;
@@ -277,12 +278,18 @@ __device__ __forceinline__ void mma_f8_ss(uint32_t d_tmem, uint64_t a_desc, uint
       : "memory");
 }
 
-template <int BT, int ST, int KB, bool ARGMAX>
+// Epilogue kinds: plain fp16 store, the fused lm_head's greedy argmax, and
+// SwiGLU over a 16-row interleaved gate/up weight (silu(gate) * up stored).
+constexpr int DC_EPI_STORE = 0, DC_EPI_ARGMAX = 1, DC_EPI_SWIGLU = 2;
+
+template <int BT, int ST, int KB, int EPI>
 __global__ void __launch_bounds__(DC_THREADS, 1)
     w8a16_dec_kernel(const __grid_constant__ CUtensorMap tm_w,
                      const __grid_constant__ CUtensorMap tm_x,
                      const __grid_constant__ CUtensorMap tm_y, const DcArgs args) {
   using L = DcLayout<BT, ST, KB>;
+  constexpr bool ARGMAX = EPI == DC_EPI_ARGMAX;
+  constexpr bool SWIGLU = EPI == DC_EPI_SWIGLU;
   constexpr int CH = L::CH;
   constexpr uint32_t ACC_COLS = L::ACC_COLS;
   constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
@@ -547,6 +554,41 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
               uint32_t& bj = best[cl * CH + jj];
               bj = cand > bj ? cand : bj;
             }
+          } else if constexpr (SWIGLU) {
+            // rows 32 b + i (i < 16) hold gate row 16 b + i and rows 32 b + 16 + i
+            // the matching up row, so lane L < 16 takes its up value from lane
+            // L + 16.  gate and up are rounded to fp16 as the two-GEMM path
+            // rounds them, then silu(g) * u in fp32 (SwiGLU_d.cu:22-24).
+            float o[CH];
+#pragma unroll
+            for (int jj = 0; jj < CH; ++jj) {
+              const float v = __half2float(__float2half_rn(fmaf(acc[jj] * sc, xsr[jj], bb)));
+              const float u = __shfl_down_sync(0xffffffffu, v, 16);
+              o[jj] = __fdividef(v, 1.0f + __expf(-v)) * u;
+            }
+            const int oc0 = (n0 >> 1) + q * 16;  // this warp's 16 output columns
+            if (args.y_tma) {
+              __half* stg = reinterpret_cast<__half*>(smem + L::OFF_O +
+                                                      (2 * (warp - 4) + ostage) * L::OW_BYTES);
+              if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+              __syncwarp();
+              if (lane < 16) {
+#pragma unroll
+                for (int jj = 0; jj < CH; ++jj) stg[jj * 16 + lane] = __float2half_rn(o[jj]);
+              }
+              ptx::fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0 && oc0 < args.out_n) {
+                ptx::tma_store_2d(&tm_y, ptx::smem_u32(stg), oc0, c0);
+                ptx::bulk_commit_group();
+              }
+              ostage ^= 1;
+            } else if (lane < 16 && oc0 + lane < args.out_n) {
+#pragma unroll
+              for (int jj = 0; jj < CH; ++jj)
+                if (c0 + jj < mvalid)
+                  args.y[(size_t)(c0 + jj) * args.out_n + oc0 + lane] = __float2half_rn(o[jj]);
+            }
           } else if (args.y_tma) {
             // each warp stages its 32 rows x CH tokens and stores them with its
             // own TMA store: no barrier across the epilogue warps
@@ -731,11 +773,11 @@ int dc_tmap_planes(CUtensorMap* m, const void* base, uint64_t K, uint64_t M, uin
   return r == CUDA_SUCCESS ? DDQ_OK : DDQ_ERR_ALIGNMENT;
 }
 
-template <int BT, int ST, int KB, bool ARGMAX>
+template <int BT, int ST, int KB, int EPI>
 int launch_dec_t(const DecPlan& p, const uint8_t* wq, const uint8_t* planes, DcArgs a,
                  cudaStream_t s) {
   using Lay = DcLayout<BT, ST, KB>;
-  auto kern = w8a16_dec_kernel<BT, ST, KB, ARGMAX>;
+  auto kern = w8a16_dec_kernel<BT, ST, KB, EPI>;
   const int dev = current_device();
   if (dev < 0 || dev >= 64) return DDQ_ERR_DEVICE;
   static bool attr_set[64] = {};
@@ -753,9 +795,10 @@ int launch_dec_t(const DecPlan& p, const uint8_t* wq, const uint8_t* planes, DcA
   if (st) return st;
   a.y_tma = 0;
   std::memset(&tm_y, 0, sizeof(tm_y));
-  if (!ARGMAX && p.splits == 1 && a.N % 8 == 0 && aligned16(a.y)) {
-    st = dc_tmap(&tm_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.y, (uint64_t)a.N, (uint64_t)a.M,
-                 (uint64_t)a.N * 2, 32, Lay::CH, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (EPI != DC_EPI_ARGMAX && p.splits == 1 && a.out_n % 8 == 0 && aligned16(a.y)) {
+    st = dc_tmap(&tm_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.y, (uint64_t)a.out_n, (uint64_t)a.M,
+                 (uint64_t)a.out_n * 2, EPI == DC_EPI_SWIGLU ? 16 : 32, Lay::CH,
+                 CU_TENSOR_MAP_SWIZZLE_NONE);
     if (st) return st;
     a.y_tma = 1;
   }
@@ -791,14 +834,14 @@ int launch_dec_t(const DecPlan& p, const uint8_t* wq, const uint8_t* planes, DcA
 
 }  // namespace
 
-DecPlan dec_plan(int64_t M, int64_t N, int64_t K, int sms) {
+DecPlan dec_plan(int64_t M, int64_t N, int64_t K, int sms, bool no_split) {
   DecPlan p{};
   p.sms = sms;
   p.bt = M <= 16 ? 16 : M <= 32 ? 32 : 64;
   const int64_t KS = (K + dc_stage_k(p.bt) - 1) / dc_stage_k(p.bt);
   const int64_t tiles = (N + DC_BN - 1) / DC_BN;
   int64_t splits = 1, kps = KS;
-  if (sms > 0 && tiles * 2 <= sms) {
+  if (sms > 0 && tiles * 2 <= sms && !no_split) {
     splits = sms / tiles;
     if (splits > kMaxSplits) splits = kMaxSplits;
     if (splits > KS) splits = KS;
@@ -816,11 +859,12 @@ DecPlan dec_plan(int64_t M, int64_t N, int64_t K, int sms) {
 int launch_dec(const __half* x, const uint8_t* wq, const float* scales, const void* bias,
                int bias_dtype, __half* y, unsigned long long* packed, int64_t vocab_offset, int M,
                int N, int K, void* ws, size_t ws_bytes, unsigned long long timeout_ns,
-               int debug_flags, cudaStream_t s) {
+               int debug_flags, cudaStream_t s, bool swiglu) {
   const int sms = device_sm_count(current_device());
   if (sms <= 0) return DDQ_ERR_DEVICE;
   if (M < 1 || M > 64) return DDQ_ERR_SHAPE;
-  const DecPlan p = dec_plan(M, N, K, sms);
+  if (swiglu && (packed || N % 32 != 0)) return DDQ_ERR_SHAPE;
+  const DecPlan p = dec_plan(M, N, K, sms, swiglu);
   if (!ws || ws_bytes < p.ws_bytes) return DDQ_ERR_WORKSPACE;
   if (reinterpret_cast<uintptr_t>(ws) & 255u) return DDQ_ERR_ALIGNMENT;
   uint8_t* planes = reinterpret_cast<uint8_t*>(ws);
@@ -864,11 +908,15 @@ int launch_dec(const __half* x, const uint8_t* wq, const float* scales, const vo
   a.kps = p.kps;
   a.timeout_ns = timeout_ns;
   a.debug_flags = debug_flags;
-  const bool am = packed != nullptr;
-#define DDQ_DC_CASE(BT_, ST_)                                                          \
-  case BT_:                                                                            \
-    return am ? launch_dec_t<BT_, ST_, dc_stage_k(BT_), true>(p, wq, planes, a, s)     \
-              : launch_dec_t<BT_, ST_, dc_stage_k(BT_), false>(p, wq, planes, a, s);
+  a.out_n = swiglu ? N / 2 : N;
+  const int epi = packed ? DC_EPI_ARGMAX : swiglu ? DC_EPI_SWIGLU : DC_EPI_STORE;
+#define DDQ_DC_CASE(BT_, ST_)                                                                  \
+  case BT_:                                                                                    \
+    return epi == DC_EPI_ARGMAX                                                                \
+               ? launch_dec_t<BT_, ST_, dc_stage_k(BT_), DC_EPI_ARGMAX>(p, wq, planes, a, s)   \
+           : epi == DC_EPI_SWIGLU                                                              \
+               ? launch_dec_t<BT_, ST_, dc_stage_k(BT_), DC_EPI_SWIGLU>(p, wq, planes, a, s)   \
+               : launch_dec_t<BT_, ST_, dc_stage_k(BT_), DC_EPI_STORE>(p, wq, planes, a, s);
   switch (p.bt) {
     DDQ_DC_CASE(16, 4)
     DDQ_DC_CASE(32, 3)

@@ -15,8 +15,8 @@
 // w8a16_pf_kernel: persistent, one CTA per SM, 384 threads; output tile =
 // 128 tokens (the MMA M, TMEM lanes) x 256 weight rows (the MMA N, TMEM
 // columns), K in stages of 64 (one 128-byte swizzle atom of fp16):
-//   warp 0      TMA producer: the x tile (128 x 64) and the w16 tile (256 x 64)
-//               of each stage on one full barrier (48 KB per stage)
+//   warp 0      TMA producer: the x tile (128 x 64) and the w16 tile (BN x 64,
+//               BN <= 256 chosen per shape) of each stage on one full barrier
 //   warp 1      MMA issuer: 4 x tcgen05.mma kind::f16 (K = 16) per stage into
 //               one of two 256-column TMEM accumulators (double buffered, so a
 //               tile's epilogue overlaps the next tile's MMAs)
@@ -66,6 +66,7 @@ struct PfArgs {
   const void* bias;
   int bias_dtype;
   int M, N, K;
+  int bn;               // weight rows per tile: a multiple of 32, at most PF_BN
   int tiles_m, tiles_n;
   unsigned long long timeout_ns;
   int debug_flags;
@@ -97,28 +98,42 @@ __device__ __forceinline__ void pf_reg_fence(uint32_t (&r)[32]) {
                  "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])::"memory");
 }
 
-// Exact expansion e4m3 -> fp16, 16 bytes in, 32 bytes out per thread step.
+// Exact expansion e4m3 -> fp16: each thread keeps four 16-byte loads in
+// flight (64 bytes in, 128 out per step) so that the pass runs at HBM rate.
+__device__ __forceinline__ void pf_expand16(const uint4& v, uint4* dst) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t h[8];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    h[2 * j] = e4m3x2_to_half2_bits((uint16_t)(w[j] & 0xFFFFu));
+    h[2 * j + 1] = e4m3x2_to_half2_bits((uint16_t)(w[j] >> 16));
+  }
+  dst[0] = make_uint4(h[0], h[1], h[2], h[3]);
+  dst[1] = make_uint4(h[4], h[5], h[6], h[7]);
+}
+
 __global__ void __launch_bounds__(256) e4m3_to_f16_kernel(const uint8_t* __restrict__ wq,
                                                           __half* __restrict__ w16, size_t n16) {
   ptx::pdl_launch_dependents();
   ptx::pdl_wait();  // w16 may still be read by the previous GEMM
   const uint4* src = reinterpret_cast<const uint4*>(wq);
   uint4* dst = reinterpret_cast<uint4*>(w16);
-  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16;
-       i += (size_t)gridDim.x * blockDim.x) {
-    const uint4 v = __ldcs(src + i);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-    uint32_t h[8];
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; i + 3 * stride < n16; i += 4 * stride) {
+    uint4 v[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      h[2 * j] = e4m3x2_to_half2_bits((uint16_t)(w[j] & 0xFFFFu));
-      h[2 * j + 1] = e4m3x2_to_half2_bits((uint16_t)(w[j] >> 16));
-    }
-    dst[2 * i] = make_uint4(h[0], h[1], h[2], h[3]);
-    dst[2 * i + 1] = make_uint4(h[4], h[5], h[6], h[7]);
+    for (int u = 0; u < 4; ++u) v[u] = __ldcs(src + i + u * stride);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) pf_expand16(v[u], dst + 2 * (i + u * stride));
   }
+  for (; i < n16; i += stride) pf_expand16(__ldcs(src + i), dst + 2 * i);
 }
 
+// SWIGLU: the weight is a 16-row interleave of gate and up (rows 32 b + i =
+// gate row 16 b + i, rows 32 b + 16 + i = up row 16 b + i) and the kernel
+// stores silu(gate) * up, N / 2 columns.
+template <bool SWIGLU>
 __global__ void __launch_bounds__(PF_THREADS, 1)
     w8a16_pf_kernel(const __grid_constant__ CUtensorMap tm_x,
                     const __grid_constant__ CUtensorMap tm_w,
@@ -179,7 +194,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
       int g = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        const int m0 = (u / args.tiles_n) * PF_BM, n0 = (u % args.tiles_n) * PF_BN;
+        const int m0 = (u / args.tiles_n) * PF_BM, n0 = (u % args.tiles_n) * args.bn;
         for (int ks = 0; ks < KS; ++ks, ++g) {
           const int s = g % PF_ST;
           if (!ptx::mbar_wait(bar_empty + 8 * s, ((uint32_t)(g / PF_ST) & 1u) ^ 1u, tmo,
@@ -189,7 +204,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
           }
           const uint32_t full = bar_full + 8 * s;
           const uint32_t dst = sbase + s * L::S_BYTES;
-          ptx::mbar_arrive_expect_tx(full, (uint32_t)L::S_BYTES);
+          ptx::mbar_arrive_expect_tx(full, (uint32_t)(L::A_BYTES + args.bn * PF_BK * 2));
           ptx::tma_load_2d(dst, &tm_x, ks * PF_BK, m0, full);
           ptx::tma_load_2d(dst + L::A_BYTES, &tm_w, ks * PF_BK, n0, full);
         }
@@ -203,7 +218,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = ptx::idesc_f16_f32(PF_BM, PF_BN);
+      const uint32_t idesc = ptx::idesc_f16_f32(PF_BM, args.bn);
       const uint64_t desc0 = ptx::smem_desc_sw128(sbase);
       ptx::pdl_wait();
       bool ok = true;
@@ -244,7 +259,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     ptx::pdl_wait();
     int it = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++it) {
-      const int m0 = (u / args.tiles_n) * PF_BM, n0 = (u % args.tiles_n) * PF_BN;
+      const int m0 = (u / args.tiles_n) * PF_BM, n0 = (u % args.tiles_n) * args.bn;
       const int b = it & 1;
       // the tile's weight scales and biases, once, into shared memory (two
       // buffers by tile parity: the barrier below keeps every warp within one
@@ -252,8 +267,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
       float* sb = reinterpret_cast<float*>(smem + L::OFF_SB) + b * 2 * PF_BN;
       {
         const int n = n0 + e;
-        sb[e] = n < args.N ? __ldg(args.scales + n) : 0.f;
-        sb[PF_BN + e] = n < args.N ? pf_load_bias(args.bias, args.bias_dtype, n) : 0.f;
+        const bool in = e < args.bn && n < args.N;
+        sb[e] = in ? __ldg(args.scales + n) : 0.f;
+        sb[PF_BN + e] = in ? pf_load_bias(args.bias, args.bias_dtype, n) : 0.f;
       }
       asm volatile("bar.sync 1, 256;" ::: "memory");
       if (!ptx::mbar_wait(bar_accfull + 8 * b, (uint32_t)(it >> 1) & 1u, tmo, abort_flag)) break;
@@ -261,7 +277,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
       ptx::tc_fence_after();
       const uint32_t taddr = tmem_base + (uint32_t)(b * ACC_COLS) + ((uint32_t)(q * 32) << 16);
 #pragma unroll 1
-      for (int c = grp; c < PF_BN / PF_CH; c += 2) {
+      for (int c = grp; c < args.bn / PF_CH; c += 2) {
         const int col0 = c * PF_CH;
         if (n0 + col0 >= args.N) break;
         uint32_t r[32];
@@ -277,29 +293,59 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         }
         ptx::tmem_ld_wait();
         pf_reg_fence(r);
-        uint32_t h[PF_CH / 2];
-#pragma unroll
-        for (int j = 0; j < PF_CH / 2; ++j) {
-          const float v0 = fmaf(__uint_as_float(r[2 * j]), sc[2 * j], bb[2 * j]);
-          const float v1 = fmaf(__uint_as_float(r[2 * j + 1]), sc[2 * j + 1], bb[2 * j + 1]);
-          const __half2 hv = __floats2half2_rn(v0, v1);
-          h[j] = *reinterpret_cast<const uint32_t*>(&hv);
-        }
-        // staging: 32 rows (tokens) x 64 B, 64-byte swizzle (16-byte chunk
-        // j of row r at chunk j ^ ((r >> 1) & 3)), matching the store map
-        if (lane == 0) ptx::bulk_wait_group_read0();
+        if (lane == 0) ptx::bulk_wait_group_read0();  // the staging buffer is free again
         __syncwarp();
+        if constexpr (SWIGLU) {
+          // a 32-column chunk is one interleave block: columns 0-15 are gate
+          // rows 16 b .. 16 b + 15, columns 16-31 the matching up rows.  gate
+          // and up are rounded to fp16 as the two-GEMM path rounds them, then
+          // silu(g) * u in fp32 (SwiGLU_d.cu:22-24); 16 outputs per token row.
+          uint32_t hz[8];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint32_t a = stg + (uint32_t)(lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4));
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(h[4 * j]),
-                       "r"(h[4 * j + 1]), "r"(h[4 * j + 2]), "r"(h[4 * j + 3])
-                       : "memory");
+          for (int j = 0; j < 8; ++j) {
+            float o[2];
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+              const int c = 2 * j + t;
+              const float g = __half2float(__float2half_rn(fmaf(__uint_as_float(r[c]), sc[c], bb[c])));
+              const float u = __half2float(
+                  __float2half_rn(fmaf(__uint_as_float(r[16 + c]), sc[16 + c], bb[16 + c])));
+              o[t] = __fdividef(g, 1.0f + __expf(-g)) * u;
+            }
+            const __half2 hv = __floats2half2_rn(o[0], o[1]);
+            hz[j] = *reinterpret_cast<const uint32_t*>(&hv);
+          }
+          // staging: 32 rows (tokens) x 32 B, unswizzled
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const uint32_t a = stg + (uint32_t)(lane * 32 + j * 16);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(hz[4 * j]),
+                         "r"(hz[4 * j + 1]), "r"(hz[4 * j + 2]), "r"(hz[4 * j + 3])
+                         : "memory");
+          }
+        } else {
+          uint32_t h[PF_CH / 2];
+#pragma unroll
+          for (int j = 0; j < PF_CH / 2; ++j) {
+            const float v0 = fmaf(__uint_as_float(r[2 * j]), sc[2 * j], bb[2 * j]);
+            const float v1 = fmaf(__uint_as_float(r[2 * j + 1]), sc[2 * j + 1], bb[2 * j + 1]);
+            const __half2 hv = __floats2half2_rn(v0, v1);
+            h[j] = *reinterpret_cast<const uint32_t*>(&hv);
+          }
+          // staging: 32 rows (tokens) x 64 B, 64-byte swizzle (16-byte chunk
+          // j of row r at chunk j ^ ((r >> 1) & 3)), matching the store map
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t a = stg + (uint32_t)(lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4));
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(h[4 * j]),
+                         "r"(h[4 * j + 1]), "r"(h[4 * j + 2]), "r"(h[4 * j + 3])
+                         : "memory");
+          }
         }
         ptx::fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0 && m0 + q * 32 < args.M) {
-          ptx::tma_store_2d(&tm_y, stg, n0 + col0, m0 + q * 32);
+          ptx::tma_store_2d(&tm_y, stg, SWIGLU ? (n0 + col0) >> 1 : n0 + col0, m0 + q * 32);
           ptx::bulk_commit_group();
         }
       }
@@ -363,13 +409,32 @@ cudaLaunchAttribute pdl_attr() {
   return at;
 }
 
+// Tile width over the weight rows: the MMA time of a tile grows with its
+// width, and the CTAs run ceil(tiles / SMs) tiles each; pick the width that
+// minimises waves x (width + a fixed per-tile cost of ~48 columns).
+int pf_pick_bn(int M, int N, int sms) {
+  const int tm = (M + PF_BM - 1) / PF_BM;
+  int best = PF_BN;
+  long best_cost = -1;
+  for (int bn = PF_BN; bn >= 128; bn -= 32) {
+    const long tiles = (long)tm * ((N + bn - 1) / bn);
+    const long waves = (tiles + sms - 1) / sms;
+    const long cost = waves * (bn + 48);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
+}
+
 }  // namespace
 
 size_t pf_workspace_bytes(int64_t N, int64_t K) { return (size_t)N * (size_t)K * 2; }
 
 int launch_pf(const __half* x, const uint8_t* wq, const float* scales, const void* bias,
               int bias_dtype, __half* y, int M, int N, int K, void* ws, size_t ws_bytes,
-              unsigned long long timeout_ns, int debug_flags, cudaStream_t s) {
+              unsigned long long timeout_ns, int debug_flags, cudaStream_t s, bool swiglu) {
   const int dev = current_device();
   const int sms = device_sm_count(dev);
   if (sms <= 0 || dev < 0 || dev >= 64) return DDQ_ERR_DEVICE;
@@ -378,13 +443,14 @@ int launch_pf(const __half* x, const uint8_t* wq, const float* scales, const voi
   if ((reinterpret_cast<uintptr_t>(ws) & 255u) || !aligned16(x) || !aligned16(y) ||
       (N % 8) != 0)
     return DDQ_ERR_ALIGNMENT;
+  if (swiglu && N % 32 != 0) return DDQ_ERR_SHAPE;
   __half* w16 = reinterpret_cast<__half*>(ws);
   // 1) exact e4m3 -> fp16 expansion of the weights
   {
     const size_t n16 = (size_t)N * (size_t)K / 16;
     cudaLaunchConfig_t cfg = {};
     const size_t want = (n16 + 255) / 256;
-    const size_t cap = (size_t)sms * 8;
+    const size_t cap = (size_t)sms * 4;
     cfg.gridDim = dim3((unsigned)(want < cap ? want : cap));
     cfg.blockDim = dim3(256);
     cfg.stream = s;
@@ -397,19 +463,24 @@ int launch_pf(const __half* x, const uint8_t* wq, const float* scales, const voi
     }
   }
   // 2) the fp16 GEMM
-  static bool attr_set[64] = {};
-  if (!attr_set[dev]) {
-    if (cudaFuncSetAttribute(w8a16_pf_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             PfLayout::ALLOC) != cudaSuccess)
+  auto kern = swiglu ? w8a16_pf_kernel<true> : w8a16_pf_kernel<false>;
+  static bool attr_set[2][64] = {};
+  if (!attr_set[swiglu][dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PfLayout::ALLOC) !=
+        cudaSuccess)
       return DDQ_ERR_LAUNCH;
-    attr_set[dev] = true;
+    attr_set[swiglu][dev] = true;
   }
   CUtensorMap tm_x, tm_w, tm_y;
   int st = pf_tmap(&tm_x, x, (uint64_t)K, (uint64_t)M, PF_BK, PF_BM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st) return st;
-  st = pf_tmap(&tm_w, w16, (uint64_t)K, (uint64_t)N, PF_BK, PF_BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  const int bn = pf_pick_bn(M, N, sms);
+  st = pf_tmap(&tm_w, w16, (uint64_t)K, (uint64_t)N, PF_BK, (uint32_t)bn, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st) return st;
-  st = pf_tmap(&tm_y, y, (uint64_t)N, (uint64_t)M, PF_CH, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+  if (swiglu)
+    st = pf_tmap(&tm_y, y, (uint64_t)(N / 2), (uint64_t)M, PF_CH / 2, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
+  else
+    st = pf_tmap(&tm_y, y, (uint64_t)N, (uint64_t)M, PF_CH, 32, CU_TENSOR_MAP_SWIZZLE_64B);
   if (st) return st;
   PfArgs a{};
   a.scales = scales;
@@ -418,8 +489,9 @@ int launch_pf(const __half* x, const uint8_t* wq, const float* scales, const voi
   a.M = M;
   a.N = N;
   a.K = K;
+  a.bn = bn;
   a.tiles_m = (M + PF_BM - 1) / PF_BM;
-  a.tiles_n = (N + PF_BN - 1) / PF_BN;
+  a.tiles_n = (N + bn - 1) / bn;
   a.timeout_ns = timeout_ns;
   a.debug_flags = debug_flags;
   const int units = a.tiles_m * a.tiles_n;
@@ -431,7 +503,7 @@ int launch_pf(const __half* x, const uint8_t* wq, const float* scales, const voi
   cudaLaunchAttribute at = pdl_attr();
   cfg.attrs = &at;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, w8a16_pf_kernel, tm_x, tm_w, tm_y, a) != cudaSuccess) {
+  if (cudaLaunchKernelEx(&cfg, kern, tm_x, tm_w, tm_y, a) != cudaSuccess) {
     cudaGetLastError();
     return DDQ_ERR_LAUNCH;
   }

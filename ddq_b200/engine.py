@@ -8,9 +8,10 @@ attention -> O -> +residual -> RMSNorm -> gate/up -> SwiGLU -> down ->
 
 * every projection is an e4m3 W8A16 GEMM from this library (the reference's
   ``_linear`` dispatch point, ``engine.py:85-86``, now calls
-  ``gemm_fp8.f8_forward``); q/k/v and gate/up are each stacked into one GEMM
-  when the weights are quantized, which the reference does per module
-  (``engine.py:190-191, 215-217``);
+  ``gemm_fp8.f8_forward``); q/k/v are stacked into one GEMM, and gate/up
+  into one GEMM whose epilogue applies SwiGLU (``gemm_fp8.f8_forward_swiglu``:
+  the [M, 2I] gate/up output is never written), where the reference runs
+  gate, up and ``swiglu_naive`` separately (``engine.py:189-193, 215-217``);
 * the lm_head runs only on the last position of each sequence and never
   writes logits: the fused kernel returns the greedy token directly
   (replacing ``engine.py:338`` + ``sampler_d`` at ``engine.py:345/351``);
@@ -80,11 +81,19 @@ class FP8Linear:
     def __init__(self, wq: torch.Tensor, scales: torch.Tensor, bias: Optional[torch.Tensor]):
         self.wq, self.scales, self.bias = wq, scales, bias
         self._wdeq = None
+        self._il = None
 
     @classmethod
     def quantize(cls, w: torch.Tensor, bias: Optional[torch.Tensor] = None) -> "FP8Linear":
         wq, s = gemm_fp8.quantize(w.contiguous())
         return cls(wq, s, None if bias is None else bias.float().contiguous())
+
+    def gate_up_interleaved(self):
+        """(wq, scales, bias) of a stacked [gate; up] projection in the fused SwiGLU
+        kernel's row order (``gemm_fp8.interleave_gate_up``), built once."""
+        if self._il is None:
+            self._il = gemm_fp8.interleave_gate_up(self.wq, self.scales, self.bias)
+        return self._il
 
     def dequantized(self) -> torch.Tensor:
         """fp32 [N,K] = e4m3 value * scale (the reference semantics' weight)."""
@@ -256,8 +265,11 @@ class Engine:
         o = o.transpose(1, 2).reshape(B, S, nh * hd)
         x = x + self.linear(o, L["o"])
         h = self.rmsnorm(x, L["post_norm"])
-        gu = self.linear(h, L["gate_up"])
-        x = x + self.linear(self.swiglu(gu, cfg.intermediate_size), L["down"])
+        if self.linear_kind == "fp8":   # gate/up GEMM with the SwiGLU epilogue
+            z = gemm_fp8.f8_forward_swiglu(h, *L["gate_up"].gate_up_interleaved())
+        else:
+            z = self.swiglu(self.linear(h, L["gate_up"]), cfg.intermediate_size)
+        x = x + self.linear(z, L["down"])
         return x
 
     def hidden(self, ids: torch.Tensor, cache: KVCache, b0: int = 0, start: int = 0,

@@ -105,6 +105,62 @@ def f8_forward(x: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor,
     return y2.reshape(*x.shape[:-1], N)
 
 
+SWIGLU_BLOCK = 16  # gate/up interleave granularity of the fused SwiGLU GEMM (rows)
+
+
+def interleave_gate_up(wq_gu: torch.Tensor, scales_gu: torch.Tensor,
+                       bias_gu: Optional[torch.Tensor] = None):
+    """Reorder a stacked [gate; up] projection ([2I, K] rows: gate 0..I-1, then up)
+    into the layout of ``f8_forward_swiglu``: blocks of 16 gate rows followed by
+    the same 16 up rows.  Returns (wq, scales, bias) with the same row count."""
+    _check(wq_gu.dim() == 2 and wq_gu.size(0) % (2 * SWIGLU_BLOCK) == 0,
+           "gemm_fp8: gate/up rows must be 2 * I with I a multiple of 16")
+    two_i, K = wq_gu.shape
+    nb = two_i // (2 * SWIGLU_BLOCK)
+
+    def il(t, tail):
+        return t.reshape(2, nb, SWIGLU_BLOCK, *tail).transpose(0, 1).reshape(two_i, *tail).contiguous()
+    b = None if bias_gu is None or bias_gu.numel() == 0 else il(bias_gu, ())
+    return il(wq_gu, (K,)), il(scales_gu, ()), b
+
+
+def f8_forward_swiglu(x: torch.Tensor, wq_il: torch.Tensor, scales_il: torch.Tensor,
+                      bias_il: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Gate/up GEMM with the SwiGLU epilogue: z[..., I] = silu(gate) * up, where
+    gate/up are the fp16 outputs the two projections would give.  The weight
+    comes from ``interleave_gate_up``.  No [M, 2I] intermediate is written."""
+    _check(x.is_cuda and wq_il.is_cuda, "gemm_fp8: CUDA tensors required")
+    _check(x.dtype == torch.float16, "gemm_fp8: fp16 x required")
+    _check(wq_il.dtype == torch.uint8 and wq_il.dim() == 2, "gemm_fp8: wq must be uint8 [2I,K]")
+    _check(scales_il.is_cuda and scales_il.dtype == torch.float32 and
+           scales_il.numel() == wq_il.size(0), "gemm_fp8: scales must be fp32 CUDA [2I]")
+    two_i, K = wq_il.shape
+    _check(two_i % (2 * SWIGLU_BLOCK) == 0, "gemm_fp8: gate/up rows must be 2 * I, I % 16 == 0")
+    _check(x.dim() >= 1 and x.size(-1) == K, "gemm_fp8: inner dim mismatch")
+    inter = two_i // 2
+    x2 = x.contiguous().reshape(-1, K)
+    M = x2.size(0)
+    z = torch.empty((M, inter), dtype=torch.float16, device=x.device)
+    bptr, bcode = None, _lib.DTYPE_NONE
+    if bias_il is not None and bias_il.numel() > 0:
+        _check(bias_il.numel() == two_i and bias_il.is_cuda and
+               bias_il.dtype in (torch.float16, torch.float32), "gemm_fp8: bias mismatch")
+        bias_il = bias_il.contiguous()
+        bptr = bias_il.data_ptr()
+        bcode = _lib.DTYPE_F16 if bias_il.dtype == torch.float16 else _lib.DTYPE_F32
+    wqc, sc = wq_il.contiguous(), scales_il.contiguous()
+    L = _lib.load()
+    with torch.cuda.device(x.device):
+        nws = L.ddq_w8a16_gemm_swiglu_workspace_size(M, inter, K)
+        ws = workspace(x.device, nws) if nws else None
+        st = L.ddq_w8a16_gemm_swiglu(x2.data_ptr(), wqc.data_ptr(), sc.data_ptr(), bptr, bcode,
+                                     z.data_ptr(), M, inter, K,
+                                     ws.data_ptr() if ws is not None else None,
+                                     ws.numel() if ws is not None else 0, _stream_ptr(x.device))
+    _lib.check(st, "gemm_fp8.f8_forward_swiglu")
+    return z.reshape(*x.shape[:-1], inter)
+
+
 def forward(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Drop-in for gemm_d.forward: quantize w (every call, as the reference does), then GEMM."""
     wq, scales = quantize(w)

@@ -71,12 +71,12 @@ int ddq_quantize_e4m3(const void* w, int w_dtype, int64_t N, int64_t K,
 
 /*
  * Bytes of device workspace ddq_w8a16_gemm needs for this shape (0 if none).
- * The first 4 KiB of a workspace hold per-tile arrival tickets, the rest
- * split-K partial sums.  Zero-fill a workspace once when allocating it;
- * every call leaves its tickets at zero again, so one workspace (sized for
- * the largest shape) serves any sequence of shapes.  Calls sharing one
- * workspace must be ordered on one stream.  The pointer must be 256-byte
- * aligned.
+ * Decode shapes (M <= 64) keep the activations split into three e4m3 planes
+ * and the per-token scales there; prefill shapes (M >= 128 by default) keep
+ * the weight expanded to fp16 (N * K * 2 bytes).  The contents need no
+ * initialisation.  One workspace sized for the largest shape serves any
+ * sequence of shapes; calls sharing it must be ordered on one stream.  The
+ * pointer must be 256-byte aligned.
  */
 size_t ddq_w8a16_gemm_workspace_size(int64_t M, int64_t N, int64_t K);
 
@@ -115,6 +115,24 @@ int ddq_w8a16_gemm(const void* x, const uint8_t* wq, const float* scales,
 int ddq_w8a16_gemm_noalloc(const void* x, const uint8_t* wq, const float* scales,
                            const void* bias, int bias_dtype, void* y,
                            int64_t M, int64_t N, int64_t K, void* stream);
+
+/*
+ * Gate/up projection with the SwiGLU epilogue, no [M, 2I] intermediate:
+ *   g = fp16( x @ (e4m3(Wg) * sg)^T + bg ),  u = fp16( x @ (e4m3(Wu) * su)^T + bu )
+ *   z[m, j] = fp16( silu(g[m, j]) * u[m, j] )            (fp32 math)
+ * Replaces: engine.py:189-193 (gate_proj, up_proj, then swiglu_naive,
+ * SwiGLU_d.cu:12-26); no reference counterpart fuses them.
+ * wq_gu [2I, K] (and scales_gu, bias [2I]) interleave gate and up in blocks of
+ * 16 rows: rows 32 b + i = gate row 16 b + i, rows 32 b + 16 + i = up row
+ * 16 b + i (0 <= i < 16).  I % 16 == 0, K % 16 == 0, 16-byte aligned x, wq_gu
+ * and z [M, I].  Workspace: ddq_w8a16_gemm_swiglu_workspace_size bytes, used
+ * as for ddq_w8a16_gemm.
+ */
+size_t ddq_w8a16_gemm_swiglu_workspace_size(int64_t M, int64_t I, int64_t K);
+int ddq_w8a16_gemm_swiglu(const void* x, const uint8_t* wq_gu, const float* scales_gu,
+                          const void* bias, int bias_dtype, void* z,
+                          int64_t M, int64_t I, int64_t K,
+                          void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Greedy argmax over fp16 logits [B, V] -> int64 [B]; ties go to the

@@ -178,6 +178,35 @@ def forward(x, w, bias=None) -> np.ndarray:
     return f8_forward(x, wq, s, bias)
 
 
+def swiglu_f16(gate, up) -> np.ndarray:
+    """``SwiGLU_d.cu:12-26``: z = fp16( g / (1 + exp(-g)) * u ) with g, u the fp16
+    inputs taken to float (evaluated here in float64, then rounded)."""
+    g = np.asarray(gate, np.float16).astype(np.float64)
+    u = np.asarray(up, np.float16).astype(np.float64)
+    with np.errstate(over="ignore"):
+        z = g / (1.0 + np.exp(-g)) * u
+    return z.astype(np.float32).astype(np.float16)
+
+
+def f8_forward_swiglu(x, wq_gu, scales_gu, bias_gu=None) -> np.ndarray:
+    """The gate/up projections then SwiGLU (``engine.py:189-193``): wq_gu is the
+    stacked [gate; up] weight [2I, K] (gate rows first), as the engine's two
+    projections would be run; returns z [..., I]."""
+    wq_gu = np.asarray(wq_gu)
+    inter = wq_gu.shape[0] // 2
+    y = f8_forward(x, wq_gu, scales_gu, bias_gu)
+    return swiglu_f16(y[..., :inter], y[..., inter:])
+
+
+def interleave_gate_up(a, block=16) -> np.ndarray:
+    """Rows of a stacked [gate; up] array in the fused SwiGLU kernel's order:
+    blocks of `block` gate rows followed by the same `block` up rows."""
+    a = np.asarray(a)
+    nb = a.shape[0] // (2 * block)
+    tail = a.shape[1:]
+    return a.reshape((2, nb, block) + tail).swapaxes(0, 1).reshape(a.shape)
+
+
 def argmax_f16(logits) -> np.ndarray:
     """Greedy argmax over the last dim of fp16 logits, ties -> lowest index.
 
