@@ -1,0 +1,54 @@
+"""Decode-step attention with RoPE and the KV-cache write fused in.
+
+``decode_attention`` replaces, for one decode step, the reference engine's
+q/k rotary embedding (``RoPe_d.cu:12-68``), the cache write
+(``engine.py:126-130``) and the attention call (``engine.py:225-251``) with one
+kernel (``ddq_decode_attention``): the new key/value row is written into the
+cache at the device-side position and the query heads attend over positions
+0..pos of their key/value head (grouped-query attention).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+
+def decode_attention(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                     cos: torch.Tensor, sin: torch.Tensor, pos: torch.Tensor,
+                     num_heads: int, num_kv_heads: int, head_dim: int,
+                     scale: float) -> torch.Tensor:
+    """qkv fp16 [B, (Hq + 2 Hkv) * D] (one token per sequence); k_cache/v_cache
+    fp16 [B, Hkv, capacity, D] (batch dim may be strided); cos/sin fp32 [D] for
+    this position; pos int64 [1] on the device.  Returns o fp16 [B, Hq * D] and
+    updates the caches at ``pos``."""
+    def need(cond, msg):
+        if not cond:
+            raise RuntimeError(msg)
+    B = qkv.shape[0]
+    need(qkv.is_cuda and qkv.dtype == torch.float16 and qkv.dim() == 2 and
+         qkv.stride(1) == 1 and qkv.shape[1] == (num_heads + 2 * num_kv_heads) * head_dim,
+         "decode_attention: qkv must be fp16 CUDA [B, (Hq + 2 Hkv) * D] with unit inner stride")
+    for c in (k_cache, v_cache):
+        need(c.is_cuda and c.dtype == torch.float16 and c.dim() == 4 and
+             tuple(c.shape[:2]) == (B, num_kv_heads) and c.shape[3] == head_dim and
+             c.stride(3) == 1 and c.stride(2) == head_dim and
+             c.stride(1) == c.shape[2] * head_dim,
+             "decode_attention: caches must be fp16 CUDA [B, Hkv, capacity, D], dense per sequence")
+    need(k_cache.stride(0) == v_cache.stride(0) and k_cache.shape == v_cache.shape,
+         "decode_attention: k and v caches must have the same shape and strides")
+    cos = cos.reshape(-1).contiguous()
+    sin = sin.reshape(-1).contiguous()
+    need(cos.dtype == torch.float32 and sin.dtype == torch.float32 and
+         cos.numel() == head_dim and sin.numel() == head_dim, "decode_attention: fp32 cos/sin [D]")
+    need(pos.is_cuda and pos.dtype == torch.int64 and pos.numel() == 1,
+         "decode_attention: pos must be an int64 CUDA scalar")
+    out = torch.empty((B, num_heads * head_dim), dtype=torch.float16, device=qkv.device)
+    with torch.cuda.device(qkv.device):
+        st = _lib.load().ddq_decode_attention(
+            qkv.data_ptr(), qkv.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
+            k_cache.stride(0), k_cache.shape[2], cos.data_ptr(), sin.data_ptr(), pos.data_ptr(),
+            out.data_ptr(), out.stride(0), B, num_heads, num_kv_heads, head_dim, float(scale),
+            torch.cuda.current_stream(qkv.device).cuda_stream)
+    _lib.check(st, "decode_attention")
+    return out

@@ -51,6 +51,11 @@ int launch_pf(const __half* x, const uint8_t* wq, const float* scales, const voi
               int bias_dtype, __half* y, int M, int N, int K, void* ws, size_t ws_bytes,
               unsigned long long timeout_ns, int debug_flags, cudaStream_t s,
               bool swiglu = false);
+// Decode-step attention with RoPE and the KV-cache write fused (attention.cu).
+int launch_decode_attention(const __half* qkv, int64_t qkv_stride, __half* kc, __half* vc,
+                            int64_t cache_bstride, int cap, const float* cos, const float* sin,
+                            const int64_t* pos, __half* out, int64_t out_stride, int B, int Hq,
+                            int Hkv, int D, float scale, cudaStream_t s);
 int launch_unpack_argmax(const unsigned long long* packed, int64_t M, int64_t* ids, cudaStream_t s);
 
 }  // namespace ddq

@@ -12,6 +12,9 @@ attention -> O -> +residual -> RMSNorm -> gate/up -> SwiGLU -> down ->
   into one GEMM whose epilogue applies SwiGLU (``gemm_fp8.f8_forward_swiglu``:
   the [M, 2I] gate/up output is never written), where the reference runs
   gate, up and ``swiglu_naive`` separately (``engine.py:189-193, 215-217``);
+* a decode step's RoPE, KV-cache write and attention run as one kernel
+  (``attention.decode_attention``) instead of the reference's RoPE kernel,
+  cache copy and attention call (``engine.py:126-130, 225-251``);
 * the lm_head runs only on the last position of each sequence and never
   writes logits: the fused kernel returns the greedy token directly
   (replacing ``engine.py:338`` + ``sampler_d`` at ``engine.py:345/351``);
@@ -39,7 +42,7 @@ from typing import List, Optional
 import torch
 import torch.nn.functional as F
 
-from . import gemm_fp8, lm_head as lmh
+from . import attention, gemm_fp8, lm_head as lmh
 
 E4M3_DECODE_LUT = None
 
@@ -243,6 +246,13 @@ class Engine:
         hd, nh, nkv = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads
         h = self.rmsnorm(x, L["in_norm"])
         qkv = self.linear(h, L["qkv"])
+        scale = hd ** -0.5
+        if pos is not None and S == 1 and self.linear_kind == "fp8":
+            # one decode step: RoPE, the cache write and the attention in one kernel
+            o = attention.decode_attention(qkv.reshape(B, -1), cache.k[li, b0:b0 + B],
+                                           cache.v[li, b0:b0 + B], cos, sin, pos, nh, nkv, hd,
+                                           scale)
+            return self._mlp_block(x + self.linear(o.reshape(B, S, nh * hd), L["o"]), L)
         q = qkv[..., : nh * hd].reshape(B, S, nh, hd).transpose(1, 2)
         k = qkv[..., nh * hd: (nh + nkv) * hd].reshape(B, S, nkv, hd).transpose(1, 2)
         v = qkv[..., (nh + nkv) * hd:].reshape(B, S, nkv, hd).transpose(1, 2)
@@ -250,7 +260,6 @@ class Engine:
         k = self.apply_rope(k, cos, sin)
         kc = cache.k[li, b0:b0 + B]
         vc = cache.v[li, b0:b0 + B]
-        scale = hd ** -0.5
         if pos is None:  # prefill from position `start` (0): causal attention over the chunk
             kc[:, :, start:start + S] = k
             vc[:, :, start:start + S] = v
@@ -263,14 +272,16 @@ class Engine:
             o = F.scaled_dot_product_attention(q, kc, vc, attn_mask=mask, scale=scale,
                                                enable_gqa=True)
         o = o.transpose(1, 2).reshape(B, S, nh * hd)
-        x = x + self.linear(o, L["o"])
+        return self._mlp_block(x + self.linear(o, L["o"]), L)
+
+    def _mlp_block(self, x: torch.Tensor, L: dict) -> torch.Tensor:
+        """RMSNorm -> gate/up -> SwiGLU -> down -> +residual."""
         h = self.rmsnorm(x, L["post_norm"])
         if self.linear_kind == "fp8":   # gate/up GEMM with the SwiGLU epilogue
             z = gemm_fp8.f8_forward_swiglu(h, *L["gate_up"].gate_up_interleaved())
         else:
-            z = self.swiglu(self.linear(h, L["gate_up"]), cfg.intermediate_size)
-        x = x + self.linear(z, L["down"])
-        return x
+            z = self.swiglu(self.linear(h, L["gate_up"]), self.cfg.intermediate_size)
+        return x + self.linear(z, L["down"])
 
     def hidden(self, ids: torch.Tensor, cache: KVCache, b0: int = 0, start: int = 0,
                pos: Optional[torch.Tensor] = None) -> torch.Tensor:

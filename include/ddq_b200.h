@@ -135,6 +135,26 @@ int ddq_w8a16_gemm_swiglu(const void* x, const uint8_t* wq_gu, const float* scal
                           void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * One decode step of grouped-query attention with RoPE and the KV-cache write
+ * fused in.  Replaces, for a decode step: the q/k RoPE (RoPe_d.cu:12-68), the
+ * cache write (engine.py:126-130) and the attention (engine.py:225-251).
+ *   qkv   fp16 [B, (Hq + 2 Hkv) * D], row stride qkv_stride (elements): q heads,
+ *         then k heads, then v heads (the stacked QKV projection's output)
+ *   k_cache, v_cache  fp16 [B, Hkv, capacity, D], batch stride in elements
+ *   cos, sin  fp32 [D]: the rotary row of this step's position
+ *   pos   device int64 scalar, 0 <= pos < capacity (read on the device)
+ *   out   fp16 [B, Hq * D], row stride out_stride
+ * Writes cache[b, g, pos] = (rope(k_g), v_g), then
+ *   out[b, h] = softmax_j(rope(q_h) . K[b, h / (Hq/Hkv), j] * scale) V[...],
+ * j = 0..pos, in fp32.  Hq % Hkv == 0, Hq / Hkv <= 8, D = 64 or 128.
+ */
+int ddq_decode_attention(const void* qkv, int64_t qkv_stride, void* k_cache, void* v_cache,
+                         int64_t cache_batch_stride, int64_t capacity, const float* cos,
+                         const float* sin, const int64_t* pos, void* out, int64_t out_stride,
+                         int64_t B, int64_t Hq, int64_t Hkv, int64_t D, float scale,
+                         void* stream);
+
+/*
  * Greedy argmax over fp16 logits [B, V] -> int64 [B]; ties go to the
  * lowest index.  Replaces: sampler_d.cu:10-70 (argmax_kernel + forward).
  */

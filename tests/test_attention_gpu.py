@@ -1,0 +1,88 @@
+"""Decode-step attention with RoPE and the cache write fused (ddq_decode_attention),
+against a PyTorch fp32 reference of the unfused steps it replaces: rotate-half
+RoPE in fp32 rounded to fp16 (``RoPe_d.cu``), the cache write, and softmax
+attention over positions 0..pos in fp32 (``engine.py:225-251``)."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def reference(qkv, kc, vc, cos, sin, pos, nh, nkv, hd, scale):
+    B = qkv.shape[0]
+    q = qkv[:, : nh * hd].reshape(B, nh, hd).float()
+    k = qkv[:, nh * hd:(nh + nkv) * hd].reshape(B, nkv, hd).float()
+    v = qkv[:, (nh + nkv) * hd:].reshape(B, nkv, hd)
+
+    def rope(x):
+        half = hd // 2
+        rot = torch.cat([-x[..., half:], x[..., :half]], dim=-1)
+        return (x * cos + rot * sin).half()
+    q, k = rope(q), rope(k)
+    kc, vc = kc.clone(), vc.clone()
+    kc[:, :, pos] = k
+    vc[:, :, pos] = v
+    g = nh // nkv
+    kk = kc[:, :, : pos + 1].float().repeat_interleave(g, dim=1)
+    vv = vc[:, :, : pos + 1].float().repeat_interleave(g, dim=1)
+    s = torch.einsum("bhd,bhjd->bhj", q.float(), kk) * scale
+    o = torch.einsum("bhj,bhjd->bhd", torch.softmax(s, dim=-1), vv)
+    return o.reshape(B, nh * hd).half(), kc, vc
+
+
+@pytest.mark.parametrize("B,nh,nkv,hd,cap,pos", [
+    (1, 14, 2, 64, 64, 0), (3, 14, 2, 64, 100, 37), (64, 14, 2, 64, 768, 600),
+    (2, 8, 8, 64, 300, 299), (4, 16, 2, 128, 256, 130), (5, 4, 1, 64, 40, 31)])
+def test_decode_attention_matches_reference(cuda_device, B, nh, nkv, hd, cap, pos):
+    from ddq_b200 import attention
+    g = torch.Generator(device="cuda").manual_seed(B * 1000 + pos)
+    qkv = torch.randn(B, (nh + 2 * nkv) * hd, generator=g, device="cuda").half()
+    kc = torch.randn(B, nkv, cap, hd, generator=g, device="cuda").half()
+    vc = torch.randn(B, nkv, cap, hd, generator=g, device="cuda").half()
+    inv = 1.0 / (1e6 ** (torch.arange(0, hd, 2, dtype=torch.float32, device="cuda") / hd))
+    f = torch.tensor([float(pos)], device="cuda")[:, None] * inv[None, :]
+    emb = torch.cat([f, f], dim=-1)
+    cos, sin = emb.cos(), emb.sin()
+    scale = 1.0 / math.sqrt(hd)
+    o_ref, kc_ref, vc_ref = reference(qkv, kc, vc, cos, sin, pos, nh, nkv, hd, scale)
+    p = torch.tensor([pos], dtype=torch.int64, device="cuda")
+    o = attention.decode_attention(qkv, kc, vc, cos, sin, p, nh, nkv, hd, scale)
+    torch.cuda.synchronize()
+    assert torch.equal(kc, kc_ref) and torch.equal(vc, vc_ref)   # cache rows bit-exact
+    err = ((o.float() - o_ref.float()).abs().amax(dim=1) /
+           o_ref.float().abs().amax(dim=1).clamp_min(1e-6)).max().item()
+    assert err < 2e-3, err
+
+
+def test_decode_attention_strided_batch_and_graph(cuda_device):
+    """A batch slice of a larger [L, B, ...] cache, replayed in a CUDA graph with
+    the position advanced on the device between replays."""
+    from ddq_b200 import attention
+    nh, nkv, hd, cap = 14, 2, 64, 96
+    g = torch.Generator(device="cuda").manual_seed(5)
+    big_k = torch.zeros(3, 8, nkv, cap, hd, dtype=torch.float16, device="cuda")
+    big_v = torch.zeros_like(big_k)
+    kc, vc = big_k[1, 2:6], big_v[1, 2:6]
+    qkv = torch.randn(4, (nh + 2 * nkv) * hd, generator=g, device="cuda").half()
+    cos = torch.ones(hd, device="cuda")
+    sin = torch.zeros(hd, device="cuda")
+    pos = torch.zeros(1, dtype=torch.int64, device="cuda")
+    out = attention.decode_attention(qkv, kc, vc, cos, sin, pos, nh, nkv, hd, 0.125)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        o2 = attention.decode_attention(qkv, kc, vc, cos, sin, pos, nh, nkv, hd, 0.125)
+    for step in range(1, 5):
+        pos.fill_(step)
+        graph.replay()
+    torch.cuda.synchronize()
+    # every written row holds the same (unrotated: cos=1, sin=0) k/v, so the
+    # attention output equals v for every position count
+    v = qkv[:, (nh + nkv) * hd:].reshape(4, nkv, hd)
+    for step in range(5):
+        assert torch.equal(vc[:, :, step], v)
+    exp = v.repeat_interleave(nh // nkv, dim=1).reshape(4, nh * hd)
+    assert (o2.float() - exp.float()).abs().max().item() < 1e-2
+    assert big_k[0].abs().sum().item() == 0 and big_k[1, :2].abs().sum().item() == 0
