@@ -189,6 +189,18 @@ extern "C" int ddq_decode_attention(const void* qkv, int64_t qkv_stride, void* k
       reinterpret_cast<cudaStream_t>(stream));
 }
 
+extern "C" int ddq_add_rmsnorm(const void* x, const void* delta, const float* w, float eps,
+                               void* x_out, void* h, int64_t M, int64_t H, void* stream) {
+  if (M < 0 || H < 0) return DDQ_ERR_SHAPE;
+  if (M == 0) return DDQ_OK;
+  if (!x || !w || !h) return DDQ_ERR_INVALID_ARGUMENT;
+  if (M > 0x7fffffff || H > 0x7fffffff) return DDQ_ERR_SHAPE;
+  return launch_add_rmsnorm(reinterpret_cast<const __half*>(x),
+                            reinterpret_cast<const __half*>(delta), w, eps,
+                            reinterpret_cast<__half*>(x_out), reinterpret_cast<__half*>(h),
+                            (int)M, (int)H, reinterpret_cast<cudaStream_t>(stream));
+}
+
 extern "C" int ddq_argmax_f16(const void* logits, int64_t B, int64_t V, int64_t* out,
                               void* stream) {
   if (B < 0 || V < 0) return DDQ_ERR_SHAPE;

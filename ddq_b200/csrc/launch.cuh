@@ -56,6 +56,9 @@ int launch_decode_attention(const __half* qkv, int64_t qkv_stride, __half* kc, _
                             int64_t cache_bstride, int cap, const float* cos, const float* sin,
                             const int64_t* pos, __half* out, int64_t out_stride, int B, int Hq,
                             int Hkv, int D, float scale, cudaStream_t s);
+// Residual add + RMSNorm (norm.cu).
+int launch_add_rmsnorm(const __half* x, const __half* delta, const float* w, float eps,
+                       __half* x_out, __half* h, int M, int H, cudaStream_t s);
 int launch_unpack_argmax(const unsigned long long* packed, int64_t M, int64_t* ids, cudaStream_t s);
 
 }  // namespace ddq

@@ -1,0 +1,129 @@
+// norm.cu - RMSNorm with the residual add fused in front (replaces the
+// reference's qwen2_rmsnorm_kernel, RMSnorm_d.cu:23-87, and the residual
+// addition before it, engine.py:254-256).
+//
+//   s = fp16(x + delta)          (delta optional; the new residual stream)
+//   h = fp16( (s * rsqrt(mean(s^2) + eps)) * w )      fp32 math
+//
+// One warp per row; rows of up to 2048 elements stay in registers (a 16-byte
+// chunk of 8 values per lane and step), longer rows are read a second time.
+#include "common.cuh"
+#include "launch.cuh"
+#include "sm100_ptx.cuh"
+
+namespace ddq {
+
+__device__ __forceinline__ uint4 nm_add8(const uint4& a, const uint4& b) {
+  uint4 r;
+  const __half2* x = reinterpret_cast<const __half2*>(&a);
+  const __half2* y = reinterpret_cast<const __half2*>(&b);
+  __half2* o = reinterpret_cast<__half2*>(&r);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) o[i] = __hadd2(x[i], y[i]);
+  return r;
+}
+
+__device__ __forceinline__ float nm_sumsq8(const uint4& a) {
+  const __half2* x = reinterpret_cast<const __half2*>(&a);
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(x[i]);
+    s = fmaf(f.x, f.x, fmaf(f.y, f.y, s));
+  }
+  return s;
+}
+
+__device__ __forceinline__ uint4 nm_scale8(const uint4& a, float r, const float* w) {
+  uint4 out;
+  const __half2* x = reinterpret_cast<const __half2*>(&a);
+  __half2* o = reinterpret_cast<__half2*>(&out);
+  const float4 w0 = reinterpret_cast<const float4*>(w)[0];
+  const float4 w1 = reinterpret_cast<const float4*>(w)[1];
+  const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(x[i]);
+    o[i] = __floats2half2_rn(__fmul_rn(__fmul_rn(f.x, r), wv[2 * i]),
+                             __fmul_rn(__fmul_rn(f.y, r), wv[2 * i + 1]));
+  }
+  return out;
+}
+
+constexpr int NM_REG_CHUNKS = 8;  // 16-byte chunks per lane kept in registers
+
+__global__ void __launch_bounds__(256) add_rmsnorm_kernel(const __half* x,
+                                                          const __half* __restrict__ delta,
+                                                          const float* __restrict__ w, float eps,
+                                                          __half* x_out, __half* __restrict__ h,
+                                                          int M, int H) {
+  ptx::pdl_wait();  // x / delta come from the previous kernels
+  ptx::pdl_launch_dependents();
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const int nch = H / 8;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * H);
+  const uint4* dr = delta ? reinterpret_cast<const uint4*>(delta + (size_t)row * H) : nullptr;
+  uint4* xo = x_out ? reinterpret_cast<uint4*>(x_out + (size_t)row * H) : nullptr;
+  uint4* hr = reinterpret_cast<uint4*>(h + (size_t)row * H);
+  const bool in_regs = nch <= 32 * NM_REG_CHUNKS;
+  uint4 v[NM_REG_CHUNKS];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < NM_REG_CHUNKS; ++j) {
+    const int c = lane + 32 * j;
+    if (in_regs && c < nch) {
+      v[j] = dr ? nm_add8(xr[c], dr[c]) : xr[c];
+      if (xo) xo[c] = v[j];
+      ss += nm_sumsq8(v[j]);
+    }
+  }
+  if (!in_regs) {
+    for (int c = lane; c < nch; c += 32) {
+      const uint4 s = dr ? nm_add8(xr[c], dr[c]) : xr[c];
+      if (xo) xo[c] = s;
+      ss += nm_sumsq8(s);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float r = rsqrtf(ss / (float)H + eps);
+  if (in_regs) {
+#pragma unroll
+    for (int j = 0; j < NM_REG_CHUNKS; ++j) {
+      const int c = lane + 32 * j;
+      if (c < nch) hr[c] = nm_scale8(v[j], r, w + 8 * c);
+    }
+  } else {
+    for (int c = lane; c < nch; c += 32) {  // x_out may alias x: re-read the stored sum
+      const uint4 s = xo ? xo[c] : (dr ? nm_add8(xr[c], dr[c]) : xr[c]);
+      hr[c] = nm_scale8(s, r, w + 8 * c);
+    }
+  }
+}
+
+int launch_add_rmsnorm(const __half* x, const __half* delta, const float* w, float eps,
+                       __half* x_out, __half* h, int M, int H, cudaStream_t s) {
+  if (M < 0 || H < 8 || H % 8 != 0) return DDQ_ERR_SHAPE;
+  if (M == 0) return DDQ_OK;
+  if (!aligned16(x) || (delta && !aligned16(delta)) || !aligned16(w) ||
+      (x_out && !aligned16(x_out)) || !aligned16(h))
+    return DDQ_ERR_ALIGNMENT;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((M + 7) / 8));
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute at;
+  at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at.val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = &at;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel, x, delta, w, eps, x_out, h, M, H) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return DDQ_ERR_LAUNCH;
+  }
+  return check_launch();
+}
+
+}  // namespace ddq

@@ -42,7 +42,7 @@ from typing import List, Optional
 import torch
 import torch.nn.functional as F
 
-from . import attention, gemm_fp8, lm_head as lmh
+from . import attention, gemm_fp8, lm_head as lmh, norm
 
 E4M3_DECODE_LUT = None
 
@@ -217,6 +217,16 @@ class Engine:
         r = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.cfg.rms_norm_eps)
         return (xf * r * w).half()
 
+    def add_rmsnorm(self, x: torch.Tensor, w: torch.Tensor, delta: Optional[torch.Tensor] = None):
+        """(x + delta, rmsnorm(x + delta)): one kernel on the fp8 path, the fp32
+        torch operations of ``rmsnorm`` otherwise."""
+        if self.linear_kind == "fp8":
+            return norm.add_rmsnorm(x.contiguous(), w, self.cfg.rms_norm_eps,
+                                    None if delta is None else delta.contiguous())
+        if delta is not None:
+            x = x + delta
+        return x, self.rmsnorm(x, w)
+
     def rope_tables(self, positions: torch.Tensor):
         f = positions.float()[:, None] * self._inv_freq[None, :]
         emb = torch.cat([f, f], dim=-1)
@@ -244,7 +254,7 @@ class Engine:
         L = self.layers[li]
         B, S, H = x.shape
         hd, nh, nkv = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads
-        h = self.rmsnorm(x, L["in_norm"])
+        _, h = self.add_rmsnorm(x, L["in_norm"])
         qkv = self.linear(h, L["qkv"])
         scale = hd ** -0.5
         if pos is not None and S == 1 and self.linear_kind == "fp8":
@@ -252,7 +262,7 @@ class Engine:
             o = attention.decode_attention(qkv.reshape(B, -1), cache.k[li, b0:b0 + B],
                                            cache.v[li, b0:b0 + B], cos, sin, pos, nh, nkv, hd,
                                            scale)
-            return self._mlp_block(x + self.linear(o.reshape(B, S, nh * hd), L["o"]), L)
+            return self._mlp_block(x, self.linear(o.reshape(B, S, nh * hd), L["o"]), L)
         q = qkv[..., : nh * hd].reshape(B, S, nh, hd).transpose(1, 2)
         k = qkv[..., nh * hd: (nh + nkv) * hd].reshape(B, S, nkv, hd).transpose(1, 2)
         v = qkv[..., (nh + nkv) * hd:].reshape(B, S, nkv, hd).transpose(1, 2)
@@ -272,11 +282,11 @@ class Engine:
             o = F.scaled_dot_product_attention(q, kc, vc, attn_mask=mask, scale=scale,
                                                enable_gqa=True)
         o = o.transpose(1, 2).reshape(B, S, nh * hd)
-        return self._mlp_block(x + self.linear(o, L["o"]), L)
+        return self._mlp_block(x, self.linear(o, L["o"]), L)
 
-    def _mlp_block(self, x: torch.Tensor, L: dict) -> torch.Tensor:
-        """RMSNorm -> gate/up -> SwiGLU -> down -> +residual."""
-        h = self.rmsnorm(x, L["post_norm"])
+    def _mlp_block(self, x: torch.Tensor, attn: torch.Tensor, L: dict) -> torch.Tensor:
+        """+attention residual -> RMSNorm -> gate/up -> SwiGLU -> down -> +residual."""
+        x, h = self.add_rmsnorm(x, L["post_norm"], attn)
         if self.linear_kind == "fp8":   # gate/up GEMM with the SwiGLU epilogue
             z = gemm_fp8.f8_forward_swiglu(h, *L["gate_up"].gate_up_interleaved())
         else:
@@ -293,7 +303,7 @@ class Engine:
             cos, sin = self.rope_tables(pos)
         for li in range(self.cfg.num_hidden_layers):
             x = self._layer(li, x, cache, b0, cos, sin, pos, start)
-        return self.rmsnorm(x, self.final_norm)
+        return self.add_rmsnorm(x, self.final_norm)[1]
 
     def greedy(self, h: torch.Tensor) -> torch.Tensor:
         """Greedy token of each row of h [M, H] (fused lm_head argmax, or the oracle)."""

@@ -155,6 +155,17 @@ int ddq_decode_attention(const void* qkv, int64_t qkv_stride, void* k_cache, voi
                          void* stream);
 
 /*
+ * Residual add + RMSNorm over rows of H (H % 8 == 0, 16-byte aligned rows):
+ *   s = fp16(x + delta)   (delta may be NULL: s = x); written to x_out if
+ *                         non-NULL (x_out may be x)
+ *   h = fp16( s * rsqrt(mean(s^2) + eps) * w )   fp32 math, w fp32 [H]
+ * Replaces: qwen2_rmsnorm_kernel (RMSnorm_d.cu:23-87) and the residual add
+ * before it (engine.py:254-256).
+ */
+int ddq_add_rmsnorm(const void* x, const void* delta, const float* w, float eps,
+                    void* x_out, void* h, int64_t M, int64_t H, void* stream);
+
+/*
  * Greedy argmax over fp16 logits [B, V] -> int64 [B]; ties go to the
  * lowest index.  Replaces: sampler_d.cu:10-70 (argmax_kernel + forward).
  */
