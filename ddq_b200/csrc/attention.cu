@@ -12,10 +12,12 @@
 // weighted sum in fp32; o rounded to fp16.  The position is read on the
 // device, so a captured CUDA graph replays it for every step.
 //
-// Work split: the 8 warps take 32-position tiles in turn (lane = position for
-// the scores, lane = two head dimensions for the weighted sum of V) with an
-// online softmax per query head; the CTA merges the 8 partial results in
-// shared memory.  K rows are read once per CTA, by one lane each (128
+// Work split: the warps (16 for 64-wide heads) take 32-position tiles in
+// turn (lane = position for the scores, lane = D / 32 head dimensions for the
+// weighted sum of V) with an online softmax per query head; the CTA merges
+// the warps' partial results in shared memory.  Every K row and every group
+// of 16 V rows is requested before it is used, so a warp waits on memory once
+// per step instead of once per row.  K rows are read once per CTA, by one lane each (128
 // contiguous bytes); V rows once, coalesced across the warp.  The step reads
 // the cache at HBM rate; the arithmetic runs on the CUDA cores.
 #include <cfloat>
@@ -26,8 +28,10 @@
 
 namespace ddq {
 
-constexpr int AT_WARPS = 8;
 constexpr int AT_GMAX = 8;  // query heads per key/value head, at most
+// warps per CTA: 16 for 64-wide heads (one 32-position tile per warp for
+// contexts up to 512), 8 for 128-wide heads (register budget)
+__host__ __device__ constexpr int at_warps(int d) { return d == 64 ? 16 : 8; }
 
 struct AtArgs {
   const __half* qkv;     // [B, (Hq + 2 Hkv) * D] row stride qkv_stride
@@ -46,15 +50,16 @@ struct AtArgs {
 };
 
 template <int D>
-__global__ void __launch_bounds__(AT_WARPS * 32) decode_attention_kernel(const AtArgs a) {
+__global__ void __launch_bounds__(at_warps(D) * 32, 1) decode_attention_kernel(const AtArgs a) {
+  constexpr int NW = at_warps(D);
   constexpr int DH = D / 2;
   constexpr int DPL = D / 32;  // head dimensions per lane in the weighted sum
   const int b = blockIdx.x / a.Hkv, g = blockIdx.x % a.Hkv;
   const int G = a.Hq / a.Hkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __shared__ float q_s[AT_GMAX][D];
-  __shared__ float m_s[AT_WARPS][AT_GMAX], l_s[AT_WARPS][AT_GMAX];
-  __shared__ float acc_s[AT_WARPS][AT_GMAX][D];
+  __shared__ __align__(16) float q_s[AT_GMAX][D];
+  __shared__ float m_s[NW][AT_GMAX], l_s[NW][AT_GMAX];
+  __shared__ float acc_s[NW][AT_GMAX][D];
 
   ptx::pdl_wait();  // qkv comes from the previous kernel
   const int64_t p = *a.pos;
@@ -98,31 +103,51 @@ __global__ void __launch_bounds__(AT_WARPS * 32) decode_attention_kernel(const A
 #pragma unroll
     for (int t = 0; t < DPL; ++t) acc[h][t] = 0.f;
   }
-  for (int t0 = warp * 32; t0 < L; t0 += AT_WARPS * 32) {
+  for (int t0 = warp * 32; t0 < L; t0 += NW * 32) {
     const int j = t0 + lane;
     const bool ok = j < L;
     float s[AT_GMAX];
 #pragma unroll
     for (int h = 0; h < AT_GMAX; ++h) s[h] = 0.f;
     if (ok) {
+      // the whole K row in flight at once, then G dot products against q
       const uint4* kr = reinterpret_cast<const uint4*>(kc + (size_t)j * D);
+      uint4 kv[D / 8];
+#pragma unroll
+      for (int c = 0; c < D / 8; ++c) kv[c] = kr[c];
 #pragma unroll
       for (int c = 0; c < D / 8; ++c) {
-        const uint4 u = kr[c];
-        const __half2* hv = reinterpret_cast<const __half2*>(&u);
+        const __half2* hv = reinterpret_cast<const __half2*>(&kv[c]);
+        float kf[8];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 kf = __half22float2(hv[e]);
-          const int d = c * 8 + 2 * e;
+        for (int t = 0; t < 4; ++t) {
+          const float2 f = __half22float2(hv[t]);
+          kf[2 * t] = f.x;
+          kf[2 * t + 1] = f.y;
+        }
 #pragma unroll
-          for (int h = 0; h < AT_GMAX; ++h)
-            if (h < G) s[h] = fmaf(q_s[h][d], kf.x, fmaf(q_s[h][d + 1], kf.y, s[h]));
+        for (int h = 0; h < AT_GMAX; ++h) {
+          if (h < G) {
+            const float4 qa = *reinterpret_cast<const float4*>(&q_s[h][c * 8]);
+            const float4 qb = *reinterpret_cast<const float4*>(&q_s[h][c * 8 + 4]);
+            float acc_s8 = s[h];
+            acc_s8 = fmaf(qa.x, kf[0], acc_s8);
+            acc_s8 = fmaf(qa.y, kf[1], acc_s8);
+            acc_s8 = fmaf(qa.z, kf[2], acc_s8);
+            acc_s8 = fmaf(qa.w, kf[3], acc_s8);
+            acc_s8 = fmaf(qb.x, kf[4], acc_s8);
+            acc_s8 = fmaf(qb.y, kf[5], acc_s8);
+            acc_s8 = fmaf(qb.z, kf[6], acc_s8);
+            acc_s8 = fmaf(qb.w, kf[7], acc_s8);
+            s[h] = acc_s8;
+          }
         }
       }
     }
     float pr[AT_GMAX];
 #pragma unroll
     for (int h = 0; h < AT_GMAX; ++h) {
+      pr[h] = 0.f;
       if (h >= G) continue;
       const float sv = ok ? s[h] * a.scale : -FLT_MAX;
       float tm = sv;
@@ -139,24 +164,44 @@ __global__ void __launch_bounds__(AT_WARPS * 32) decode_attention_kernel(const A
 #pragma unroll
       for (int t = 0; t < DPL; ++t) acc[h][t] *= corr;
     }
-    const int jn = min(32, L - t0);
-    for (int jj = 0; jj < jn; ++jj) {
-      const __half* vr = vc + (size_t)(t0 + jj) * D + lane * DPL;
-      float vf[DPL];
-      if constexpr (DPL == 2) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(vr));
-        vf[0] = f.x;
-        vf[1] = f.y;
-      } else {
+    // weighted sum of V: 16 rows at a time, all their loads in flight first;
+    // rows past the last position read as zero (their weights are zero too)
 #pragma unroll
-        for (int t = 0; t < DPL; ++t) vf[t] = __half2float(vr[t]);
+    for (int j0 = 0; j0 < 32; j0 += 16) {
+      if (t0 + j0 >= L) break;
+      float vf[16][DPL];
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj) {
+        const int pj = t0 + j0 + jj;
+        const __half* vr = vc + (size_t)pj * D + lane * DPL;
+        if (pj < L) {
+          if constexpr (DPL == 2) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(vr));
+            vf[jj][0] = f.x;
+            vf[jj][1] = f.y;
+          } else {
+            const uint2 u = *reinterpret_cast<const uint2*>(vr);
+            const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+            const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+            vf[jj][0] = f0.x;
+            vf[jj][1] = f0.y;
+            vf[jj][2] = f1.x;
+            vf[jj][3] = f1.y;
+          }
+        } else {
+#pragma unroll
+          for (int t = 0; t < DPL; ++t) vf[jj][t] = 0.f;
+        }
       }
 #pragma unroll
-      for (int h = 0; h < AT_GMAX; ++h) {
-        if (h >= G) continue;
-        const float pj = __shfl_sync(0xffffffffu, pr[h], jj);
+      for (int jj = 0; jj < 16; ++jj) {
 #pragma unroll
-        for (int t = 0; t < DPL; ++t) acc[h][t] = fmaf(pj, vf[t], acc[h][t]);
+        for (int h = 0; h < AT_GMAX; ++h) {
+          if (h >= G) continue;
+          const float pj = __shfl_sync(0xffffffffu, pr[h], j0 + jj);
+#pragma unroll
+          for (int t = 0; t < DPL; ++t) acc[h][t] = fmaf(pj, vf[jj][t], acc[h][t]);
+        }
       }
     }
   }
@@ -176,9 +221,9 @@ __global__ void __launch_bounds__(AT_WARPS * 32) decode_attention_kernel(const A
   for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
     const int h = i / D, d = i % D;
     float mx = -FLT_MAX;
-    for (int w = 0; w < AT_WARPS; ++w) mx = fmaxf(mx, m_s[w][h]);
+    for (int w = 0; w < NW; ++w) mx = fmaxf(mx, m_s[w][h]);
     float den = 0.f, num = 0.f;
-    for (int w = 0; w < AT_WARPS; ++w) {
+    for (int w = 0; w < NW; ++w) {
       const float c = l_s[w][h] > 0.f ? __expf(m_s[w][h] - mx) : 0.f;
       den = fmaf(l_s[w][h], c, den);
       num = fmaf(acc_s[w][h][d], c, num);
@@ -199,7 +244,7 @@ int launch_decode_attention(const __half* qkv, int64_t qkv_stride, __half* kc, _
            scale};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(B * Hkv));
-  cfg.blockDim = dim3(AT_WARPS * 32);
+  cfg.blockDim = dim3(at_warps(D) * 32);
   cfg.stream = s;
   cudaLaunchAttribute at;
   at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
