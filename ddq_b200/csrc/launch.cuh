@@ -55,7 +55,8 @@ int launch_pf(const __half* x, const uint8_t* wq, const float* scales, const voi
 int launch_decode_attention(const __half* qkv, int64_t qkv_stride, __half* kc, __half* vc,
                             int64_t cache_bstride, int cap, const float* cos, const float* sin,
                             const int64_t* pos, __half* out, int64_t out_stride, int B, int Hq,
-                            int Hkv, int D, float scale, cudaStream_t s);
+                            int Hkv, int D, float scale, unsigned long long timeout_ns,
+                            cudaStream_t s);
 // Residual add + RMSNorm (norm.cu).
 int launch_add_rmsnorm(const __half* x, const __half* delta, const float* w, float eps,
                        __half* x_out, __half* h, int M, int H, cudaStream_t s);
