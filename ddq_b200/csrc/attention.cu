@@ -255,6 +255,7 @@ struct At2Smem {
   float q[AT_GMAX][64];
   float acc[AT2_NW][AT_GMAX][64];
   float m[AT2_NW][AT_GMAX], l[AT2_NW][AT_GMAX];
+  float p[AT2_NW][AT_GMAX][AT2_ROWS];           // per warp: this chunk's weights
   unsigned long long full[AT2_NW];
   int abort_flag;
 };
@@ -262,6 +263,7 @@ struct At2Smem {
 // byte offset of 16-byte chunk j of row r in a 128-byte-swizzled tile
 __device__ __forceinline__ uint32_t at2_swz(int r, int j) { return r * 128 + ((j ^ (r & 7)) << 4); }
 
+template <int G>
 __global__ void __launch_bounds__(AT2_NW * 32, 1)
     decode_attention_tma_kernel(const __grid_constant__ CUtensorMap tm_k,
                                 const __grid_constant__ CUtensorMap tm_v, const AtArgs a,
@@ -271,7 +273,6 @@ __global__ void __launch_bounds__(AT2_NW * 32, 1)
   At2Smem& sm = *reinterpret_cast<At2Smem*>((reinterpret_cast<uintptr_t>(at2_raw) + 1023) &
                                             ~static_cast<uintptr_t>(1023));
   const int b = blockIdx.x / a.Hkv, g = blockIdx.x % a.Hkv;
-  const int G = a.Hq / a.Hkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int w = 0; w < AT2_NW; ++w) ptx::mbar_init(ptx::smem_u32(&sm.full[w]), 1);
@@ -323,13 +324,14 @@ __global__ void __launch_bounds__(AT2_NW * 32, 1)
   };
   if (lane == 0 && warp < nchunks) issue(warp);
 
-  float m[AT_GMAX], l[AT_GMAX], acc[AT_GMAX][2];
+  float m[G], l[G], acc[G][2];
 #pragma unroll
-  for (int h = 0; h < AT_GMAX; ++h) {
+  for (int h = 0; h < G; ++h) {
     m[h] = -FLT_MAX;
     l[h] = 0.f;
     acc[h][0] = acc[h][1] = 0.f;
   }
+  float* pw = &sm.p[warp][0][0];
   int phase = 0, pending = warp < nchunks ? 1 : 0;
   for (int c = warp; c < nchunks; c += AT2_NW, phase ^= 1) {
     if (!ptx::mbar_wait(full, (uint32_t)phase, timeout_ns, &sm.abort_flag)) break;
@@ -337,12 +339,11 @@ __global__ void __launch_bounds__(AT2_NW * 32, 1)
     const uint8_t* ks = &sm.ring[warp][0][0];
     const uint8_t* vs = &sm.ring[warp][1][0];
     const int t0 = c * AT2_ROWS;
-    const int j = t0 + lane;
-    const bool ok = j < L;
+    const bool ok = t0 + lane < L;
     // scores: lane = position, its K row from the swizzled tile
-    float s[AT_GMAX];
+    float s[G];
 #pragma unroll
-    for (int h = 0; h < AT_GMAX; ++h) s[h] = 0.f;
+    for (int h = 0; h < G; ++h) s[h] = 0.f;
 #pragma unroll
     for (int cc = 0; cc < D / 8; ++cc) {
       const uint4 u = *reinterpret_cast<const uint4*>(ks + at2_swz(lane, cc));
@@ -355,36 +356,33 @@ __global__ void __launch_bounds__(AT2_NW * 32, 1)
         kf[2 * t + 1] = f.y;
       }
 #pragma unroll
-      for (int h = 0; h < AT_GMAX; ++h) {
-        if (h < G) {
-          const float4 qa = *reinterpret_cast<const float4*>(&sm.q[h][cc * 8]);
-          const float4 qb = *reinterpret_cast<const float4*>(&sm.q[h][cc * 8 + 4]);
-          float v = s[h];
-          v = fmaf(qa.x, kf[0], v);
-          v = fmaf(qa.y, kf[1], v);
-          v = fmaf(qa.z, kf[2], v);
-          v = fmaf(qa.w, kf[3], v);
-          v = fmaf(qb.x, kf[4], v);
-          v = fmaf(qb.y, kf[5], v);
-          v = fmaf(qb.z, kf[6], v);
-          v = fmaf(qb.w, kf[7], v);
-          s[h] = v;
-        }
+      for (int h = 0; h < G; ++h) {
+        const float4 qa = *reinterpret_cast<const float4*>(&sm.q[h][cc * 8]);
+        const float4 qb = *reinterpret_cast<const float4*>(&sm.q[h][cc * 8 + 4]);
+        float v = s[h];
+        v = fmaf(qa.x, kf[0], v);
+        v = fmaf(qa.y, kf[1], v);
+        v = fmaf(qa.z, kf[2], v);
+        v = fmaf(qa.w, kf[3], v);
+        v = fmaf(qb.x, kf[4], v);
+        v = fmaf(qb.y, kf[5], v);
+        v = fmaf(qb.z, kf[6], v);
+        v = fmaf(qb.w, kf[7], v);
+        s[h] = v;
       }
     }
-    float pr[AT_GMAX];
+    // online softmax per query head; this chunk's weights go to shared memory
 #pragma unroll
-    for (int h = 0; h < AT_GMAX; ++h) {
-      pr[h] = 0.f;
-      if (h >= G) continue;
+    for (int h = 0; h < G; ++h) {
       const float sv = ok ? s[h] * a.scale : -FLT_MAX;
       float tm = sv;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, o));
       const float mn = fmaxf(m[h], tm);
       const float corr = __expf(m[h] - mn);
-      pr[h] = ok ? __expf(sv - mn) : 0.f;
-      float ps = pr[h];
+      const float pv = ok ? __expf(sv - mn) : 0.f;
+      pw[h * AT2_ROWS + lane] = pv;
+      float ps = pv;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
       l[h] = l[h] * corr + ps;
@@ -392,21 +390,32 @@ __global__ void __launch_bounds__(AT2_NW * 32, 1)
       acc[h][0] *= corr;
       acc[h][1] *= corr;
     }
-    // weighted sum: lane = head dimensions 2 lane, 2 lane + 1 of each V row
+    __syncwarp();
+    // weighted sum: lane = head dimensions 2 lane, 2 lane + 1 of each V row;
+    // rows past the last position are skipped (the cache there is not ours)
     const int jn = min(AT2_ROWS, L - t0);
     const uint32_t voff = (uint32_t)(lane >> 2), vsub = (uint32_t)(lane & 3) * 4;
-    for (int jj = 0; jj < jn; ++jj) {
-      const float2 vf = __half22float2(
-          *reinterpret_cast<const __half2*>(vs + at2_swz(jj, (int)voff) + vsub));
 #pragma unroll
-      for (int h = 0; h < AT_GMAX; ++h) {
-        if (h >= G) continue;
-        const float pj = __shfl_sync(0xffffffffu, pr[h], jj);
-        acc[h][0] = fmaf(pj, vf.x, acc[h][0]);
-        acc[h][1] = fmaf(pj, vf.y, acc[h][1]);
+    for (int j4 = 0; j4 < AT2_ROWS; j4 += 4) {
+      if (j4 >= jn) break;
+      float2 vf[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t)
+        vf[t] = j4 + t < jn ? __half22float2(*reinterpret_cast<const __half2*>(
+                                  vs + at2_swz(j4 + t, (int)voff) + vsub))
+                            : make_float2(0.f, 0.f);
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const float4 p4 = *reinterpret_cast<const float4*>(pw + h * AT2_ROWS + j4);
+        const float pp[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          acc[h][0] = fmaf(pp[t], vf[t].x, acc[h][0]);
+          acc[h][1] = fmaf(pp[t], vf[t].y, acc[h][1]);
+        }
       }
     }
-    // the slot is free: fetch this warp's next chunk into it
+    // the slot and the weights are free: fetch this warp's next chunk
     __syncwarp();
     ptx::fence_proxy_async_smem();
     if (c + AT2_NW < nchunks) {
@@ -424,8 +433,7 @@ __global__ void __launch_bounds__(AT2_NW * 32, 1)
 
   // ---- merge the warps' partial softmax sums
 #pragma unroll
-  for (int h = 0; h < AT_GMAX; ++h) {
-    if (h >= G) continue;
+  for (int h = 0; h < G; ++h) {
     if (lane == 0) {
       sm.m[warp][h] = m[h];
       sm.l[warp][h] = l[h];
@@ -509,17 +517,28 @@ int launch_decode_attention(const __half* qkv, int64_t qkv_stride, __half* kc, _
     if (st) return st;
     const int dev = current_device();
     if (dev < 0 || dev >= 64) return DDQ_ERR_DEVICE;
-    static bool attr_set[64] = {};
+    static bool attr_set[AT_GMAX][64] = {};
     const int smem = (int)sizeof(At2Smem) + 1024;
-    if (!attr_set[dev]) {
-      if (cudaFuncSetAttribute(decode_attention_tma_kernel,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-        return DDQ_ERR_LAUNCH;
-      attr_set[dev] = true;
-    }
     cfg.blockDim = dim3(AT2_NW * 32);
     cfg.dynamicSmemBytes = smem;
-    e = cudaLaunchKernelEx(&cfg, decode_attention_tma_kernel, tk, tv, a, timeout_ns);
+    switch (Hq / Hkv) {
+#define DDQ_AT_G(G_)                                                                     \
+  case G_:                                                                               \
+    if (!attr_set[G_ - 1][dev]) {                                                        \
+      if (cudaFuncSetAttribute(decode_attention_tma_kernel<G_>,                          \
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=     \
+          cudaSuccess)                                                                   \
+        return DDQ_ERR_LAUNCH;                                                           \
+      attr_set[G_ - 1][dev] = true;                                                      \
+    }                                                                                    \
+    e = cudaLaunchKernelEx(&cfg, decode_attention_tma_kernel<G_>, tk, tv, a, timeout_ns); \
+    break;
+      DDQ_AT_G(1) DDQ_AT_G(2) DDQ_AT_G(3) DDQ_AT_G(4)
+      DDQ_AT_G(5) DDQ_AT_G(6) DDQ_AT_G(7) DDQ_AT_G(8)
+#undef DDQ_AT_G
+      default:
+        return DDQ_ERR_SHAPE;
+    }
   } else {
     e = cudaLaunchKernelEx(&cfg, decode_attention_kernel<128>, a);
   }
