@@ -32,6 +32,10 @@ _SIGNATURES = {
                                             _c_int64, ctypes.c_float, _vp]),
     "ddq_add_rmsnorm": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_float, _vp, _vp, _c_int64,
                                        _c_int64, _vp]),
+    "ddq_add_rmsnorm_split": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_float, _vp, _vp, _vp, _vp,
+                                             _c_int64, _c_int64, _vp]),
+    "ddq_w8a16_gemm_planes": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, ctypes.c_int, _vp,
+                                             _c_int64, _c_int64, _c_int64, ctypes.c_int, _vp]),
     "ddq_argmax_f16": (ctypes.c_int, [_vp, _c_int64, _c_int64, _vp, _vp]),
     "ddq_lm_head_argmax_workspace_size": (ctypes.c_size_t, [_c_int64, _c_int64, _c_int64]),
     "ddq_lm_head_argmax": (ctypes.c_int, [_vp, _vp, _vp, _c_int64, _c_int64, _c_int64, _c_int64,

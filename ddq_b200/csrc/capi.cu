@@ -201,6 +201,38 @@ extern "C" int ddq_add_rmsnorm(const void* x, const void* delta, const float* w,
                             (int)M, (int)H, reinterpret_cast<cudaStream_t>(stream));
 }
 
+extern "C" int ddq_add_rmsnorm_split(const void* x, const void* delta, const float* w, float eps,
+                                     void* x_out, void* h, uint8_t* planes, float* xscale,
+                                     int64_t M, int64_t H, void* stream) {
+  if (M < 0 || H < 0) return DDQ_ERR_SHAPE;
+  if (M == 0) return DDQ_OK;
+  if (!x || !w || !planes || !xscale) return DDQ_ERR_INVALID_ARGUMENT;
+  if (M > 0x7fffffff || H > 0x7fffffff) return DDQ_ERR_SHAPE;
+  return launch_add_rmsnorm_split(
+      reinterpret_cast<const __half*>(x), reinterpret_cast<const __half*>(delta), w, eps,
+      reinterpret_cast<__half*>(x_out), reinterpret_cast<__half*>(h), planes, xscale, (int)M,
+      (int)H, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ddq_w8a16_gemm_planes(const uint8_t* planes, const float* xscale,
+                                     const uint8_t* wq, const float* scales, const void* bias,
+                                     int bias_dtype, void* y, int64_t M, int64_t N, int64_t K,
+                                     int swiglu, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return DDQ_ERR_SHAPE;
+  if (bias_dtype != DDQ_DTYPE_NONE && bias_dtype != DDQ_DTYPE_F16 && bias_dtype != DDQ_DTYPE_F32)
+    return DDQ_ERR_INVALID_ARGUMENT;
+  if (bias_dtype != DDQ_DTYPE_NONE && !bias) return DDQ_ERR_INVALID_ARGUMENT;
+  if (M == 0 || N == 0) return DDQ_OK;
+  if (!planes || !xscale || !wq || !scales || !y) return DDQ_ERR_INVALID_ARGUMENT;
+  if (M > kDecodeMaxM || K == 0 || K % 16 != 0 || N > 0x7fffffff || K > 0x7fffffff ||
+      (swiglu && N % 32 != 0))
+    return DDQ_ERR_SHAPE;
+  if (!aligned16(wq) || !aligned16(y)) return DDQ_ERR_ALIGNMENT;
+  return launch_dec(nullptr, wq, scales, bias, bias_dtype, reinterpret_cast<__half*>(y), nullptr,
+                    0, (int)M, (int)N, (int)K, nullptr, 0, g_wait_timeout_ns, g_debug_flags,
+                    reinterpret_cast<cudaStream_t>(stream), swiglu != 0, planes, xscale);
+}
+
 extern "C" int ddq_argmax_f16(const void* logits, int64_t B, int64_t V, int64_t* out,
                               void* stream) {
   if (B < 0 || V < 0) return DDQ_ERR_SHAPE;

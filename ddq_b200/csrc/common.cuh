@@ -1,6 +1,8 @@
 // common.cuh - shared device helpers for the sm_100a W8A16 kernels.
 #pragma once
 
+#include <cfloat>
+
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <cuda_fp8.h>
@@ -51,6 +53,40 @@ __device__ __forceinline__ uint16_t float2_to_e4m3x2(float a, float b) {
 }
 
 // Monotone 16-bit key of an fp16 value: larger fp16 -> larger key.
+// Split 8 fp32 values (already scaled by 2^e) into three e4m3 planes; the
+// bytes keep the element order (element 0 -> lowest byte).
+__device__ __forceinline__ void split8(const float* z, uint2& p1, uint2& p2, uint2& p3) {
+  uint32_t o1[2] = {0u, 0u}, o2[2] = {0u, 0u}, o3[2] = {0u, 0u};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float z0 = z[2 * i], z1 = z[2 * i + 1];
+    const uint16_t b1 = float2_to_e4m3x2(z0, z1);
+    const float2 d1 = e4m3x2_to_float2(b1);
+    const float r0 = z0 - d1.x, r1 = z1 - d1.y;  // exact (Sterbenz)
+    const uint16_t b2 = float2_to_e4m3x2(r0, r1);
+    const float2 d2 = e4m3x2_to_float2(b2);
+    const uint16_t b3 = float2_to_e4m3x2(r0 - d2.x, r1 - d2.y);
+    const int word = i >> 1, sh = (i & 1) * 16;
+    o1[word] |= (uint32_t)b1 << sh;
+    o2[word] |= (uint32_t)b2 << sh;
+    o3[word] |= (uint32_t)b3 << sh;
+  }
+  p1 = make_uint2(o1[0], o1[1]);
+  p2 = make_uint2(o2[0], o2[1]);
+  p3 = make_uint2(o3[0], o3[1]);
+}
+
+// Power-of-two shift e of a token row for the three-plane split: with the row
+// maximum amax = f * 2^ex (f in [0.5, 1)), z = x * 2^e has max |z| in
+// [128, 256), the top binade of e4m3 below its 448 limit; 0 for an all-zero
+// or non-finite row.
+__device__ __forceinline__ int split_shift(float amax) {
+  int ex = 0;
+  const bool finite = amax > 0.f && amax <= FLT_MAX;
+  if (finite) frexpf(amax, &ex);
+  return finite ? 8 - ex : 0;
+}
+
 __device__ __forceinline__ uint32_t f16_order_key(__half h) {
   uint16_t b = __half_as_ushort(h);
   return (b & 0x8000u) ? (uint32_t)(uint16_t)(~b) : (uint32_t)(b | 0x8000u);

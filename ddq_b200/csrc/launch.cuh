@@ -43,7 +43,8 @@ DecPlan dec_plan(int64_t M, int64_t N, int64_t K, int sms, bool no_split = false
 int launch_dec(const __half* x, const uint8_t* wq, const float* scales, const void* bias,
                int bias_dtype, __half* y, unsigned long long* packed, int64_t vocab_offset, int M,
                int N, int K, void* ws, size_t ws_bytes, unsigned long long timeout_ns,
-               int debug_flags, cudaStream_t s, bool swiglu = false);
+               int debug_flags, cudaStream_t s, bool swiglu = false,
+               const uint8_t* ext_planes = nullptr, const float* ext_xscale = nullptr);
 // Prefill shapes: exact e4m3 -> fp16 weight expansion into the workspace
 // (N * K * 2 bytes), then the fp16 tensor-core GEMM (tc_prefill.cu).
 size_t pf_workspace_bytes(int64_t N, int64_t K);
@@ -57,6 +58,11 @@ int launch_decode_attention(const __half* qkv, int64_t qkv_stride, __half* kc, _
                             const int64_t* pos, __half* out, int64_t out_stride, int B, int Hq,
                             int Hkv, int D, float scale, unsigned long long timeout_ns,
                             cudaStream_t s);
+// Residual add + RMSNorm, optionally followed by the three-plane split of the
+// result for a decode GEMM (norm.cu).
+int launch_add_rmsnorm_split(const __half* x, const __half* delta, const float* w, float eps,
+                             __half* x_out, __half* h, uint8_t* planes, float* xscale, int M,
+                             int H, cudaStream_t s);
 // Residual add + RMSNorm (norm.cu).
 int launch_add_rmsnorm(const __half* x, const __half* delta, const float* w, float eps,
                        __half* x_out, __half* h, int M, int H, cudaStream_t s);

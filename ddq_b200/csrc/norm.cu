@@ -102,6 +102,104 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(const __half* x,
   }
 }
 
+// The same, followed by the three-plane e4m3 split of h that the decode GEMM
+// takes as its B operand (as xsplit_kernel would produce it from h): planes
+// [3][M][H], token scales 2^-e [M].  h itself is stored only if asked for.
+// Rows of up to 2048 elements (one warp, in registers).
+__global__ void __launch_bounds__(256) add_rmsnorm_split_kernel(
+    const __half* x, const __half* __restrict__ delta, const float* __restrict__ w, float eps,
+    __half* x_out, __half* __restrict__ h, uint8_t* __restrict__ planes,
+    float* __restrict__ xscale, int M, int H) {
+  ptx::pdl_wait();
+  ptx::pdl_launch_dependents();
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const int nch = H / 8;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * H);
+  const uint4* dr = delta ? reinterpret_cast<const uint4*>(delta + (size_t)row * H) : nullptr;
+  uint4* xo = x_out ? reinterpret_cast<uint4*>(x_out + (size_t)row * H) : nullptr;
+  uint4 v[NM_REG_CHUNKS];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < NM_REG_CHUNKS; ++j) {
+    const int c = lane + 32 * j;
+    if (c < nch) {
+      v[j] = dr ? nm_add8(xr[c], dr[c]) : xr[c];
+      if (xo) xo[c] = v[j];
+      ss += nm_sumsq8(v[j]);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float r = rsqrtf(ss / (float)H + eps);
+  float amax = 0.f;
+#pragma unroll
+  for (int j = 0; j < NM_REG_CHUNKS; ++j) {
+    const int c = lane + 32 * j;
+    if (c < nch) {
+      v[j] = nm_scale8(v[j], r, w + 8 * c);
+      if (h) reinterpret_cast<uint4*>(h + (size_t)row * H)[c] = v[j];
+      const __half2* hv = reinterpret_cast<const __half2*>(&v[j]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(hv[i]);
+        amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const int e = split_shift(amax);
+  const float up = ldexpf(1.f, e);
+  if (lane == 0) xscale[row] = ldexpf(1.f, -e);
+  const size_t plane = (size_t)M * H;
+  uint8_t* p1 = planes + (size_t)row * H;
+#pragma unroll
+  for (int j = 0; j < NM_REG_CHUNKS; ++j) {
+    const int c = lane + 32 * j;
+    if (c < nch) {
+      const __half2* hv = reinterpret_cast<const __half2*>(&v[j]);
+      float z[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(hv[i]);
+        z[2 * i] = f.x * up;  // exact: power-of-two scale
+        z[2 * i + 1] = f.y * up;
+      }
+      uint2 a, b, cc;
+      split8(z, a, b, cc);
+      *reinterpret_cast<uint2*>(p1 + (size_t)c * 8) = a;
+      *reinterpret_cast<uint2*>(p1 + plane + (size_t)c * 8) = b;
+      *reinterpret_cast<uint2*>(p1 + 2 * plane + (size_t)c * 8) = cc;
+    }
+  }
+}
+
+int launch_add_rmsnorm_split(const __half* x, const __half* delta, const float* w, float eps,
+                             __half* x_out, __half* h, uint8_t* planes, float* xscale, int M,
+                             int H, cudaStream_t s) {
+  if (M < 0 || H < 16 || H % 16 != 0 || H > 32 * NM_REG_CHUNKS * 8) return DDQ_ERR_SHAPE;
+  if (M == 0) return DDQ_OK;
+  if (!aligned16(x) || (delta && !aligned16(delta)) || !aligned16(w) ||
+      (x_out && !aligned16(x_out)) || (h && !aligned16(h)) || !aligned16(planes))
+    return DDQ_ERR_ALIGNMENT;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((M + 7) / 8));
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute at;
+  at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at.val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = &at;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, add_rmsnorm_split_kernel, x, delta, w, eps, x_out, h, planes,
+                         xscale, M, H) != cudaSuccess) {
+    cudaGetLastError();
+    return DDQ_ERR_LAUNCH;
+  }
+  return check_launch();
+}
+
 int launch_add_rmsnorm(const __half* x, const __half* delta, const float* w, float eps,
                        __half* x_out, __half* h, int M, int H, cudaStream_t s) {
   if (M < 0 || H < 8 || H % 8 != 0) return DDQ_ERR_SHAPE;

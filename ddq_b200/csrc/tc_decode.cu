@@ -57,29 +57,6 @@ __host__ __device__ constexpr int dc_stage_k(int bt) { return bt <= 32 ? 256 : 1
 // ----------------------------------------------------------------------------
 // Activation split pre-pass
 // ----------------------------------------------------------------------------
-// Split 8 fp32 values (already scaled by 2^e) into three e4m3 planes; the
-// bytes keep the element order (element 0 -> lowest byte).
-__device__ __forceinline__ void split8(const float* z, uint2& p1, uint2& p2, uint2& p3) {
-  uint32_t o1[2] = {0u, 0u}, o2[2] = {0u, 0u}, o3[2] = {0u, 0u};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float z0 = z[2 * i], z1 = z[2 * i + 1];
-    const uint16_t b1 = float2_to_e4m3x2(z0, z1);
-    const float2 d1 = e4m3x2_to_float2(b1);
-    const float r0 = z0 - d1.x, r1 = z1 - d1.y;  // exact (Sterbenz)
-    const uint16_t b2 = float2_to_e4m3x2(r0, r1);
-    const float2 d2 = e4m3x2_to_float2(b2);
-    const uint16_t b3 = float2_to_e4m3x2(r0 - d2.x, r1 - d2.y);
-    const int word = i >> 1, sh = (i & 1) * 16;
-    o1[word] |= (uint32_t)b1 << sh;
-    o2[word] |= (uint32_t)b2 << sh;
-    o3[word] |= (uint32_t)b3 << sh;
-  }
-  p1 = make_uint2(o1[0], o1[1]);
-  p2 = make_uint2(o2[0], o2[1]);
-  p3 = make_uint2(o3[0], o3[1]);
-}
-
 // One CTA (256 threads) per token row; the row's 16-byte chunks stay in
 // registers (CPT per thread), so x is read once: load, row max, scale, split,
 // store.  Rows longer than 256 * CPT * 8 elements use the CPT = 0 variant,
@@ -129,10 +106,7 @@ __global__ void __launch_bounds__(256) xsplit_kernel(const __half* __restrict__ 
   amax = red[0];
 #pragma unroll
   for (int w = 1; w < 8; ++w) amax = fmaxf(amax, red[w]);
-  int ex = 0;
-  const bool finite = amax > 0.f && amax <= FLT_MAX;
-  if (finite) frexpf(amax, &ex);          // amax = f * 2^ex, f in [0.5, 1)
-  const int e = finite ? 8 - ex : 0;      // max |z| in [128, 256)
+  const int e = split_shift(amax);      // max |z| in [128, 256)
   const float up = ldexpf(1.f, e);
   if (threadIdx.x == 0) xscale[m] = ldexpf(1.f, -e);
   const size_t plane = (size_t)M * K;
@@ -859,19 +833,29 @@ DecPlan dec_plan(int64_t M, int64_t N, int64_t K, int sms, bool no_split) {
 int launch_dec(const __half* x, const uint8_t* wq, const float* scales, const void* bias,
                int bias_dtype, __half* y, unsigned long long* packed, int64_t vocab_offset, int M,
                int N, int K, void* ws, size_t ws_bytes, unsigned long long timeout_ns,
-               int debug_flags, cudaStream_t s, bool swiglu) {
+               int debug_flags, cudaStream_t s, bool swiglu, const uint8_t* ext_planes,
+               const float* ext_xscale) {
   const int sms = device_sm_count(current_device());
   if (sms <= 0) return DDQ_ERR_DEVICE;
   if (M < 1 || M > 64) return DDQ_ERR_SHAPE;
   if (swiglu && (packed || N % 32 != 0)) return DDQ_ERR_SHAPE;
   const DecPlan p = dec_plan(M, N, K, sms, swiglu);
-  if (!ws || ws_bytes < p.ws_bytes) return DDQ_ERR_WORKSPACE;
-  if (reinterpret_cast<uintptr_t>(ws) & 255u) return DDQ_ERR_ALIGNMENT;
-  uint8_t* planes = reinterpret_cast<uint8_t*>(ws);
-  float* xscale = reinterpret_cast<float*>(planes + ((p.plane_bytes + 255) & ~(size_t)255));
+  uint8_t* planes;
+  float* xscale;
+  if (ext_planes) {  // the caller split the activations already
+    if (!ext_xscale) return DDQ_ERR_INVALID_ARGUMENT;
+    if (reinterpret_cast<uintptr_t>(ext_planes) & 15u) return DDQ_ERR_ALIGNMENT;
+    planes = const_cast<uint8_t*>(ext_planes);
+    xscale = const_cast<float*>(ext_xscale);
+  } else {
+    if (!ws || ws_bytes < p.ws_bytes) return DDQ_ERR_WORKSPACE;
+    if (reinterpret_cast<uintptr_t>(ws) & 255u) return DDQ_ERR_ALIGNMENT;
+    planes = reinterpret_cast<uint8_t*>(ws);
+    xscale = reinterpret_cast<float*>(planes + ((p.plane_bytes + 255) & ~(size_t)255));
+  }
   // 1) split the activations into three e4m3 planes (PDL: waits for the
   //    producer of x, lets the GEMM launch early)
-  {
+  if (!ext_planes) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)M);
     cfg.blockDim = dim3(256);

@@ -131,6 +131,7 @@ class Engine:
         hd = cfg.head_dim
         inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, hd, 2, dtype=torch.float32) / hd))
         self._inv_freq = inv.to(self.device)
+        self._split_bufs: dict = {}   # (tokens, hidden) -> reusable split-activation buffers
         self._rope_cache = {}
         self._graphs = {}
 
@@ -248,15 +249,20 @@ class Engine:
         return (g * torch.sigmoid(g) * u).half()
 
     # ------------------------------------------------------------------ layers
-    def _layer(self, li: int, x: torch.Tensor, cache: KVCache, b0: int, cos, sin,
-               pos: Optional[torch.Tensor], start: int) -> torch.Tensor:
+    def _layer(self, li: int, x: torch.Tensor, delta: Optional[torch.Tensor], cache: KVCache,
+               b0: int, cos, sin, pos: Optional[torch.Tensor], start: int):
+        """One decoder layer.  The previous layer's MLP output `delta` is added to
+        the residual stream `x` inside this layer's first RMSNorm; returns the
+        new stream and this layer's MLP output, still to be added."""
         cfg = self.cfg
         L = self.layers[li]
         B, S, H = x.shape
         hd, nh, nkv = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads
-        _, h = self.add_rmsnorm(x, L["in_norm"])
-        qkv = self.linear(h, L["qkv"])
         scale = hd ** -0.5
+        if pos is not None and S == 1 and self.linear_kind == "fp8" and B <= 64:
+            return self._decode_layer(li, x, delta, cache, b0, cos, sin, pos)
+        x, h = self.add_rmsnorm(x, L["in_norm"], delta)
+        qkv = self.linear(h, L["qkv"])
         if pos is not None and S == 1 and self.linear_kind == "fp8":
             # one decode step: RoPE, the cache write and the attention in one kernel
             o = attention.decode_attention(qkv.reshape(B, -1), cache.k[li, b0:b0 + B],
@@ -284,14 +290,38 @@ class Engine:
         o = o.transpose(1, 2).reshape(B, S, nh * hd)
         return self._mlp_block(x, self.linear(o, L["o"]), L)
 
-    def _mlp_block(self, x: torch.Tensor, attn: torch.Tensor, L: dict) -> torch.Tensor:
-        """+attention residual -> RMSNorm -> gate/up -> SwiGLU -> down -> +residual."""
+    def _decode_layer(self, li: int, x: torch.Tensor, delta: Optional[torch.Tensor],
+                      cache: KVCache, b0: int, cos, sin, pos: torch.Tensor):
+        """A decode-step layer (B <= 64 tokens) with the fewest kernels: each RMSNorm
+        also splits its output into the operand form of the GEMM that follows
+        (no split pre-pass there), then RoPE + cache write + attention in one
+        kernel, and gate/up with the SwiGLU epilogue."""
+        cfg = self.cfg
+        L = self.layers[li]
+        B, S, H = x.shape
+        hd, nh, nkv = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads
+        eps = cfg.rms_norm_eps
+        bufs = self._split_bufs.setdefault((B, H), [None, None])
+        x, bufs[0] = norm.add_rmsnorm_split(x.contiguous(), L["in_norm"], eps, delta, bufs[0])
+        p = L["qkv"]
+        qkv = gemm_fp8.f8_forward_planes(bufs[0], p.wq, p.scales, p.bias)
+        o = attention.decode_attention(qkv, cache.k[li, b0:b0 + B], cache.v[li, b0:b0 + B],
+                                       cos, sin, pos, nh, nkv, hd, hd ** -0.5)
+        attn = self.linear(o.reshape(B, S, nh * hd), L["o"])
+        x, bufs[1] = norm.add_rmsnorm_split(x, L["post_norm"], eps, attn.contiguous(), bufs[1])
+        wq, sc, b = L["gate_up"].gate_up_interleaved()
+        z = gemm_fp8.f8_forward_planes(bufs[1], wq, sc, b, swiglu=True)
+        return x, self.linear(z.reshape(B, S, -1), L["down"])
+
+    def _mlp_block(self, x: torch.Tensor, attn: torch.Tensor, L: dict):
+        """+attention residual -> RMSNorm -> gate/up -> SwiGLU -> down; returns the
+        stream and the down projection (the residual add happens in the next norm)."""
         x, h = self.add_rmsnorm(x, L["post_norm"], attn)
         if self.linear_kind == "fp8":   # gate/up GEMM with the SwiGLU epilogue
             z = gemm_fp8.f8_forward_swiglu(h, *L["gate_up"].gate_up_interleaved())
         else:
             z = self.swiglu(self.linear(h, L["gate_up"]), self.cfg.intermediate_size)
-        return x + self.linear(z, L["down"])
+        return x, self.linear(z, L["down"])
 
     def hidden(self, ids: torch.Tensor, cache: KVCache, b0: int = 0, start: int = 0,
                pos: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -301,9 +331,10 @@ class Engine:
             cos, sin = self.rope_tables(torch.arange(start, start + ids.shape[1], device=ids.device))
         else:
             cos, sin = self.rope_tables(pos)
+        delta = None
         for li in range(self.cfg.num_hidden_layers):
-            x = self._layer(li, x, cache, b0, cos, sin, pos, start)
-        return self.add_rmsnorm(x, self.final_norm)[1]
+            x, delta = self._layer(li, x, delta, cache, b0, cos, sin, pos, start)
+        return self.add_rmsnorm(x, self.final_norm, delta)[1]
 
     def greedy(self, h: torch.Tensor) -> torch.Tensor:
         """Greedy token of each row of h [M, H] (fused lm_head argmax, or the oracle)."""

@@ -161,6 +161,29 @@ def f8_forward_swiglu(x: torch.Tensor, wq_il: torch.Tensor, scales_il: torch.Ten
     return z.reshape(*x.shape[:-1], inter)
 
 
+def f8_forward_planes(act, wq: torch.Tensor, scales: torch.Tensor,
+                      bias: Optional[torch.Tensor] = None, swiglu: bool = False) -> torch.Tensor:
+    """The decode GEMM (M <= 64) on activations split by ``norm.add_rmsnorm_split``
+    (``act``): y [M, N] (or, with ``swiglu`` and an interleaved gate/up weight,
+    z [M, N/2]) - the same values f8_forward / f8_forward_swiglu give on h."""
+    N, K = wq.shape
+    _check(act.H == K, "gemm_fp8: inner dim mismatch")
+    M = act.M
+    y = torch.empty((M, N // 2 if swiglu else N), dtype=torch.float16, device=wq.device)
+    bptr, bcode = None, _lib.DTYPE_NONE
+    if bias is not None and bias.numel() > 0:
+        bias = bias.contiguous()
+        bptr = bias.data_ptr()
+        bcode = _lib.DTYPE_F16 if bias.dtype == torch.float16 else _lib.DTYPE_F32
+    with torch.cuda.device(wq.device):
+        st = _lib.load().ddq_w8a16_gemm_planes(act.planes.data_ptr(), act.xscale.data_ptr(),
+                                               wq.data_ptr(), scales.data_ptr(), bptr, bcode,
+                                               y.data_ptr(), M, N, K, 1 if swiglu else 0,
+                                               _stream_ptr(wq.device))
+    _lib.check(st, "gemm_fp8.f8_forward_planes")
+    return y
+
+
 def forward(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Drop-in for gemm_d.forward: quantize w (every call, as the reference does), then GEMM."""
     wq, scales = quantize(w)

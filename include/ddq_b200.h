@@ -166,6 +166,31 @@ int ddq_add_rmsnorm(const void* x, const void* delta, const float* w, float eps,
                     void* x_out, void* h, int64_t M, int64_t H, void* stream);
 
 /*
+ * Residual add + RMSNorm as ddq_add_rmsnorm, followed by the split of h that
+ * the decode GEMM takes as its operand (what ddq_w8a16_gemm's pre-pass does
+ * with x): per row a power-of-two scale 2^e with max |h * 2^e| in [128, 256),
+ * and h * 2^e = p1 + p2 + p3 in three e4m3 planes.
+ *   planes  e4m3 [3][M][H] (16-byte aligned), xscale fp32 [M] = 2^-e
+ *   h       fp16 [M, H], optional (NULL: not stored)
+ * H % 16 == 0 and H <= 2048.  Replaces, on the decode path, the RMSNorm
+ * before a projection (RMSnorm_d.cu:23-87) and the projection's own split.
+ */
+int ddq_add_rmsnorm_split(const void* x, const void* delta, const float* w, float eps,
+                          void* x_out, void* h, uint8_t* planes, float* xscale,
+                          int64_t M, int64_t H, void* stream);
+
+/*
+ * The decode-shape GEMM (M <= 64) on activations already split by
+ * ddq_add_rmsnorm_split: same result as ddq_w8a16_gemm on the h they came
+ * from (or, with swiglu != 0, as ddq_w8a16_gemm_swiglu with N = 2I rows and
+ * y = z [M, N/2]).  Replaces: gemm_FP8_d.cu:171-210 for a projection whose
+ * input is produced by an RMSNorm.  No workspace.
+ */
+int ddq_w8a16_gemm_planes(const uint8_t* planes, const float* xscale, const uint8_t* wq,
+                          const float* scales, const void* bias, int bias_dtype, void* y,
+                          int64_t M, int64_t N, int64_t K, int swiglu, void* stream);
+
+/*
  * Greedy argmax over fp16 logits [B, V] -> int64 [B]; ties go to the
  * lowest index.  Replaces: sampler_d.cu:10-70 (argmax_kernel + forward).
  */

@@ -39,3 +39,36 @@ def test_add_rmsnorm_in_place(cuda_device):
     s, h = norm.add_rmsnorm(x, w, 1e-6, d, inplace=True)
     assert s.data_ptr() == x.data_ptr() and torch.equal(x, s_ref)
     assert (h.float() - h_ref.float()).abs().max().item() <= 2e-3
+
+
+@pytest.mark.parametrize("M", [1, 7, 16, 64])
+@pytest.mark.parametrize("with_delta", [False, True])
+def test_norm_split_feeds_the_decode_gemm_exactly(cuda_device, M, with_delta):
+    """RMSNorm + split, then the GEMM on the planes, gives bit for bit what the
+    RMSNorm's fp16 output gives through the ordinary GEMM (whose pre-pass
+    splits it the same way); the same for the SwiGLU epilogue."""
+    import numpy as np
+    from ddq_b200 import gemm_fp8, norm
+    from oracle import w8a16 as o
+    H, N, I = 896, 1152, 512
+    g = torch.Generator(device="cuda").manual_seed(M)
+    x = (torch.randn(1, M, H, generator=g, device="cuda") * 2).half()
+    d = (torch.randn(1, M, H, generator=g, device="cuda") * 2).half() if with_delta else None
+    w = torch.rand(H, generator=g, device="cuda") + 0.5
+    wq, s = gemm_fp8.quantize(torch.randn(N, H, generator=g, device="cuda") * 0.02)
+    b = torch.randn(N, generator=g, device="cuda") * 0.02
+    s_ref, h = norm.add_rmsnorm(x.clone(), w, 1e-6, d)
+    s_new, act = norm.add_rmsnorm_split(x.clone(), w, 1e-6, d)
+    assert torch.equal(s_new, s_ref)
+    y_ref = gemm_fp8.f8_forward(h.reshape(M, H), wq, s, b)
+    y = gemm_fp8.f8_forward_planes(act, wq, s, b)
+    assert torch.equal(y, y_ref)
+    wgu, sgu = gemm_fp8.quantize(torch.randn(2 * I, H, generator=g, device="cuda") * 0.05)
+    wil, sil, _ = gemm_fp8.interleave_gate_up(wgu, sgu)
+    z_ref = gemm_fp8.f8_forward_swiglu(h.reshape(M, H), wil, sil)
+    z = gemm_fp8.f8_forward_planes(act, wil, sil, swiglu=True)
+    assert torch.equal(z, z_ref)
+    # and the oracle agrees with both
+    ref = o.f8_forward(h.reshape(M, H).cpu().numpy(), wq.cpu().numpy(), s.cpu().numpy(),
+                       b.cpu().numpy())
+    assert o.normwise_rel_err(y.cpu().numpy(), ref) <= 3e-3
