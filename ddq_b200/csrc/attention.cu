@@ -3,23 +3,24 @@
 // kernel, the cache copy and the attention call of a decode step:
 // RoPe_d.cu:12-68, engine.py:126-130 and 225-251).
 //
-// For each sequence b and key/value head g (one CTA, 256 threads):
+// For each sequence b and key/value head g (one CTA):
 //   q_h  = fp16(rope(q_h, pos))   for the G query heads h of group g
 //   k    = fp16(rope(k_g, pos)),  v = v_g        -> cache[b, g, pos, :]
 //   o_h  = softmax_j( q_h . K[b, g, j, :] * scale ) V[b, g, j, :],  j = 0..pos
 // Rotate-half RoPE in fp32 with the caller's cos/sin row for this position,
-// rounded to fp16 as the unfused path rounds it; scores, softmax and the
-// weighted sum in fp32; o rounded to fp16.  The position is read on the
-// device, so a captured CUDA graph replays it for every step.
+// rounded to fp16 as the unfused path rounds it; scores and softmax in fp32;
+// o rounded to fp16.  The position is read on the device, so a captured CUDA
+// graph replays it for every step.
 //
-// Work split: the warps (16 for 64-wide heads) take 32-position tiles in
-// turn (lane = position for the scores, lane = D / 32 head dimensions for the
-// weighted sum of V) with an online softmax per query head; the CTA merges
-// the warps' partial results in shared memory.  Every K row and every group
-// of 16 V rows is requested before it is used, so a warp waits on memory once
-// per step instead of once per row.  K rows are read once per CTA, by one lane each (128
-// contiguous bytes); V rows once, coalesced across the warp.  The step reads
-// the cache at HBM rate; the arithmetic runs on the CUDA cores.
+// Two kernels:
+//   decode_attention_mma_kernel<G>  64-wide heads (the Qwen2 shapes): K and V
+//       chunks stream into shared memory through TMA, q K^T and P V run on
+//       the tensor cores (mma.sync, fp16 operands, fp32 accumulation).
+//   decode_attention_kernel<128>    128-wide heads: per-lane loads, the
+//       arithmetic on the CUDA cores (lane = position for the scores, lane =
+//       D / 32 head dimensions for the weighted sum).
+// Both split the positions between the warps with an online softmax per query
+// head and merge the warps' partial results in shared memory.
 #include <cudaTypedefs.h>
 
 #include <cfloat>
@@ -236,59 +237,132 @@ __global__ void __launch_bounds__(at_warps(D) * 32, 1) decode_attention_kernel(c
 }
 
 // ----------------------------------------------------------------------------
-// 64-wide heads: the K and V rows stream into shared memory through TMA.
+// 64-wide heads: K and V stream into shared memory through TMA; both products
+// run on the tensor cores.
 // ----------------------------------------------------------------------------
-// Per-lane global loads left the kernel waiting on memory (one latency per
-// row group, a few warps per SM).  Here the positions are cut into 32-row
-// chunks (4 KB of K + 4 KB of V); warp w owns ring slot w and the chunks
-// w, w + 16, ...; each warp's lane 0 issues the TMA copies of its next chunk
-// as soon as it has finished with the slot, so up to 16 chunks per CTA are in
-// flight.  The copies use the 128-byte swizzle, which keeps both access
-// patterns free of bank conflicts: lane = position reads its K row, lane =
-// two head dimensions reads a V row.
-constexpr int AT2_NW = 16;        // warps = ring slots
-constexpr int AT2_ROWS = 32;      // positions per chunk
-constexpr int AT2_CHUNK = AT2_ROWS * 64 * 2;  // bytes of K (and of V) per chunk
+// The positions are cut into 32-row chunks (4 KB of K + 4 KB of V, 128-byte
+// swizzle, which keeps every 8x8 matrix load below free of bank conflicts).
+// Warp w takes chunks w, w + 8, w + 16, ... through a ring of AM_DEPTH slots
+// of its own, so up to 8 x AM_DEPTH chunks (768 positions) of a sequence are
+// in flight at once, and refills a slot as soon as it has used it.  Before
+// the grid dependency resolves, the CTA asks L2 for rows 0..pos of its K and
+// V (a prefetch only: what the kernel uses is read after the wait).
+//
+// Per chunk and warp (mma.sync m16n8k16, fp16 operands, fp32 accumulation),
+// with the G <= 8 query heads on MMA rows 0..7:
+//   S[h, j]  = q_h . K[j]            16 MMAs (4 tiles of 8 positions x 4 K steps)
+//   online softmax of S * scale per head, fp32, in registers (quad shuffles)
+//   O[h, :] += P[h, :] V             16 MMAs (8 tiles of 8 dims x 2 K steps)
+// q (the RoPE output, rounded to fp16 as the unfused path rounds it), K and
+// V are fp16, so every product is exact.  Each weight p is carried as
+// p_hi = fp16(p) on MMA row h and p_lo = fp16(p - p_hi) on row h + 8 of the
+// same fragment: about 22 bits of p reach the weighted sum at no extra MMA
+// (O = rows 0..7 + rows 8..15).  Rows past the last position are masked in S
+// and zeroed in the V tile before use (the cache there may hold anything,
+// and 0 x NaN is NaN).
+constexpr int AM_NW = 8;          // warps
+constexpr int AM_DEPTH = 3;       // ring slots per warp
+constexpr int AM_ROWS = 32;       // positions per chunk
+constexpr int AM_CHUNK = AM_ROWS * 64 * 2;  // bytes of K (and of V) per chunk
 
-struct At2Smem {
-  uint8_t ring[AT2_NW][2][AT2_CHUNK];          // [slot][K | V]
-  float q[AT_GMAX][64];
-  float acc[AT2_NW][AT_GMAX][64];
-  float m[AT2_NW][AT_GMAX], l[AT2_NW][AT_GMAX];
-  float p[AT2_NW][AT_GMAX][AT2_ROWS];           // per warp: this chunk's weights
-  unsigned long long full[AT2_NW];
+struct AmSmem {
+  uint8_t ring[AM_NW * AM_DEPTH][2][AM_CHUNK];  // [slot][K | V]
+  float acc[AM_NW][AT_GMAX][64];
+  __half q[AT_GMAX][64];
+  float m[AM_NW][AT_GMAX], l[AM_NW][AT_GMAX];
+  unsigned long long full[AM_NW * AM_DEPTH];
   int abort_flag;
 };
 
 // byte offset of 16-byte chunk j of row r in a 128-byte-swizzled tile
 __device__ __forceinline__ uint32_t at2_swz(int r, int j) { return r * 128 + ((j ^ (r & 7)) << 4); }
 
+__device__ __forceinline__ void am_ldsm(uint32_t addr, uint32_t* r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
+}
+
+__device__ __forceinline__ void am_ldsm_t(uint32_t addr, uint32_t* r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
+}
+
+// d += A (16 x 16, row-major fragment a0..a3) * B (16 x 8, column fragment b0, b1)
+__device__ __forceinline__ void am_mma(float* d, uint32_t a0, uint32_t a1, uint32_t a2,
+                                       uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, "
+      "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t am_h2(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
 template <int G>
-__global__ void __launch_bounds__(AT2_NW * 32, 1)
-    decode_attention_tma_kernel(const __grid_constant__ CUtensorMap tm_k,
+__global__ void __launch_bounds__(AM_NW * 32, 1)
+    decode_attention_mma_kernel(const __grid_constant__ CUtensorMap tm_k,
                                 const __grid_constant__ CUtensorMap tm_v, const AtArgs a,
                                 unsigned long long timeout_ns) {
   constexpr int D = 64, DH = 32;
-  extern __shared__ uint8_t at2_raw[];
-  At2Smem& sm = *reinterpret_cast<At2Smem*>((reinterpret_cast<uintptr_t>(at2_raw) + 1023) &
-                                            ~static_cast<uintptr_t>(1023));
+  static_assert(G >= 1 && G <= 8, "query heads per group");
+  extern __shared__ uint8_t am_raw[];
+  AmSmem& sm = *reinterpret_cast<AmSmem*>((reinterpret_cast<uintptr_t>(am_raw) + 1023) &
+                                          ~static_cast<uintptr_t>(1023));
   const int b = blockIdx.x / a.Hkv, g = blockIdx.x % a.Hkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gid = lane >> 2, tig = lane & 3;
+  __half* kc = a.kc + (size_t)b * a.cache_bstride + (size_t)g * a.cap * D;
+  __half* vc = a.vc + (size_t)b * a.cache_bstride + (size_t)g * a.cap * D;
   if (threadIdx.x == 0) {
-    for (int w = 0; w < AT2_NW; ++w) ptx::mbar_init(ptx::smem_u32(&sm.full[w]), 1);
+    for (int s = 0; s < AM_NW * AM_DEPTH; ++s) ptx::mbar_init(ptx::smem_u32(&sm.full[s]), 1);
     sm.abort_flag = 0;
     ptx::fence_mbar_init();
     ptx::prefetch_tmap(&tm_k);
     ptx::prefetch_tmap(&tm_v);
+  } else if (threadIdx.x == 32) {
+    // L2 prefetch of rows 0..pos while the previous kernel finishes; the
+    // position read here may be stale, which only makes the hint less useful
+    const int64_t ph = *a.pos;
+    if (ph >= 0 && ph < a.cap) {
+      const uint32_t bytes = (uint32_t)(ph + 1) * (uint32_t)(D * 2);
+      for (uint32_t off = 0; off < bytes; off += 32768u) {
+        const uint32_t n = bytes - off < 32768u ? bytes - off : 32768u;
+        ptx::bulk_prefetch_l2(reinterpret_cast<const uint8_t*>(kc) + off, n);
+        ptx::bulk_prefetch_l2(reinterpret_cast<const uint8_t*>(vc) + off, n);
+      }
+    }
   }
-  ptx::pdl_wait();  // qkv comes from the previous kernel
+  ptx::pdl_wait();  // qkv comes from the previous kernel; earlier cache rows are complete
   const int64_t p = *a.pos;
   if (p < 0 || p >= a.cap) return;  // the host checks the range; nothing to do otherwise
   const int L = (int)p + 1;
-  const int nchunks = (L + AT2_ROWS - 1) / AT2_ROWS;
+  const int nchunks = (L + AM_ROWS - 1) / AM_ROWS;
+  const int last = nchunks - 1;  // the chunk that holds the new row
   const __half* row = a.qkv + (size_t)b * a.qkv_stride;
-  __half* kc = a.kc + (size_t)b * a.cache_bstride + (size_t)g * a.cap * D;
-  __half* vc = a.vc + (size_t)b * a.cache_bstride + (size_t)g * a.cap * D;
+  const uint32_t ring0 = ptx::smem_u32(&sm.ring[0][0][0]);
+  __syncthreads();  // barriers initialised
+
+  auto issue = [&](int c) {  // chunk c into its slot of this warp's ring
+    const int s = warp * AM_DEPTH + (c / AM_NW) % AM_DEPTH;
+    const uint32_t full = ptx::smem_u32(&sm.full[s]);
+    const uint32_t dst = ring0 + (uint32_t)(s * 2 * AM_CHUNK);
+    ptx::mbar_arrive_expect_tx(full, 2u * AM_CHUNK);
+    ptx::tma_load_4d(dst, &tm_k, 0, c * AM_ROWS, g, b, full);
+    ptx::tma_load_4d(dst + AM_CHUNK, &tm_v, 0, c * AM_ROWS, g, b, full);
+  };
+  // chunks without the new row can be requested before it is written
+  if (lane == 0)
+    for (int i = 0; i < AM_DEPTH; ++i) {
+      const int c = warp + i * AM_NW;
+      if (c < last) issue(c);
+    }
 
   // ---- rotary embedding of the G query heads and the new key; cache write
   for (int i = threadIdx.x; i < (G + 1) * DH; i += blockDim.x) {
@@ -296,158 +370,155 @@ __global__ void __launch_bounds__(AT2_NW * 32, 1)
     const __half* src = h < G ? row + (size_t)(g * G + h) * D : row + (size_t)(a.Hq + g) * D;
     const float x1 = __half2float(src[d]), x2 = __half2float(src[d + DH]);
     // x * cos + rotate_half(x) * sin, each product rounded as torch rounds it
-    const float y1 = __half2float(
-        __float2half_rn(__fadd_rn(__fmul_rn(x1, a.cos[d]), __fmul_rn(-x2, a.sin[d]))));
-    const float y2 = __half2float(
-        __float2half_rn(__fadd_rn(__fmul_rn(x2, a.cos[d + DH]), __fmul_rn(x1, a.sin[d + DH]))));
+    const __half y1 =
+        __float2half_rn(__fadd_rn(__fmul_rn(x1, a.cos[d]), __fmul_rn(-x2, a.sin[d])));
+    const __half y2 =
+        __float2half_rn(__fadd_rn(__fmul_rn(x2, a.cos[d + DH]), __fmul_rn(x1, a.sin[d + DH])));
     if (h < G) {
       sm.q[h][d] = y1;
       sm.q[h][d + DH] = y2;
     } else {
-      kc[(size_t)p * D + d] = __float2half_rn(y1);
-      kc[(size_t)p * D + d + DH] = __float2half_rn(y2);
+      kc[(size_t)p * D + d] = y1;
+      kc[(size_t)p * D + d + DH] = y2;
     }
   }
+  for (int i = threadIdx.x; i < (AT_GMAX - G) * D; i += blockDim.x)
+    sm.q[G + i / D][i % D] = __float2half_rn(0.f);
   for (int d = threadIdx.x; d < D; d += blockDim.x)
     vc[(size_t)p * D + d] = row[(size_t)(a.Hq + a.Hkv + g) * D + d];
   ptx::fence_proxy_async_global();  // the new cache row is read back through TMA
   __syncthreads();
   if (threadIdx.x == 0) ptx::pdl_launch_dependents();
+  if (lane == 0 && last % AM_NW == warp && last < AM_NW * AM_DEPTH) issue(last);
 
-  const uint32_t full = ptx::smem_u32(&sm.full[warp]);
-  const uint32_t kdst = ptx::smem_u32(&sm.ring[warp][0][0]);
-  const uint32_t vdst = ptx::smem_u32(&sm.ring[warp][1][0]);
-  auto issue = [&](int c) {
-    ptx::mbar_arrive_expect_tx(full, 2u * AT2_CHUNK);
-    ptx::tma_load_4d(kdst, &tm_k, 0, c * AT2_ROWS, g, b, full);
-    ptx::tma_load_4d(vdst, &tm_v, 0, c * AT2_ROWS, g, b, full);
-  };
-  if (lane == 0 && warp < nchunks) issue(warp);
-
-  float m[G], l[G], acc[G][2];
+  // q fragments (rows 0..7 = heads; rows 8..15 of the A operand are zero)
+  uint32_t qa[4][2];
 #pragma unroll
-  for (int h = 0; h < G; ++h) {
-    m[h] = -FLT_MAX;
-    l[h] = 0.f;
-    acc[h][0] = acc[h][1] = 0.f;
+  for (int kk = 0; kk < 4; ++kk) {
+    qa[kk][0] = *reinterpret_cast<const uint32_t*>(&sm.q[gid][16 * kk + 2 * tig]);
+    qa[kk][1] = *reinterpret_cast<const uint32_t*>(&sm.q[gid][16 * kk + 8 + 2 * tig]);
   }
-  float* pw = &sm.p[warp][0][0];
-  int phase = 0, pending = warp < nchunks ? 1 : 0;
-  for (int c = warp; c < nchunks; c += AT2_NW, phase ^= 1) {
-    if (!ptx::mbar_wait(full, (uint32_t)phase, timeout_ns, &sm.abort_flag)) break;
-    pending = 0;
-    const uint8_t* ks = &sm.ring[warp][0][0];
-    const uint8_t* vs = &sm.ring[warp][1][0];
-    const int t0 = c * AT2_ROWS;
-    const bool ok = t0 + lane < L;
-    // scores: lane = position, its K row from the swizzled tile
-    float s[G];
+  float m_r = -FLT_MAX, l_r = 0.f;  // running max and sum of head gid
+  float o[8][4];                    // O tiles: rows gid (p_hi part), gid + 8 (p_lo part)
 #pragma unroll
-    for (int h = 0; h < G; ++h) s[h] = 0.f;
+  for (int nd = 0; nd < 8; ++nd) o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.f;
+
+  int it = 0;
+  for (int c = warp; c < nchunks; c += AM_NW, ++it) {
+    const int s = warp * AM_DEPTH + it % AM_DEPTH;
+    if (!ptx::mbar_wait(ptx::smem_u32(&sm.full[s]), (uint32_t)((it / AM_DEPTH) & 1), timeout_ns,
+                        &sm.abort_flag))
+      break;
+    const uint32_t ks = ring0 + (uint32_t)(s * 2 * AM_CHUNK), vs = ks + AM_CHUNK;
+    const int jn = min(AM_ROWS, L - c * AM_ROWS);  // positions of this chunk in use
+    if (jn < AM_ROWS) {
+      uint8_t* vrow = &sm.ring[s][1][0];
+      for (int idx = lane; idx < (AM_ROWS - jn) * 8; idx += 32)
+        *reinterpret_cast<uint4*>(vrow + (jn + idx / 8) * 128 + (idx % 8) * 16) =
+            make_uint4(0u, 0u, 0u, 0u);
+      __syncwarp();
+    }
+    // S = Q K^T: tile nt holds positions 8 nt + 2 tig (+1) of head gid
+    float sc[4][4];
 #pragma unroll
-    for (int cc = 0; cc < D / 8; ++cc) {
-      const uint4 u = *reinterpret_cast<const uint4*>(ks + at2_swz(lane, cc));
-      const __half2* hv = reinterpret_cast<const __half2*>(&u);
-      float kf[8];
+    for (int nt = 0; nt < 4; ++nt) {
+      sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const float2 f = __half22float2(hv[t]);
-        kf[2 * t] = f.x;
-        kf[2 * t + 1] = f.y;
-      }
-#pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const float4 qa = *reinterpret_cast<const float4*>(&sm.q[h][cc * 8]);
-        const float4 qb = *reinterpret_cast<const float4*>(&sm.q[h][cc * 8 + 4]);
-        float v = s[h];
-        v = fmaf(qa.x, kf[0], v);
-        v = fmaf(qa.y, kf[1], v);
-        v = fmaf(qa.z, kf[2], v);
-        v = fmaf(qa.w, kf[3], v);
-        v = fmaf(qb.x, kf[4], v);
-        v = fmaf(qb.y, kf[5], v);
-        v = fmaf(qb.z, kf[6], v);
-        v = fmaf(qb.w, kf[7], v);
-        s[h] = v;
+      for (int kh = 0; kh < 2; ++kh) {
+        uint32_t r[4];
+        am_ldsm(ks + at2_swz(8 * nt + (lane & 7), 4 * kh + (lane >> 3)), r);
+        am_mma(sc[nt], qa[2 * kh][0], 0u, qa[2 * kh][1], 0u, r[0], r[1]);
+        am_mma(sc[nt], qa[2 * kh + 1][0], 0u, qa[2 * kh + 1][1], 0u, r[2], r[3]);
       }
     }
-    // online softmax per query head; this chunk's weights go to shared memory
+    // online softmax of head gid over the chunk (the quad of lanes shares the row)
+    float sv[4][2];
+    float mx = -FLT_MAX;
 #pragma unroll
-    for (int h = 0; h < G; ++h) {
-      const float sv = ok ? s[h] * a.scale : -FLT_MAX;
-      float tm = sv;
+    for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, o));
-      const float mn = fmaxf(m[h], tm);
-      const float corr = __expf(m[h] - mn);
-      const float pv = ok ? __expf(sv - mn) : 0.f;
-      pw[h * AT2_ROWS + lane] = pv;
-      float ps = pv;
+      for (int e = 0; e < 2; ++e) {
+        sv[nt][e] = 8 * nt + 2 * tig + e < jn ? sc[nt][e] * a.scale : -FLT_MAX;
+        mx = fmaxf(mx, sv[nt][e]);
+      }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float mn = fmaxf(m_r, mx);
+    const float corr = __expf(m_r - mn);
+    float ps = 0.f;
+    uint32_t phi[4], plo[4];
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
-      l[h] = l[h] * corr + ps;
-      m[h] = mn;
-      acc[h][0] *= corr;
-      acc[h][1] *= corr;
+    for (int nt = 0; nt < 4; ++nt) {
+      const float p0 = 8 * nt + 2 * tig < jn ? __expf(sv[nt][0] - mn) : 0.f;
+      const float p1 = 8 * nt + 2 * tig + 1 < jn ? __expf(sv[nt][1] - mn) : 0.f;
+      ps += p0 + p1;
+      const __half2 hi = __floats2half2_rn(p0, p1);
+      const float2 hf = __half22float2(hi);
+      phi[nt] = *reinterpret_cast<const uint32_t*>(&hi);
+      plo[nt] = am_h2(p0 - hf.x, p1 - hf.y);  // exact difference, then rounded
     }
-    __syncwarp();
-    // weighted sum: lane = head dimensions 2 lane, 2 lane + 1 of each V row;
-    // rows past the last position are skipped (the cache there is not ours)
-    const int jn = min(AT2_ROWS, L - t0);
-    const uint32_t voff = (uint32_t)(lane >> 2), vsub = (uint32_t)(lane & 3) * 4;
+    ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+    l_r = l_r * corr + ps;
+    m_r = mn;
 #pragma unroll
-    for (int j4 = 0; j4 < AT2_ROWS; j4 += 4) {
-      if (j4 >= jn) break;
-      float2 vf[4];
+    for (int nd = 0; nd < 8; ++nd) {
+      o[nd][0] *= corr;
+      o[nd][1] *= corr;
+      o[nd][2] *= corr;
+      o[nd][3] *= corr;
+    }
+    // O += P V: K step k2 covers positions 16 k2 .. 16 k2 + 15
 #pragma unroll
-      for (int t = 0; t < 4; ++t)
-        vf[t] = j4 + t < jn ? __half22float2(*reinterpret_cast<const __half2*>(
-                                  vs + at2_swz(j4 + t, (int)voff) + vsub))
-                            : make_float2(0.f, 0.f);
+    for (int k2 = 0; k2 < 2; ++k2) {
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const float4 p4 = *reinterpret_cast<const float4*>(pw + h * AT2_ROWS + j4);
-        const float pp[4] = {p4.x, p4.y, p4.z, p4.w};
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          acc[h][0] = fmaf(pp[t], vf[t].x, acc[h][0]);
-          acc[h][1] = fmaf(pp[t], vf[t].y, acc[h][1]);
-        }
+      for (int np = 0; np < 4; ++np) {
+        const int mi = lane >> 3;
+        uint32_t r[4];
+        am_ldsm_t(vs + at2_swz(16 * k2 + (mi & 1) * 8 + (lane & 7), 2 * np + (mi >> 1)), r);
+        am_mma(o[2 * np], phi[2 * k2], plo[2 * k2], phi[2 * k2 + 1], plo[2 * k2 + 1], r[0], r[1]);
+        am_mma(o[2 * np + 1], phi[2 * k2], plo[2 * k2], phi[2 * k2 + 1], plo[2 * k2 + 1], r[2],
+               r[3]);
       }
     }
-    // the slot and the weights are free: fetch this warp's next chunk
+    // the slot is free: fetch this warp's chunk AM_DEPTH steps ahead into it
     __syncwarp();
     ptx::fence_proxy_async_smem();
-    if (c + AT2_NW < nchunks) {
-      if (lane == 0) issue(c + AT2_NW);
-      pending = 1;
-    }
+    const int cn = c + AM_NW * AM_DEPTH;
+    if (cn < nchunks && lane == 0) issue(cn);
   }
-  // after a timeout, wait (bounded) for a copy still landing in this slot
-  if (pending && lane == 0) {
-    const long long t0 = clock64();
-    while (!ptx::mbar_try_wait(full, (uint32_t)phase)) {
-      if (clock64() - t0 > (long long)(timeout_ns * 2ull)) break;
+  // after a timeout, wait (bounded) for copies still landing in this warp's slots
+  if (lane == 0 && sm.abort_flag) {
+    for (int k = 0; k < AM_DEPTH; ++k) {
+      const int j = it + k;
+      if (warp + j * AM_NW >= nchunks) break;
+      const uint32_t full = ptx::smem_u32(&sm.full[warp * AM_DEPTH + j % AM_DEPTH]);
+      const long long t0 = clock64();
+      while (!ptx::mbar_try_wait(full, (uint32_t)((j / AM_DEPTH) & 1))) {
+        if (clock64() - t0 > (long long)(timeout_ns * 2ull)) break;
+      }
     }
   }
 
   // ---- merge the warps' partial softmax sums
+  if (gid < G) {
 #pragma unroll
-  for (int h = 0; h < G; ++h) {
-    if (lane == 0) {
-      sm.m[warp][h] = m[h];
-      sm.l[warp][h] = l[h];
+    for (int nd = 0; nd < 8; ++nd) {
+      sm.acc[warp][gid][8 * nd + 2 * tig] = o[nd][0] + o[nd][2];
+      sm.acc[warp][gid][8 * nd + 2 * tig + 1] = o[nd][1] + o[nd][3];
     }
-    sm.acc[warp][h][2 * lane] = acc[h][0];
-    sm.acc[warp][h][2 * lane + 1] = acc[h][1];
+    if (tig == 0) {
+      sm.m[warp][gid] = m_r;
+      sm.l[warp][gid] = l_r;
+    }
   }
   __syncthreads();
   for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
     const int h = i / D, d = i % D;
     float mx = -FLT_MAX;
-    for (int w = 0; w < AT2_NW; ++w) mx = fmaxf(mx, sm.m[w][h]);
+    for (int w = 0; w < AM_NW; ++w) mx = fmaxf(mx, sm.m[w][h]);
     float den = 0.f, num = 0.f;
-    for (int w = 0; w < AT2_NW; ++w) {
+    for (int w = 0; w < AM_NW; ++w) {
       const float cw = sm.l[w][h] > 0.f ? __expf(sm.m[w][h] - mx) : 0.f;
       den = fmaf(sm.l[w][h], cw, den);
       num = fmaf(sm.acc[w][h][d], cw, num);
@@ -478,7 +549,7 @@ int at_cache_map(CUtensorMap* m, const void* base, int cap, int Hkv, int B, int6
   if (!enc) return DDQ_ERR_DEVICE;
   cuuint64_t dims[4] = {64, (cuuint64_t)cap, (cuuint64_t)Hkv, (cuuint64_t)B};
   cuuint64_t strides[3] = {128, (cuuint64_t)cap * 128, (cuuint64_t)bstride * 2};
-  cuuint32_t box[4] = {64, AT2_ROWS, 1, 1};
+  cuuint32_t box[4] = {64, AM_ROWS, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides,
                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -509,7 +580,7 @@ int launch_decode_attention(const __half* qkv, int64_t qkv_stride, __half* kc, _
   cfg.numAttrs = 1;
   cudaError_t e;
   if (D == 64) {
-    // TMA-streamed variant (the cache must be 16-byte aligned per batch)
+    // TMA-streamed tensor-core variant (the cache must be 16-byte aligned per batch)
     CUtensorMap tk, tv;
     int st = at_cache_map(&tk, kc, cap, Hkv, B, cache_bstride);
     if (st) return st;
@@ -518,20 +589,20 @@ int launch_decode_attention(const __half* qkv, int64_t qkv_stride, __half* kc, _
     const int dev = current_device();
     if (dev < 0 || dev >= 64) return DDQ_ERR_DEVICE;
     static bool attr_set[AT_GMAX][64] = {};
-    const int smem = (int)sizeof(At2Smem) + 1024;
-    cfg.blockDim = dim3(AT2_NW * 32);
+    const int smem = (int)sizeof(AmSmem) + 1024;
+    cfg.blockDim = dim3(AM_NW * 32);
     cfg.dynamicSmemBytes = smem;
     switch (Hq / Hkv) {
 #define DDQ_AT_G(G_)                                                                     \
   case G_:                                                                               \
     if (!attr_set[G_ - 1][dev]) {                                                        \
-      if (cudaFuncSetAttribute(decode_attention_tma_kernel<G_>,                          \
+      if (cudaFuncSetAttribute(decode_attention_mma_kernel<G_>,                          \
                                cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=     \
           cudaSuccess)                                                                   \
         return DDQ_ERR_LAUNCH;                                                           \
       attr_set[G_ - 1][dev] = true;                                                      \
     }                                                                                    \
-    e = cudaLaunchKernelEx(&cfg, decode_attention_tma_kernel<G_>, tk, tv, a, timeout_ns); \
+    e = cudaLaunchKernelEx(&cfg, decode_attention_mma_kernel<G_>, tk, tv, a, timeout_ns); \
     break;
       DDQ_AT_G(1) DDQ_AT_G(2) DDQ_AT_G(3) DDQ_AT_G(4)
       DDQ_AT_G(5) DDQ_AT_G(6) DDQ_AT_G(7) DDQ_AT_G(8)

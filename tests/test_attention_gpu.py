@@ -35,7 +35,9 @@ def reference(qkv, kc, vc, cos, sin, pos, nh, nkv, hd, scale):
 
 @pytest.mark.parametrize("B,nh,nkv,hd,cap,pos", [
     (1, 14, 2, 64, 64, 0), (3, 14, 2, 64, 100, 37), (64, 14, 2, 64, 768, 600),
-    (2, 8, 8, 64, 300, 299), (4, 16, 2, 128, 256, 130), (5, 4, 1, 64, 40, 31)])
+    (2, 8, 8, 64, 300, 299), (4, 16, 2, 128, 256, 130), (5, 4, 1, 64, 40, 31),
+    # more chunks than the 64-wide kernel keeps in flight (ring refills), G = 8 and G = 3
+    (2, 16, 2, 64, 1100, 1099), (3, 6, 2, 64, 2048, 1500), (2, 14, 2, 64, 800, 767)])
 def test_decode_attention_matches_reference(cuda_device, B, nh, nkv, hd, cap, pos):
     from ddq_b200 import attention
     g = torch.Generator(device="cuda").manual_seed(B * 1000 + pos)
@@ -86,3 +88,27 @@ def test_decode_attention_strided_batch_and_graph(cuda_device):
     exp = v.repeat_interleave(nh // nkv, dim=1).reshape(4, nh * hd)
     assert (o2.float() - exp.float()).abs().max().item() < 1e-2
     assert big_k[0].abs().sum().item() == 0 and big_k[1, :2].abs().sum().item() == 0
+
+
+def test_decode_attention_ignores_garbage_past_the_position(cuda_device):
+    """Cache rows after `pos` are not part of the step: NaN and Inf there must not
+    reach the output (a zero weight times NaN would)."""
+    from ddq_b200 import attention
+    B, nh, nkv, hd, cap, pos = 3, 14, 2, 64, 200, 70
+    g = torch.Generator(device="cuda").manual_seed(11)
+    qkv = torch.randn(B, (nh + 2 * nkv) * hd, generator=g, device="cuda").half()
+    kc = torch.randn(B, nkv, cap, hd, generator=g, device="cuda").half()
+    vc = torch.randn(B, nkv, cap, hd, generator=g, device="cuda").half()
+    kc[:, :, pos + 1:] = float("nan")
+    vc[:, :, pos + 1:] = float("inf")
+    vc[:, :, pos + 1::2] = float("nan")
+    cos = torch.ones(hd, device="cuda")
+    sin = torch.zeros(hd, device="cuda")
+    o_ref, _, _ = reference(qkv, kc, vc, cos, sin, pos, nh, nkv, hd, 0.125)
+    p = torch.tensor([pos], dtype=torch.int64, device="cuda")
+    o = attention.decode_attention(qkv, kc, vc, cos, sin, p, nh, nkv, hd, 0.125)
+    torch.cuda.synchronize()
+    assert torch.isfinite(o.float()).all()
+    err = ((o.float() - o_ref.float()).abs().amax(dim=1) /
+           o_ref.float().abs().amax(dim=1).clamp_min(1e-6)).max().item()
+    assert err < 2e-3, err
