@@ -108,7 +108,7 @@ __device__ __forceinline__ void record_device_error(int code) {
 // Phase trace (debug flag bit 1): %globaltimer stamps per CTA, read back with
 // ddq_read_trace().  kTraceSlots stamps for each of the first kTraceCtas CTAs.
 constexpr int kTraceCtas = 2048;
-constexpr int kTraceSlots = 8;
+constexpr int kTraceSlots = 16;
 extern __device__ unsigned long long g_trace[kTraceCtas * kTraceSlots];
 
 __device__ __forceinline__ void trace_stamp(bool on, int slot) {

@@ -50,6 +50,21 @@ __device__ __forceinline__ uint4 nm_scale8(const uint4& a, float r, const float*
   return out;
 }
 
+__device__ __forceinline__ uint4 nm_scale8w(const uint4& a, float r, const float4& w0,
+                                            const float4& w1) {
+  uint4 out;
+  const __half2* x = reinterpret_cast<const __half2*>(&a);
+  __half2* o = reinterpret_cast<__half2*>(&out);
+  const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(x[i]);
+    o[i] = __floats2half2_rn(__fmul_rn(__fmul_rn(f.x, r), wv[2 * i]),
+                             __fmul_rn(__fmul_rn(f.y, r), wv[2 * i + 1]));
+  }
+  return out;
+}
+
 constexpr int NM_REG_CHUNKS = 8;  // 16-byte chunks per lane kept in registers
 
 __global__ void __launch_bounds__(256) add_rmsnorm_kernel(const __half* x,
@@ -110,11 +125,22 @@ __global__ void __launch_bounds__(256) add_rmsnorm_split_kernel(
     const __half* x, const __half* __restrict__ delta, const float* __restrict__ w, float eps,
     __half* x_out, __half* __restrict__ h, uint8_t* __restrict__ planes,
     float* __restrict__ xscale, int M, int H) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  const int nch = H / 8;
+  // the norm weight is not produced by the previous kernel: load it while that
+  // kernel finishes
+  float4 wr[NM_REG_CHUNKS][2];
+#pragma unroll
+  for (int j = 0; j < NM_REG_CHUNKS; ++j) {
+    const int c = lane + 32 * j;
+    if (c < nch) {
+      wr[j][0] = __ldg(reinterpret_cast<const float4*>(w + 8 * c));
+      wr[j][1] = __ldg(reinterpret_cast<const float4*>(w + 8 * c) + 1);
+    }
+  }
   ptx::pdl_wait();
   ptx::pdl_launch_dependents();
-  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= M) return;
-  const int nch = H / 8;
   const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * H);
   const uint4* dr = delta ? reinterpret_cast<const uint4*>(delta + (size_t)row * H) : nullptr;
   uint4* xo = x_out ? reinterpret_cast<uint4*>(x_out + (size_t)row * H) : nullptr;
@@ -137,7 +163,7 @@ __global__ void __launch_bounds__(256) add_rmsnorm_split_kernel(
   for (int j = 0; j < NM_REG_CHUNKS; ++j) {
     const int c = lane + 32 * j;
     if (c < nch) {
-      v[j] = nm_scale8(v[j], r, w + 8 * c);
+      v[j] = nm_scale8w(v[j], r, wr[j][0], wr[j][1]);
       if (h) reinterpret_cast<uint4*>(h + (size_t)row * H)[c] = v[j];
       const __half2* hv = reinterpret_cast<const __half2*>(&v[j]);
 #pragma unroll

@@ -141,6 +141,22 @@ __global__ void __launch_bounds__(256) xsplit_kernel(const __half* __restrict__ 
 // ----------------------------------------------------------------------------
 // Decode GEMM
 // ----------------------------------------------------------------------------
+// Split-K ownership: rank r of a cluster of n owns the 4-token groups of
+// tokens [r tpo, (r + 1) tpo), tpo = ceil(M / n) rounded up to 4.
+__host__ __device__ constexpr int dc_tpo(int m, int n) { return ((m + n - 1) / n + 3) & ~3; }
+// bytes of one rank's own groups (128 rows x 16 B per group), worst case over n
+__host__ __device__ constexpr int dc_own_bytes_max(int bt) { return dc_tpo(bt, 2) * DC_BN * 4; }
+// bytes a rank receives: n - 1 senders x its groups, worst case over 2 <= n <= 8
+static_assert(kMaxSplits <= 8, "split-K bounds below assume at most 8 ranks");
+__host__ __device__ constexpr int dc_recv_bytes_max(int bt) {
+  int w = 0;
+  for (int n = 2; n <= 8; ++n) {
+    const int b = (n - 1) * dc_tpo(bt, n) * DC_BN * 4;
+    w = b > w ? b : w;
+  }
+  return w;
+}
+
 // A stage holds KB bytes of K (NA = KB / 128 swizzle atoms) of the weight
 // tile and of the three activation planes.
 template <int BT, int ST, int KB>
@@ -157,18 +173,29 @@ struct DcLayout {
   static constexpr int OW_BYTES = CH * 32 * 2;          // one warp's output staging chunk
   static constexpr int OFF_O = ST * S_BYTES;             // 8 warps x 2 staging buffers
   static constexpr int OFF_BAR = OFF_O + 16 * OW_BYTES;
-  static constexpr int NBAR = 2 * ST + 4 + 1;            // full, empty; acc x2 x2; drain
+  static constexpr int NBAR = 2 * ST + 4 + 2;            // full, empty; acc x2 x2; drain; recv
   static constexpr int OFF_MISC = (OFF_BAR + NBAR * 8 + 15) & ~15;
   static constexpr int OFF_RED = OFF_MISC + 16;
   static constexpr int RED_BYTES = 4 * BT * 8;
   static constexpr int OFF_XS = OFF_RED + RED_BYTES;  // token scales 2^-e [BT]
-  static constexpr int BYTES = OFF_XS + BT * 4;
+  static constexpr int CORE_BYTES = OFF_XS + BT * 4;
+  // split-K: this CTA's own 4-token groups at the start of the ring (free
+  // once its MMAs are done); the groups the other ranks send, which may
+  // arrive while this CTA still streams, behind everything else when that
+  // fits, else in the last ring stage (ring depth ST - 1 in split mode)
+  static constexpr int OFF_OWN = 0;
+  static constexpr bool RECV_IN_RING = CORE_BYTES + 16 + dc_recv_bytes_max(BT) + 1024 > 232448;
+  static constexpr int OFF_RECV = RECV_IN_RING ? (ST - 1) * S_BYTES : (CORE_BYTES + 15) & ~15;
+  static constexpr int BYTES = RECV_IN_RING ? CORE_BYTES : OFF_RECV + dc_recv_bytes_max(BT);
   static constexpr int ALLOC = BYTES + 1024;
   static constexpr int ACC_COLS = 3 * BT <= 64 ? 64 : 3 * BT <= 128 ? 128 : 256;  // per buffer
   static_assert(S_BYTES % 1024 == 0 && XA_BYTES % 1024 == 0, "atoms keep 1024-B alignment");
   static_assert(KB == 128 || KB == 256, "stage K bytes");
   static_assert(OFF_XS % 16 == 0, "token scales are read as float4");
-  static_assert(P_BYTES <= ST * S_BYTES, "split-K partial must fit in the ring");
+  static_assert(ST >= 2, "split-K keeps ST - 1 ring stages");
+  static_assert(dc_own_bytes_max(BT) <= (ST - 1) * S_BYTES, "own split-K groups fit the ring");
+  static_assert(!RECV_IN_RING || dc_recv_bytes_max(BT) <= S_BYTES,
+                "received split-K groups fit one stage");
   static_assert(ALLOC <= 232448, "shared memory budget");
   static_assert(3 * BT <= 256, "N = 3 BT must fit one MMA");
 };
@@ -280,6 +307,10 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
   const int unit0 = (int)blockIdx.x;
   const int ustride = (nsplit > 1) ? units : (int)gridDim.x;
   const int mvalid = min(BT, args.M);
+  // ring depth: in split-K mode the last stage may receive the other ranks' partials
+  const int NS = nsplit > 1 && L::RECV_IN_RING ? ST - 1 : ST;
+  const int tpo = dc_tpo(mvalid, nsplit);  // split-K tokens per rank (multiple of 4)
+  const int m4 = (mvalid + 3) & ~3;
   auto unit_k = [&](int& kb, int& nk) {
     kb = (nsplit > 1 ? (int)blockIdx.z : 0) * args.kps;
     nk = max(0, min(args.kps, KS - kb));
@@ -291,6 +322,7 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
   const uint32_t bar_accfull = bar_empty + 8 * ST;   // [2]
   const uint32_t bar_accempty = bar_accfull + 16;    // [2]
   const uint32_t bar_drain = bar_accempty + 16;
+  const uint32_t bar_recv = bar_drain + 8;           // split-K partials from the other ranks
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
 
@@ -305,8 +337,15 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
       ptx::mbar_init(bar_accempty + 8 * b, 8);
     }
     ptx::mbar_init(bar_drain, 1);
+    if (nsplit > 1) ptx::mbar_init(bar_recv, 1);
     *abort_flag = 0;
     ptx::fence_mbar_init();
+    if (nsplit > 1) {
+      // this rank's groups, 16 bytes per row from each of the other ranks
+      const int r = (int)ptx::cluster_ctarank();
+      const int ng = max(0, min(tpo, m4 - r * tpo)) >> 2;
+      ptx::mbar_arrive_expect_tx(bar_recv, (uint32_t)((nsplit - 1) * ng * DC_BN * 16));
+    }
     ptx::prefetch_tmap(&tm_w);
     ptx::prefetch_tmap(&tm_x);
     if (args.y_tma) ptx::prefetch_tmap(&tm_y);
@@ -319,6 +358,9 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  // split-K: every rank's receive barrier is initialised before any rank sends
+  // (the matching wait comes just before the first send, or at the end)
+  if (nsplit > 1) ptx::cluster_arrive_relaxed();
   if (threadIdx.x == 0) trace_stamp(tr, 1);
   if (threadIdx.x == 0) ptx::pdl_launch_dependents();
 
@@ -340,7 +382,15 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
           ptx::tma_load_2d(sbase + L::OFF_S + s * L::S_BYTES + a * L::WA_BYTES, &tm_w,
                            ks * KB + a * DC_AK, n0, full);
       };
-      int g = 0;
+      int g = 0, rs = 0;  // stage count; its ring slot g % NS and phase (g / NS) & 1
+      uint32_t rph = 0u;
+      auto adv = [&] {
+        ++g;
+        if (++rs == NS) {
+          rs = 0;
+          rph ^= 1u;
+        }
+      };
       bool ok = true, waited = false;
       for (int u = unit0; u < units && ok; u += ustride) {
         int kb, nk;
@@ -348,28 +398,27 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
         const int n0 = u * DC_BN;
         int i = 0;
         if (!waited) {
-          const int pre = nk < ST ? nk : ST;
-          for (; i < pre; ++i, ++g) issue_w(g, kb + i, n0);  // fresh stages: no wait
-          for (int i2 = ST; i2 < nk; ++i2)
+          const int pre = nk < NS ? nk : NS;
+          for (; i < pre; ++i, adv()) issue_w(rs, kb + i, n0);  // fresh stages: no wait
+          for (int i2 = NS; i2 < nk; ++i2)
             for (int a = 0; a < stage_atoms(kb + i2); ++a)
               ptx::tma_prefetch_l2_2d(&tm_w, (kb + i2) * KB + a * DC_AK, n0);
           trace_stamp(tr, 2);
           ptx::pdl_wait();
           waited = true;
         }
-        for (; i < nk; ++i, ++g) {
-          const int s = g % ST;
-          if (!ptx::mbar_wait(bar_empty + 8 * s, ((uint32_t)(g / ST) & 1u) ^ 1u, tmo, abort_flag)) {
+        for (; i < nk; ++i, adv()) {
+          if (!ptx::mbar_wait(bar_empty + 8 * rs, rph ^ 1u, tmo, abort_flag)) {
             ok = false;
             break;
           }
-          issue_w(s, kb + i, n0);
+          issue_w(rs, kb + i, n0);
         }
       }
       if (!waited) ptx::pdl_wait();
       if (*abort_flag) {
-        for (int i = g > ST ? g - ST : 0; i < g; ++i)
-          dc_wait_drain(bar_full + 8 * (i % ST), (uint32_t)(i / ST) & 1u, tmo);
+        for (int i = g > NS ? g - NS : 0; i < g; ++i)
+          dc_wait_drain(bar_full + 8 * (i % NS), (uint32_t)(i / NS) & 1u, tmo);
       }
     }
     __syncwarp();
@@ -379,28 +428,34 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
     // rows p BT + m, tokens m >= M zero-filled
     if (lane == 0) {
       ptx::pdl_wait();  // the planes come from the split pre-pass
-      int g = 0;
+      trace_stamp(tr, 3);
+      int g = 0, rs = 0;
+      uint32_t rph = 0u;
       bool ok = true;
       for (int u = unit0; u < units && ok; u += ustride) {
         int kb, nk;
         unit_k(kb, nk);
-        for (int i = 0; i < nk; ++i, ++g) {
-          const int s = g % ST;
-          if (!ptx::mbar_wait(bar_empty + 8 * s, ((uint32_t)(g / ST) & 1u) ^ 1u, tmo, abort_flag)) {
+        for (int i = 0; i < nk; ++i) {
+          if (!ptx::mbar_wait(bar_empty + 8 * rs, rph ^ 1u, tmo, abort_flag)) {
             ok = false;
             break;
           }
           const int na = stage_atoms(kb + i);
-          const uint32_t full = bar_full + 8 * s;
+          const uint32_t full = bar_full + 8 * rs;
           ptx::mbar_arrive_expect_tx(full, (uint32_t)(na * L::XA_BYTES));
-          const uint32_t dst = sbase + L::OFF_S + s * L::S_BYTES + L::W_BYTES;
+          const uint32_t dst = sbase + L::OFF_S + rs * L::S_BYTES + L::W_BYTES;
           for (int a = 0; a < na; ++a)
             ptx::tma_load_3d(dst + a * L::XA_BYTES, &tm_x, (kb + i) * KB + a * DC_AK, 0, 0, full);
+          ++g;
+          if (++rs == NS) {
+            rs = 0;
+            rph ^= 1u;
+          }
         }
       }
       if (*abort_flag) {
-        for (int i = g > ST ? g - ST : 0; i < g; ++i)
-          dc_wait_drain(bar_full + 8 * (i % ST), (uint32_t)(i / ST) & 1u, tmo);
+        for (int i = g > NS ? g - NS : 0; i < g; ++i)
+          dc_wait_drain(bar_full + 8 * (i % NS), (uint32_t)(i / NS) & 1u, tmo);
       }
     }
     __syncwarp();
@@ -413,7 +468,8 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
       const uint64_t desc0 = ptx::smem_desc_sw128(sbase + L::OFF_S);
       ptx::pdl_wait();
       bool ok = true;
-      int g = 0, it = 0;
+      int it = 0, rs = 0;
+      uint32_t rph = 0u;
       for (int u = unit0; u < units && ok; u += ustride, ++it) {
         int kb, nk;
         unit_k(kb, nk);
@@ -422,9 +478,14 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
         ok = ptx::mbar_wait(bar_accempty + 8 * b, ((uint32_t)(it >> 1) & 1u) ^ 1u, tmo, abort_flag);
         if (!ok) break;
         ptx::tc_fence_after();
-        for (int i = 0; i < nk; ++i, ++g) {
-          const int s = g % ST;
-          ok = ptx::mbar_wait(bar_full + 8 * s, (uint32_t)(g / ST) & 1u, tmo, abort_flag);
+        for (int i = 0; i < nk; ++i) {
+          const int s = rs;  // ring slot and phase of this stage
+          const uint32_t ph = rph;
+          if (++rs == NS) {
+            rs = 0;
+            rph ^= 1u;
+          }
+          ok = ptx::mbar_wait(bar_full + 8 * s, ph, tmo, abort_flag);
           if (!ok) break;
           ptx::tc_fence_after();
           const int rem = args.K - (kb + i) * KB;
@@ -464,6 +525,9 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
     float* xs_s = reinterpret_cast<float*>(smem + L::OFF_XS);
     if (e < BT) xs_s[e] = e < args.M ? __ldg(args.xscale + e) : 0.f;
     dc_epi_bar();
+    // split-K: the other ranks' receive barriers are ready (arrived at set-up)
+    const uint32_t rank = nsplit > 1 ? ptx::cluster_ctarank() : 0u;
+    if (nsplit > 1) ptx::cluster_wait();
     constexpr int NCH = BT / CH;                // chunks per tile
     constexpr int NCG = (NCH + 1) / 2;          // chunks per group (at most)
     constexpr int NB = ARGMAX ? NCG * CH : 1;   // running best per owned token
@@ -515,9 +579,29 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
             acc[jj] = (__uint_as_float(rr[0][jj]) + __uint_as_float(rr[1][jj])) +
                       __uint_as_float(rr[2][jj]);
           if (nsplit > 1) {
-            float* part = reinterpret_cast<float*>(smem);
+            // split-K: each 4-token group of this row goes to the rank that
+            // owns it (16 bytes straight from registers into its shared
+            // memory, counted on its receive barrier); this rank's own
+            // groups stay in the start of its ring
 #pragma unroll
-            for (int jj = 0; jj < CH; ++jj) part[(c0 + jj) * DC_BN + row] = acc[jj];
+            for (int gq = 0; gq < CH / 4; ++gq) {
+              const int t0 = c0 + 4 * gq;
+              if (t0 < m4) {
+                const int o = t0 / tpo;
+                const int gl = (t0 - o * tpo) >> 2;
+                const float4 v = make_float4(acc[4 * gq], acc[4 * gq + 1], acc[4 * gq + 2],
+                                             acc[4 * gq + 3]);
+                if (o == (int)rank) {
+                  *reinterpret_cast<float4*>(smem + L::OFF_OWN + (gl * DC_BN + row) * 16) = v;
+                } else {
+                  const int slot = (int)rank < o ? (int)rank : (int)rank - 1;
+                  const uint32_t off =
+                      sbase + (uint32_t)(L::OFF_RECV + ((slot * (tpo >> 2) + gl) * DC_BN + row) * 16);
+                  ptx::st_async_v4(ptx::mapa_shared(off, (uint32_t)o), v,
+                                   ptx::mapa_shared(bar_recv, (uint32_t)o));
+                }
+              }
+            }
           } else if constexpr (ARGMAX) {
 #pragma unroll
             for (int jj = 0; jj < CH; ++jj) {
@@ -598,6 +682,76 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar_accempty + 8 * b);
     }
+    if (nsplit > 1) {
+      // ---------------------------------------------------------- split-K owner
+      // sum the partials of this rank's groups in rank (= K) order, then the
+      // same scale / bias / fp16 (or greedy key) as the unsplit epilogue.
+      // The receive wait is never skipped: no CTA may leave while another
+      // rank can still store into its shared memory (after an abort it is a
+      // bounded drain).
+      if (e == 0) trace_stamp(tr, 8);
+      // per-row weight scale and bias: read while the partials arrive
+      const int n = unit0 * DC_BN + row;
+      const bool nok = n < args.N;
+      const float sc = nok ? args.scales[n] : 0.f;
+      const float bb = nok ? dc_load_bias(args.bias, args.bias_dtype, n) : 0.f;
+      dc_epi_bar();  // own groups written by both thread groups
+      const int ng = max(0, min(tpo, m4 - (int)rank * tpo)) >> 2;
+      bool got = ng == 0 || ptx::mbar_wait_cluster(bar_recv, 0u, tmo, abort_flag);
+      if (!got) {
+        const long long t0 = clock64();
+        while (!ptx::mbar_try_wait_cluster(bar_recv, 0u)) {
+          if (clock64() - t0 > (long long)(tmo * 2ull)) break;
+        }
+      }
+      if (e == 0) trace_stamp(tr, 9);
+      if (got && have_acc) {
+        for (int gl = grp; gl < ng; gl += 2) {
+          float4 pv[kMaxSplits];
+#pragma unroll
+          for (int sp = 0; sp < kMaxSplits; ++sp) {
+            if (sp < nsplit) {
+              const int off = sp == (int)rank
+                                  ? L::OFF_OWN + (gl * DC_BN + row) * 16
+                                  : L::OFF_RECV +
+                                        (((sp < (int)rank ? sp : sp - 1) * (tpo >> 2) + gl) *
+                                             DC_BN + row) * 16;
+              pv[sp] = *reinterpret_cast<const float4*>(smem + off);
+            }
+          }
+          float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int sp = 0; sp < kMaxSplits; ++sp) {  // rank order
+            if (sp < nsplit) {
+              a4.x += pv[sp].x;
+              a4.y += pv[sp].y;
+              a4.z += pv[sp].z;
+              a4.w += pv[sp].w;
+            }
+          }
+          const int t0 = (int)rank * tpo + 4 * gl;
+          const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const int t = t0 + q4;
+            if (ARGMAX) {
+              unsigned long long k = 0ull;
+              if (t < mvalid) {
+                const __half v = __float2half_rn(av[q4] * sc * xs_s[t]);
+                if (nok && __half2float(v) > -FLT_MAX)
+                  k = ((unsigned long long)f16_order_key(v) << 32) |
+                      (unsigned long long)(0xFFFFFFFFu - (uint32_t)((int64_t)n + args.vocab_offset));
+              }
+              k = dc_warp_max_u64(k);
+              if (lane == 0 && k) atomicMax(args.packed + t, k);
+            } else if (nok && t < mvalid) {
+              args.y[(size_t)t * args.N + n] = __float2half_rn(fmaf(av[q4] * sc, xs_s[t], bb));
+            }
+          }
+        }
+      }
+      if (e == 0) trace_stamp(tr, 10);
+    }
     if (args.y_tma && lane == 0) ptx::bulk_wait_group_read0();
     if constexpr (ARGMAX) {
       if (nsplit == 1) {
@@ -632,60 +786,8 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
     __syncwarp();
   }
 
-  if (nsplit > 1) {
-    // ------------------------------------------------------------ cluster split-K reduction
-    __syncwarp();
-    ptx::cluster_sync();
-    if (warp >= 4 && have_acc) {
-      const int n0 = unit0 * DC_BN;
-      const uint32_t rank = ptx::cluster_ctarank();
-      const int w8 = warp - 4;
-      const int r0 = 4 * lane;
-      float sc4[4], bb4[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int ne = n0 + r0 + q;
-        sc4[q] = ne < args.N ? args.scales[ne] : 0.f;
-        bb4[q] = ne < args.N ? dc_load_bias(args.bias, args.bias_dtype, ne) : 0.f;
-      }
-      for (int jb = (int)rank + w8 * nsplit; jb < mvalid; jb += 8 * nsplit) {
-        const uint32_t loc = sbase + (uint32_t)((jb * DC_BN + r0) * 4);
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int sp = 0; sp < nsplit; ++sp) {  // fixed order: deterministic
-          const float4 p = ptx::ld_dsmem_f4(ptx::mapa_shared(loc, (uint32_t)sp));
-          acc.x += p.x;
-          acc.y += p.y;
-          acc.z += p.z;
-          acc.w += p.w;
-        }
-        const float xs = reinterpret_cast<const float*>(smem + L::OFF_XS)[jb];
-        const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
-        if (ARGMAX) {
-          unsigned long long k = 0ull;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int nq = n0 + r0 + q;
-            const __half v = __float2half_rn(a4[q] * sc4[q] * xs);
-            if (nq < args.N && __half2float(v) > -FLT_MAX) {
-              const unsigned long long kq =
-                  ((unsigned long long)f16_order_key(v) << 32) |
-                  (unsigned long long)(0xFFFFFFFFu - (uint32_t)((int64_t)nq + args.vocab_offset));
-              k = kq > k ? kq : k;
-            }
-          }
-          k = dc_warp_max_u64(k);
-          if (lane == 0 && k) atomicMax(args.packed + jb, k);
-        } else {
-          __half* yrow = args.y + (size_t)jb * args.N;
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            if (n0 + r0 + q < args.N) yrow[n0 + r0 + q] = __float2half_rn(fmaf(a4[q] * sc4[q], xs, bb4[q]));
-        }
-      }
-    }
-    __syncwarp();
-    ptx::cluster_sync();
-  }
+  // split-K: the other warps pass the cluster barrier they arrived at during set-up
+  if (nsplit > 1 && warp < 4) ptx::cluster_wait();
 
   if (threadIdx.x == 128) trace_stamp(tr, 6);
   ptx::tc_fence_before();

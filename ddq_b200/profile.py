@@ -121,7 +121,7 @@ def main(argv=None):
         launch(a.warmup + a.iters)       # cold weights (next copy in the rotation)
         torch.cuda.synchronize(dev)
         L.ddq_set_debug(0, 0)
-        buf = np.zeros((2048, 8), dtype=np.uint64)
+        buf = np.zeros((2048, 16), dtype=np.uint64)  # 16 stamp slots per CTA
         _lib.check(L.ddq_read_trace(buf.ctypes.data_as(ctypes.c_void_p), 2048,
                                     stream.cuda_stream), "read trace")
         used = buf[(buf[:, 0] > 0) & (buf[:, 7] > 0)].astype(np.int64)

@@ -245,11 +245,14 @@ int ddq_set_debug(int flags, uint64_t wait_timeout_ns);
 
 /*
  * Tracing hook (no reference counterpart): with debug flag bit 1 set, each of
- * the first 2048 CTAs of a tensor-core launch writes 8 %globaltimer stamps
- * (ns): entry, set-up done, first weight loads issued, first weight tile
- * landed, last MMA issued, accumulator ready, epilogue done, exit.  This
- * copies the stamps of the first max_ctas CTAs (8 uint64 each) to host
- * memory `dst` and synchronises `stream`.
+ * the first 2048 CTAs of a tensor-core launch writes %globaltimer stamps (ns)
+ * into 16 slots: 0 entry, 1 set-up done, 2 first weight loads issued, 3 first
+ * weight tile landed (decode kernel: activation producer past the grid
+ * dependency), 4 last MMA issued, 5 accumulator ready, 6 epilogue done,
+ * 7 exit; decode kernel in split-K mode also 8 partials sent, 9 the other
+ * ranks' partials received, 10 partials reduced; other slots stay 0.  This copies the
+ * stamps of the first max_ctas CTAs (16 uint64 each) to host memory `dst`
+ * and synchronises `stream`.
  */
 int ddq_read_trace(uint64_t* dst, int max_ctas, void* stream);
 
