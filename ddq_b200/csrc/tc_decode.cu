@@ -307,8 +307,12 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
   const int unit0 = (int)blockIdx.x;
   const int ustride = (nsplit > 1) ? units : (int)gridDim.x;
   const int mvalid = min(BT, args.M);
+  // split-K partials: up to 32 tokens each rank pushes the owners their
+  // groups; 64-token tiles (4x the bytes, where pushing measured slower) park
+  // them for the owners to read
+  constexpr bool PUSH = BT <= 32;
   // ring depth: in split-K mode the last stage may receive the other ranks' partials
-  const int NS = nsplit > 1 && L::RECV_IN_RING ? ST - 1 : ST;
+  const int NS = nsplit > 1 && PUSH && L::RECV_IN_RING ? ST - 1 : ST;
   const int tpo = dc_tpo(mvalid, nsplit);  // split-K tokens per rank (multiple of 4)
   const int m4 = (mvalid + 3) & ~3;
   auto unit_k = [&](int& kb, int& nk) {
@@ -337,10 +341,10 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
       ptx::mbar_init(bar_accempty + 8 * b, 8);
     }
     ptx::mbar_init(bar_drain, 1);
-    if (nsplit > 1) ptx::mbar_init(bar_recv, 1);
+    if (PUSH && nsplit > 1) ptx::mbar_init(bar_recv, 1);
     *abort_flag = 0;
     ptx::fence_mbar_init();
-    if (nsplit > 1) {
+    if (PUSH && nsplit > 1) {
       // this rank's groups, 16 bytes per row from each of the other ranks
       const int r = (int)ptx::cluster_ctarank();
       const int ng = max(0, min(tpo, m4 - r * tpo)) >> 2;
@@ -360,7 +364,7 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
   const uint32_t tmem_base = *tmem_holder;
   // split-K: every rank's receive barrier is initialised before any rank sends
   // (the matching wait comes just before the first send, or at the end)
-  if (nsplit > 1) ptx::cluster_arrive_relaxed();
+  if (PUSH && nsplit > 1) ptx::cluster_arrive_relaxed();
   if (threadIdx.x == 0) trace_stamp(tr, 1);
   if (threadIdx.x == 0) ptx::pdl_launch_dependents();
 
@@ -527,7 +531,7 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
     dc_epi_bar();
     // split-K: the other ranks' receive barriers are ready (arrived at set-up)
     const uint32_t rank = nsplit > 1 ? ptx::cluster_ctarank() : 0u;
-    if (nsplit > 1) ptx::cluster_wait();
+    if (PUSH && nsplit > 1) ptx::cluster_wait();
     constexpr int NCH = BT / CH;                // chunks per tile
     constexpr int NCG = (NCH + 1) / 2;          // chunks per group (at most)
     constexpr int NB = ARGMAX ? NCG * CH : 1;   // running best per owned token
@@ -578,7 +582,12 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
           for (int jj = 0; jj < CH; ++jj)
             acc[jj] = (__uint_as_float(rr[0][jj]) + __uint_as_float(rr[1][jj])) +
                       __uint_as_float(rr[2][jj]);
-          if (nsplit > 1) {
+          if (nsplit > 1 && !PUSH) {
+            // 64-token split-K: park the partial [token][row] in the ring
+            float* part = reinterpret_cast<float*>(smem);
+#pragma unroll
+            for (int jj = 0; jj < CH; ++jj) part[(c0 + jj) * DC_BN + row] = acc[jj];
+          } else if (nsplit > 1) {
             // split-K: each 4-token group of this row goes to the rank that
             // owns it (16 bytes straight from registers into its shared
             // memory, counted on its receive barrier); this rank's own
@@ -682,7 +691,7 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar_accempty + 8 * b);
     }
-    if (nsplit > 1) {
+    if (PUSH && nsplit > 1) {
       // ---------------------------------------------------------- split-K owner
       // sum the partials of this rank's groups in rank (= K) order, then the
       // same scale / bias / fp16 (or greedy key) as the unsplit epilogue.
@@ -787,7 +796,78 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
   }
 
   // split-K: the other warps pass the cluster barrier they arrived at during set-up
-  if (nsplit > 1 && warp < 4) ptx::cluster_wait();
+  if (PUSH && nsplit > 1 && warp < 4) ptx::cluster_wait();
+
+  if (!PUSH && nsplit > 1) {
+    // ------------------------------------------------------------ 64-token split-K
+    // after a cluster barrier the owner of token jb (rank jb mod n, one warp
+    // per token) reads that token's 128-row partial from every rank - all
+    // the remote loads in flight together - and sums them in rank (= K)
+    // order; a second barrier keeps every CTA alive while others read it
+    const int n0 = unit0 * DC_BN;
+    const int r0 = 4 * lane;
+    float sc4[4] = {0.f, 0.f, 0.f, 0.f}, bb4[4] = {0.f, 0.f, 0.f, 0.f};
+    if (warp >= 4) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int ne = n0 + r0 + q;
+        sc4[q] = ne < args.N ? args.scales[ne] : 0.f;
+        bb4[q] = ne < args.N ? dc_load_bias(args.bias, args.bias_dtype, ne) : 0.f;
+      }
+    }
+    __syncwarp();
+    if (threadIdx.x == 128) trace_stamp(tr, 8);
+    ptx::cluster_sync();
+    if (threadIdx.x == 128) trace_stamp(tr, 9);
+    if (warp >= 4 && have_acc) {
+      const uint32_t rank = ptx::cluster_ctarank();
+      const int w8 = warp - 4;
+      for (int jb = (int)rank + w8 * nsplit; jb < mvalid; jb += 8 * nsplit) {
+        const uint32_t loc = sbase + (uint32_t)((jb * DC_BN + r0) * 4);
+        float4 pv[kMaxSplits];
+#pragma unroll
+        for (int sp = 0; sp < kMaxSplits; ++sp)
+          if (sp < nsplit) pv[sp] = ptx::ld_dsmem_f4(ptx::mapa_shared(loc, (uint32_t)sp));
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int sp = 0; sp < kMaxSplits; ++sp) {  // rank order: deterministic
+          if (sp < nsplit) {
+            acc.x += pv[sp].x;
+            acc.y += pv[sp].y;
+            acc.z += pv[sp].z;
+            acc.w += pv[sp].w;
+          }
+        }
+        const float xs = reinterpret_cast<const float*>(smem + L::OFF_XS)[jb];
+        const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+        if (ARGMAX) {
+          unsigned long long k = 0ull;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int nq = n0 + r0 + q;
+            const __half v = __float2half_rn(a4[q] * sc4[q] * xs);
+            if (nq < args.N && __half2float(v) > -FLT_MAX) {
+              const unsigned long long kq =
+                  ((unsigned long long)f16_order_key(v) << 32) |
+                  (unsigned long long)(0xFFFFFFFFu - (uint32_t)((int64_t)nq + args.vocab_offset));
+              k = kq > k ? kq : k;
+            }
+          }
+          k = dc_warp_max_u64(k);
+          if (lane == 0 && k) atomicMax(args.packed + jb, k);
+        } else {
+          __half* yrow = args.y + (size_t)jb * args.N;
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            if (n0 + r0 + q < args.N)
+              yrow[n0 + r0 + q] = __float2half_rn(fmaf(a4[q] * sc4[q], xs, bb4[q]));
+        }
+      }
+    }
+    __syncwarp();
+    if (threadIdx.x == 128) trace_stamp(tr, 10);
+    ptx::cluster_sync();
+  }
 
   if (threadIdx.x == 128) trace_stamp(tr, 6);
   ptx::tc_fence_before();
