@@ -51,6 +51,7 @@ struct AtArgs {
   int64_t out_stride;
   int Hq, Hkv;
   float scale;
+  int trace;             // debug flag bit 1: phase stamps (see ddq_read_trace)
 };
 
 template <int D>
@@ -269,6 +270,8 @@ struct AmSmem {
   uint8_t ring[AM_NW * AM_DEPTH][2][AM_CHUNK];  // [slot][K | V]
   float acc[AM_NW][AT_GMAX][64];
   __half q[AT_GMAX][64];
+  __align__(16) __half knew[64];  // the new cache row (patched into its chunk's tile)
+  __align__(16) __half vnew[64];
   float m[AM_NW][AT_GMAX], l[AM_NW][AT_GMAX];
   unsigned long long full[AM_NW * AM_DEPTH];
   int abort_flag;
@@ -318,6 +321,8 @@ __global__ void __launch_bounds__(AM_NW * 32, 1)
   const int b = blockIdx.x / a.Hkv, g = blockIdx.x % a.Hkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gid = lane >> 2, tig = lane & 3;
+  const bool tr = a.trace != 0;
+  if (threadIdx.x == 0) trace_stamp(tr, 0);
   __half* kc = a.kc + (size_t)b * a.cache_bstride + (size_t)g * a.cap * D;
   __half* vc = a.vc + (size_t)b * a.cache_bstride + (size_t)g * a.cap * D;
   if (threadIdx.x == 0) {
@@ -340,12 +345,34 @@ __global__ void __launch_bounds__(AM_NW * 32, 1)
     }
   }
   ptx::pdl_wait();  // qkv comes from the previous kernel; earlier cache rows are complete
+  if (threadIdx.x == 0) trace_stamp(tr, 1);
+  // one memory round trip: the position, this group's q / k / v values and
+  // the rotary rows are all requested before any of them is used
+  const __half* row = a.qkv + (size_t)b * a.qkv_stride;
+  constexpr int NT = AM_NW * 32;
+  constexpr int NRI = ((G + 1) * DH + NT - 1) / NT;  // rotary pairs per thread
+  float x1[NRI], x2[NRI], c1[NRI], s1[NRI], c2[NRI], s2[NRI];
   const int64_t p = *a.pos;
+#pragma unroll
+  for (int r = 0; r < NRI; ++r) {
+    const int i = threadIdx.x + r * NT;
+    if (i < (G + 1) * DH) {
+      const int h = i / DH, d = i % DH;
+      const __half* src = h < G ? row + (size_t)(g * G + h) * D : row + (size_t)(a.Hq + g) * D;
+      x1[r] = __half2float(src[d]);
+      x2[r] = __half2float(src[d + DH]);
+      c1[r] = a.cos[d];
+      s1[r] = a.sin[d];
+      c2[r] = a.cos[d + DH];
+      s2[r] = a.sin[d + DH];
+    }
+  }
+  const __half vnew = threadIdx.x < D ? row[(size_t)(a.Hq + a.Hkv + g) * D + threadIdx.x]
+                                      : __float2half_rn(0.f);
   if (p < 0 || p >= a.cap) return;  // the host checks the range; nothing to do otherwise
   const int L = (int)p + 1;
   const int nchunks = (L + AM_ROWS - 1) / AM_ROWS;
   const int last = nchunks - 1;  // the chunk that holds the new row
-  const __half* row = a.qkv + (size_t)b * a.qkv_stride;
   const uint32_t ring0 = ptx::smem_u32(&sm.ring[0][0][0]);
   __syncthreads();  // barriers initialised
 
@@ -357,39 +384,44 @@ __global__ void __launch_bounds__(AM_NW * 32, 1)
     ptx::tma_load_4d(dst, &tm_k, 0, c * AM_ROWS, g, b, full);
     ptx::tma_load_4d(dst + AM_CHUNK, &tm_v, 0, c * AM_ROWS, g, b, full);
   };
-  // chunks without the new row can be requested before it is written
+  // every chunk can be requested now: the new row is not read back from the
+  // cache (its stale copy in the last chunk's tile is overwritten in shared
+  // memory), so the copies overlap the rotary embedding below
   if (lane == 0)
     for (int i = 0; i < AM_DEPTH; ++i) {
       const int c = warp + i * AM_NW;
-      if (c < last) issue(c);
+      if (c < nchunks) issue(c);
     }
 
   // ---- rotary embedding of the G query heads and the new key; cache write
-  for (int i = threadIdx.x; i < (G + 1) * DH; i += blockDim.x) {
-    const int h = i / DH, d = i % DH;
-    const __half* src = h < G ? row + (size_t)(g * G + h) * D : row + (size_t)(a.Hq + g) * D;
-    const float x1 = __half2float(src[d]), x2 = __half2float(src[d + DH]);
-    // x * cos + rotate_half(x) * sin, each product rounded as torch rounds it
-    const __half y1 =
-        __float2half_rn(__fadd_rn(__fmul_rn(x1, a.cos[d]), __fmul_rn(-x2, a.sin[d])));
-    const __half y2 =
-        __float2half_rn(__fadd_rn(__fmul_rn(x2, a.cos[d + DH]), __fmul_rn(x1, a.sin[d + DH])));
-    if (h < G) {
-      sm.q[h][d] = y1;
-      sm.q[h][d + DH] = y2;
-    } else {
-      kc[(size_t)p * D + d] = y1;
-      kc[(size_t)p * D + d + DH] = y2;
+#pragma unroll
+  for (int r = 0; r < NRI; ++r) {
+    const int i = threadIdx.x + r * NT;
+    if (i < (G + 1) * DH) {
+      const int h = i / DH, d = i % DH;
+      // x * cos + rotate_half(x) * sin, each product rounded as torch rounds it
+      const __half y1 = __float2half_rn(__fadd_rn(__fmul_rn(x1[r], c1[r]), __fmul_rn(-x2[r], s1[r])));
+      const __half y2 = __float2half_rn(__fadd_rn(__fmul_rn(x2[r], c2[r]), __fmul_rn(x1[r], s2[r])));
+      if (h < G) {
+        sm.q[h][d] = y1;
+        sm.q[h][d + DH] = y2;
+      } else {
+        kc[(size_t)p * D + d] = y1;
+        kc[(size_t)p * D + d + DH] = y2;
+        sm.knew[d] = y1;
+        sm.knew[d + DH] = y2;
+      }
     }
   }
   for (int i = threadIdx.x; i < (AT_GMAX - G) * D; i += blockDim.x)
     sm.q[G + i / D][i % D] = __float2half_rn(0.f);
-  for (int d = threadIdx.x; d < D; d += blockDim.x)
-    vc[(size_t)p * D + d] = row[(size_t)(a.Hq + a.Hkv + g) * D + d];
-  ptx::fence_proxy_async_global();  // the new cache row is read back through TMA
+  if (threadIdx.x < D) {
+    vc[(size_t)p * D + threadIdx.x] = vnew;
+    sm.vnew[threadIdx.x] = vnew;
+  }
   __syncthreads();
+  if (threadIdx.x == 0) trace_stamp(tr, 2);
   if (threadIdx.x == 0) ptx::pdl_launch_dependents();
-  if (lane == 0 && last % AM_NW == warp && last < AM_NW * AM_DEPTH) issue(last);
 
   // q fragments (rows 0..7 = heads; rows 8..15 of the A operand are zero)
   uint32_t qa[4][2];
@@ -409,10 +441,20 @@ __global__ void __launch_bounds__(AM_NW * 32, 1)
     if (!ptx::mbar_wait(ptx::smem_u32(&sm.full[s]), (uint32_t)((it / AM_DEPTH) & 1), timeout_ns,
                         &sm.abort_flag))
       break;
+    if (threadIdx.x == 0 && it == 0) trace_stamp(tr, 3);
     const uint32_t ks = ring0 + (uint32_t)(s * 2 * AM_CHUNK), vs = ks + AM_CHUNK;
     const int jn = min(AM_ROWS, L - c * AM_ROWS);  // positions of this chunk in use
-    if (jn < AM_ROWS) {
+    if (c == last) {
+      // the new row (position jn - 1 of this chunk) from shared memory; the
+      // rows after it are zeroed in the V tile
+      uint8_t* krow = &sm.ring[s][0][0];
       uint8_t* vrow = &sm.ring[s][1][0];
+      const int rp = jn - 1;
+      if (lane < 16) {
+        const int j = lane & 7;
+        const uint4 v = *reinterpret_cast<const uint4*>(lane < 8 ? &sm.knew[8 * j] : &sm.vnew[8 * j]);
+        *reinterpret_cast<uint4*>((lane < 8 ? krow : vrow) + at2_swz(rp, j)) = v;
+      }
       for (int idx = lane; idx < (AM_ROWS - jn) * 8; idx += 32)
         *reinterpret_cast<uint4*>(vrow + (jn + idx / 8) * 128 + (idx % 8) * 16) =
             make_uint4(0u, 0u, 0u, 0u);
@@ -501,6 +543,7 @@ __global__ void __launch_bounds__(AM_NW * 32, 1)
   }
 
   // ---- merge the warps' partial softmax sums
+  if (threadIdx.x == 0) trace_stamp(tr, 4);
   if (gid < G) {
 #pragma unroll
     for (int nd = 0; nd < 8; ++nd) {
@@ -513,19 +556,40 @@ __global__ void __launch_bounds__(AM_NW * 32, 1)
     }
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
-    const int h = i / D, d = i % D;
-    float mx = -FLT_MAX;
-    for (int w = 0; w < AM_NW; ++w) mx = fmaxf(mx, sm.m[w][h]);
-    float den = 0.f, num = 0.f;
+  if (threadIdx.x == 0) trace_stamp(tr, 5);
+  // warp h merges head h: lane w < 8 holds warp w's max and sum, every lane
+  // two head dimensions; the weights are summed in warp order
+  static_assert(AT_GMAX <= AM_NW, "one warp per query head in the merge");
+  if (warp < G) {
+    const int h = warp;
+    const float mw = lane < AM_NW ? sm.m[lane][h] : -FLT_MAX;
+    const float lw = lane < AM_NW ? sm.l[lane][h] : 0.f;
+    float mx = mw;
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    mx = __shfl_sync(0xffffffffu, mx, 0);
+    const float cw = lw > 0.f ? __expf(mw - mx) : 0.f;
+    float den = 0.f, n0 = 0.f, n1 = 0.f;
+#pragma unroll
     for (int w = 0; w < AM_NW; ++w) {
-      const float cw = sm.l[w][h] > 0.f ? __expf(sm.m[w][h] - mx) : 0.f;
-      den = fmaf(sm.l[w][h], cw, den);
-      num = fmaf(sm.acc[w][h][d], cw, num);
+      const float c = __shfl_sync(0xffffffffu, cw, w);
+      const float l = __shfl_sync(0xffffffffu, lw, w);
+      const float2 av = *reinterpret_cast<const float2*>(&sm.acc[w][h][2 * lane]);
+      den = fmaf(l, c, den);
+      n0 = fmaf(av.x, c, n0);
+      n1 = fmaf(av.y, c, n1);
     }
-    a.out[(size_t)b * a.out_stride + (size_t)(g * G + h) * D + d] = __float2half_rn(num / den);
+    __half* dst = a.out + (size_t)b * a.out_stride + (size_t)(g * G + h) * D + 2 * lane;
+    const __half2 o2 = __floats2half2_rn(n0 / den, n1 / den);
+    if ((reinterpret_cast<uintptr_t>(dst) & 3u) == 0) {
+      *reinterpret_cast<__half2*>(dst) = o2;
+    } else {  // caller's output row stride is odd
+      dst[0] = __low2half(o2);
+      dst[1] = __high2half(o2);
+    }
   }
   if (threadIdx.x == 0 && sm.abort_flag) record_device_error(DDQ_ERR_TIMEOUT);
+  if (threadIdx.x == 0) trace_stamp(tr, 6);
 }
 
 namespace {
@@ -562,13 +626,13 @@ int launch_decode_attention(const __half* qkv, int64_t qkv_stride, __half* kc, _
                             int64_t cache_bstride, int cap, const float* cos, const float* sin,
                             const int64_t* pos, __half* out, int64_t out_stride, int B, int Hq,
                             int Hkv, int D, float scale, unsigned long long timeout_ns,
-                            cudaStream_t s) {
+                            int debug_flags, cudaStream_t s) {
   if (B < 1 || Hkv < 1 || Hq < Hkv || Hq % Hkv != 0 || Hq / Hkv > AT_GMAX || cap < 1)
     return DDQ_ERR_SHAPE;
   if (D != 64 && D != 128) return DDQ_ERR_SHAPE;
   if (!aligned16(kc) || !aligned16(vc) || (cache_bstride % 8) != 0) return DDQ_ERR_ALIGNMENT;
   AtArgs a{qkv, qkv_stride, kc, vc, cache_bstride, cap, cos, sin, pos, out, out_stride, Hq, Hkv,
-           scale};
+           scale, (debug_flags & 2) != 0 ? 1 : 0};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(B * Hkv));
   cfg.blockDim = dim3(at_warps(D) * 32);

@@ -186,7 +186,7 @@ extern "C" int ddq_decode_attention(const void* qkv, int64_t qkv_stride, void* k
       reinterpret_cast<const __half*>(qkv), qkv_stride, reinterpret_cast<__half*>(k_cache),
       reinterpret_cast<__half*>(v_cache), cache_batch_stride, (int)capacity, cos, sin, pos,
       reinterpret_cast<__half*>(out), out_stride, (int)B, (int)Hq, (int)Hkv, (int)D, scale,
-      g_wait_timeout_ns, reinterpret_cast<cudaStream_t>(stream));
+      g_wait_timeout_ns, g_debug_flags, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int ddq_add_rmsnorm(const void* x, const void* delta, const float* w, float eps,
