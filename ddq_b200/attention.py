@@ -1,4 +1,5 @@
-"""Decode-step attention with RoPE and the KV-cache write fused in.
+"""Attention-side kernels: the decode step with RoPE and the KV-cache write
+fused in, and the prefill RoPE + cache write.
 
 ``decode_attention`` replaces, for one decode step, the reference engine's
 q/k rotary embedding (``RoPe_d.cu:12-68``), the cache write
@@ -52,3 +53,45 @@ def decode_attention(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Te
             torch.cuda.current_stream(qkv.device).cuda_stream)
     _lib.check(st, "decode_attention")
     return out
+
+
+def prefill_rope_kv(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                    cos: torch.Tensor, sin: torch.Tensor, start: int, num_heads: int,
+                    num_kv_heads: int, head_dim: int) -> torch.Tensor:
+    """Prefill chunk (``ddq_prefill_rope_kv``): qkv fp16 [B, S, (Hq + 2 Hkv) * D]
+    (or [B * S, ...] with B taken from the caches); cos/sin fp32 [S, D] for
+    positions start .. start + S - 1.  Writes rope(k) and v into the caches at
+    start .. start + S - 1 and returns rope(q) fp16 [B, S, Hq, D].  Replaces the
+    reference's q/k RoPE (``RoPe_d.cu:12-68``, ``engine.py:219-220``) and cache
+    write (``engine.py:126-130``)."""
+    def need(cond, msg):
+        if not cond:
+            raise RuntimeError(msg)
+    B = k_cache.shape[0]
+    width = (num_heads + 2 * num_kv_heads) * head_dim
+    need(qkv.is_cuda and qkv.dtype == torch.float16 and qkv.shape[-1] == width and
+         qkv.stride(-1) == 1, "prefill_rope_kv: qkv must be fp16 CUDA [..., (Hq + 2 Hkv) * D]")
+    rows = qkv.reshape(-1, width)
+    need(rows.shape[0] % B == 0, "prefill_rope_kv: qkv rows must be B * S")
+    S = rows.shape[0] // B
+    for c in (k_cache, v_cache):
+        need(c.is_cuda and c.dtype == torch.float16 and c.dim() == 4 and
+             tuple(c.shape[:2]) == (B, num_kv_heads) and c.shape[3] == head_dim and
+             c.stride(3) == 1 and c.stride(2) == head_dim and
+             c.stride(1) == c.shape[2] * head_dim,
+             "prefill_rope_kv: caches must be fp16 CUDA [B, Hkv, capacity, D], dense per sequence")
+    need(k_cache.stride(0) == v_cache.stride(0) and k_cache.shape == v_cache.shape,
+         "prefill_rope_kv: k and v caches must have the same shape and strides")
+    cos = cos.reshape(S, head_dim).contiguous()
+    sin = sin.reshape(S, head_dim).contiguous()
+    need(cos.dtype == torch.float32 and sin.dtype == torch.float32,
+         "prefill_rope_kv: fp32 cos/sin [S, D]")
+    q = torch.empty((B, S, num_heads, head_dim), dtype=torch.float16, device=qkv.device)
+    with torch.cuda.device(qkv.device):
+        st = _lib.load().ddq_prefill_rope_kv(
+            rows.data_ptr(), rows.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
+            k_cache.stride(0), k_cache.shape[2], cos.data_ptr(), sin.data_ptr(), int(start),
+            q.data_ptr(), B, S, num_heads, num_kv_heads, head_dim,
+            torch.cuda.current_stream(qkv.device).cuda_stream)
+    _lib.check(st, "prefill_rope_kv")
+    return q

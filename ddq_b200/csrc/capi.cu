@@ -170,6 +170,25 @@ extern "C" int ddq_w8a16_gemm_swiglu(const void* x, const uint8_t* wq_gu, const 
                    workspace, workspace_bytes, g_wait_timeout_ns, g_debug_flags, s, true);
 }
 
+extern "C" int ddq_prefill_rope_kv(const void* qkv, int64_t qkv_stride, void* k_cache,
+                                   void* v_cache, int64_t cache_batch_stride, int64_t capacity,
+                                   const float* cos, const float* sin, int64_t start,
+                                   void* q_out, int64_t B, int64_t S, int64_t Hq, int64_t Hkv,
+                                   int64_t D, void* stream) {
+  if (B < 0 || S < 0 || Hq < 0 || Hkv < 0 || capacity < 0 || start < 0) return DDQ_ERR_SHAPE;
+  if (B == 0 || S == 0) return DDQ_OK;
+  if (!qkv || !k_cache || !v_cache || !cos || !sin || !q_out) return DDQ_ERR_INVALID_ARGUMENT;
+  if (Hq < 1 || Hkv < 1 || B * S > 0x7fffffffll || Hq > 1024 || Hkv > 1024 ||
+      capacity > 0x7fffffff || start + S > capacity || qkv_stride < (Hq + 2 * Hkv) * D ||
+      cache_batch_stride < Hkv * capacity * D)
+    return DDQ_ERR_SHAPE;
+  return launch_prefill_rope_kv(
+      reinterpret_cast<const __half*>(qkv), qkv_stride, reinterpret_cast<__half*>(k_cache),
+      reinterpret_cast<__half*>(v_cache), cache_batch_stride, (int)capacity, cos, sin,
+      (int)start, reinterpret_cast<__half*>(q_out), (int)B, (int)S, (int)Hq, (int)Hkv, (int)D,
+      reinterpret_cast<cudaStream_t>(stream));
+}
+
 extern "C" int ddq_decode_attention(const void* qkv, int64_t qkv_stride, void* k_cache,
                                     void* v_cache, int64_t cache_batch_stride, int64_t capacity,
                                     const float* cos, const float* sin, const int64_t* pos,

@@ -52,6 +52,11 @@ int launch_pf(const __half* x, const uint8_t* wq, const float* scales, const voi
               int bias_dtype, __half* y, int M, int N, int K, void* ws, size_t ws_bytes,
               unsigned long long timeout_ns, int debug_flags, cudaStream_t s,
               bool swiglu = false);
+// Prefill: RoPE of q and k, q in token-major layout, k/v into the cache (rope.cu).
+int launch_prefill_rope_kv(const __half* qkv, int64_t qkv_stride, __half* kc, __half* vc,
+                           int64_t cache_bstride, int cap, const float* cos, const float* sin,
+                           int start, __half* q_out, int B, int S, int Hq, int Hkv, int D,
+                           cudaStream_t s);
 // Decode-step attention with RoPE and the KV-cache write fused (attention.cu).
 int launch_decode_attention(const __half* qkv, int64_t qkv_stride, __half* kc, __half* vc,
                             int64_t cache_bstride, int cap, const float* cos, const float* sin,

@@ -155,6 +155,25 @@ int ddq_decode_attention(const void* qkv, int64_t qkv_stride, void* k_cache, voi
                          void* stream);
 
 /*
+ * Prefill rotary embedding and KV-cache write for a chunk of S tokens per
+ * sequence starting at cache position `start`.  Replaces, for a prefill
+ * chunk, the RoPE kernel on q and k (RoPe_d.cu:12-68, called from
+ * engine.py:219-220) and the cache write (engine.py:126-130, 222).
+ *   qkv    fp16 [B * S, (Hq + 2 Hkv) * D] token rows (b major), row stride
+ *          qkv_stride (elements, multiple of 8): q heads, k heads, v heads
+ *   k_cache, v_cache  fp16 [B, Hkv, capacity, D], batch stride in elements
+ *   cos, sin  fp32 [S, D]: the rotary rows of positions start .. start + S - 1
+ *   q_out  fp16 [B, S, Hq, D] (contiguous)
+ * Writes q_out[b, s, h] = rope(q_h), cache[b, g, start + s] = (rope(k_g), v_g)
+ * with rope(x) = x cos + rotate_half(x) sin in fp32, rounded to fp16.
+ * D = 64 or 128; start + S <= capacity; every pointer 16-byte aligned.
+ */
+int ddq_prefill_rope_kv(const void* qkv, int64_t qkv_stride, void* k_cache, void* v_cache,
+                        int64_t cache_batch_stride, int64_t capacity, const float* cos,
+                        const float* sin, int64_t start, void* q_out, int64_t B, int64_t S,
+                        int64_t Hq, int64_t Hkv, int64_t D, void* stream);
+
+/*
  * Residual add + RMSNorm over rows of H (H % 8 == 0, 16-byte aligned rows):
  *   s = fp16(x + delta)   (delta may be NULL: s = x); written to x_out if
  *                         non-NULL (x_out may be x)

@@ -112,3 +112,40 @@ def test_decode_attention_ignores_garbage_past_the_position(cuda_device):
     err = ((o.float() - o_ref.float()).abs().amax(dim=1) /
            o_ref.float().abs().amax(dim=1).clamp_min(1e-6)).max().item()
     assert err < 2e-3, err
+
+
+@pytest.mark.parametrize("B,S,nh,nkv,hd,cap,start", [
+    (2, 40, 14, 2, 64, 64, 0), (3, 17, 14, 2, 64, 50, 5), (2, 9, 16, 2, 128, 32, 20),
+    (8, 512, 14, 2, 64, 528, 0)])
+def test_prefill_rope_kv_is_the_fp32_torch_rope(cuda_device, B, S, nh, nkv, hd, cap, start):
+    """ddq_prefill_rope_kv against the unfused steps it replaces, bit for bit:
+    fp32 rotate-half RoPE of q and k rounded to fp16, and the cache writes."""
+    from ddq_b200 import attention
+    g = torch.Generator(device="cuda").manual_seed(B * 100 + S)
+    qkv = torch.randn(B, S, (nh + 2 * nkv) * hd, generator=g, device="cuda").half()
+    kc = torch.randn(B, nkv, cap, hd, generator=g, device="cuda").half()
+    vc = torch.randn(B, nkv, cap, hd, generator=g, device="cuda").half()
+    kc0, vc0 = kc.clone(), vc.clone()
+    inv = 1.0 / (1e6 ** (torch.arange(0, hd, 2, dtype=torch.float32, device="cuda") / hd))
+    f = torch.arange(start, start + S, dtype=torch.float32, device="cuda")[:, None] * inv[None, :]
+    emb = torch.cat([f, f], dim=-1)
+    cos, sin = emb.cos(), emb.sin()
+
+    def rope(x):  # [B, H, S, D] fp16 -> fp16, as the engine's fp32 path
+        xf = x.float()
+        half = hd // 2
+        rot = torch.cat([-xf[..., half:], xf[..., :half]], dim=-1)
+        return (xf * cos + rot * sin).half()
+    q_ref = rope(qkv[..., : nh * hd].reshape(B, S, nh, hd).transpose(1, 2))
+    k_ref = rope(qkv[..., nh * hd:(nh + nkv) * hd].reshape(B, S, nkv, hd).transpose(1, 2))
+    v_ref = qkv[..., (nh + nkv) * hd:].reshape(B, S, nkv, hd).transpose(1, 2)
+    q = attention.prefill_rope_kv(qkv, kc, vc, cos, sin, start, nh, nkv, hd)
+    torch.cuda.synchronize()
+    assert q.shape == (B, S, nh, hd)
+    assert torch.equal(q.transpose(1, 2), q_ref)
+    assert torch.equal(kc[:, :, start:start + S], k_ref)
+    assert torch.equal(vc[:, :, start:start + S], v_ref)
+    # rows outside the chunk are untouched
+    assert torch.equal(kc[:, :, :start], kc0[:, :, :start])
+    assert torch.equal(kc[:, :, start + S:], kc0[:, :, start + S:])
+    assert torch.equal(vc[:, :, start + S:], vc0[:, :, start + S:])
