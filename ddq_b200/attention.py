@@ -57,11 +57,13 @@ def decode_attention(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Te
 
 def prefill_rope_kv(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                     cos: torch.Tensor, sin: torch.Tensor, start: int, num_heads: int,
-                    num_kv_heads: int, head_dim: int) -> torch.Tensor:
+                    num_kv_heads: int, head_dim: int, kv_out: bool = False):
     """Prefill chunk (``ddq_prefill_rope_kv``): qkv fp16 [B, S, (Hq + 2 Hkv) * D]
     (or [B * S, ...] with B taken from the caches); cos/sin fp32 [S, D] for
     positions start .. start + S - 1.  Writes rope(k) and v into the caches at
-    start .. start + S - 1 and returns rope(q) fp16 [B, S, Hq, D].  Replaces the
+    start .. start + S - 1 and returns rope(q) fp16 [B, S, Hq, D]; with ``kv_out``
+    returns (q, k, v), k and v token-major [B, S, Hkv, D] copies of the new rows
+    (attention inputs whose strides do not depend on the cache).  Replaces the
     reference's q/k RoPE (``RoPe_d.cu:12-68``, ``engine.py:219-220``) and cache
     write (``engine.py:126-130``)."""
     def need(cond, msg):
@@ -87,11 +89,16 @@ def prefill_rope_kv(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Ten
     need(cos.dtype == torch.float32 and sin.dtype == torch.float32,
          "prefill_rope_kv: fp32 cos/sin [S, D]")
     q = torch.empty((B, S, num_heads, head_dim), dtype=torch.float16, device=qkv.device)
+    k = v = None
+    if kv_out:
+        k = torch.empty((B, S, num_kv_heads, head_dim), dtype=torch.float16, device=qkv.device)
+        v = torch.empty_like(k)
     with torch.cuda.device(qkv.device):
         st = _lib.load().ddq_prefill_rope_kv(
             rows.data_ptr(), rows.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
             k_cache.stride(0), k_cache.shape[2], cos.data_ptr(), sin.data_ptr(), int(start),
-            q.data_ptr(), B, S, num_heads, num_kv_heads, head_dim,
+            q.data_ptr(), k.data_ptr() if kv_out else None, v.data_ptr() if kv_out else None,
+            B, S, num_heads, num_kv_heads, head_dim,
             torch.cuda.current_stream(qkv.device).cuda_stream)
     _lib.check(st, "prefill_rope_kv")
-    return q
+    return (q, k, v) if kv_out else q

@@ -173,8 +173,8 @@ extern "C" int ddq_w8a16_gemm_swiglu(const void* x, const uint8_t* wq_gu, const 
 extern "C" int ddq_prefill_rope_kv(const void* qkv, int64_t qkv_stride, void* k_cache,
                                    void* v_cache, int64_t cache_batch_stride, int64_t capacity,
                                    const float* cos, const float* sin, int64_t start,
-                                   void* q_out, int64_t B, int64_t S, int64_t Hq, int64_t Hkv,
-                                   int64_t D, void* stream) {
+                                   void* q_out, void* k_out, void* v_out, int64_t B, int64_t S,
+                                   int64_t Hq, int64_t Hkv, int64_t D, void* stream) {
   if (B < 0 || S < 0 || Hq < 0 || Hkv < 0 || capacity < 0 || start < 0) return DDQ_ERR_SHAPE;
   if (B == 0 || S == 0) return DDQ_OK;
   if (!qkv || !k_cache || !v_cache || !cos || !sin || !q_out) return DDQ_ERR_INVALID_ARGUMENT;
@@ -185,7 +185,8 @@ extern "C" int ddq_prefill_rope_kv(const void* qkv, int64_t qkv_stride, void* k_
   return launch_prefill_rope_kv(
       reinterpret_cast<const __half*>(qkv), qkv_stride, reinterpret_cast<__half*>(k_cache),
       reinterpret_cast<__half*>(v_cache), cache_batch_stride, (int)capacity, cos, sin,
-      (int)start, reinterpret_cast<__half*>(q_out), (int)B, (int)S, (int)Hq, (int)Hkv, (int)D,
+      (int)start, reinterpret_cast<__half*>(q_out), reinterpret_cast<__half*>(k_out),
+      reinterpret_cast<__half*>(v_out), (int)B, (int)S, (int)Hq, (int)Hkv, (int)D,
       reinterpret_cast<cudaStream_t>(stream));
 }
 

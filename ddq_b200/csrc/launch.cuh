@@ -55,8 +55,8 @@ int launch_pf(const __half* x, const uint8_t* wq, const float* scales, const voi
 // Prefill: RoPE of q and k, q in token-major layout, k/v into the cache (rope.cu).
 int launch_prefill_rope_kv(const __half* qkv, int64_t qkv_stride, __half* kc, __half* vc,
                            int64_t cache_bstride, int cap, const float* cos, const float* sin,
-                           int start, __half* q_out, int B, int S, int Hq, int Hkv, int D,
-                           cudaStream_t s);
+                           int start, __half* q_out, __half* k_out, __half* v_out, int B,
+                           int S, int Hq, int Hkv, int D, cudaStream_t s);
 // Decode-step attention with RoPE and the KV-cache write fused (attention.cu).
 int launch_decode_attention(const __half* qkv, int64_t qkv_stride, __half* kc, __half* vc,
                             int64_t cache_bstride, int cap, const float* cos, const float* sin,

@@ -6,8 +6,10 @@
 // For every token (b, s) of a chunk that starts at cache position `start`:
 //   q_h  = fp16(rope(q_h, start + s))  -> q_out[b, s, h, :]   (token-major, the
 //                                          layout attention reads without a copy)
-//   k_g  = fp16(rope(k_g, start + s))  -> k_cache[b, g, start + s, :]
-//   v_g                                -> v_cache[b, g, start + s, :]
+//   k_g  = fp16(rope(k_g, start + s))  -> k_cache[b, g, start + s, :]  (and k_out[b, s, g, :])
+//   v_g                                -> v_cache[b, g, start + s, :]  (and v_out[b, s, g, :])
+// The optional token-major k_out / v_out give attention inputs whose strides do
+// not depend on the cache capacity.
 // rope(x)[d] = x[d] cos[d] + rotate_half(x)[d] sin[d] with rotate_half(x) =
 // (-x[D/2:], x[:D/2]); each product and the sum rounded in fp32 as the
 // unfused fp32 path rounds them, then to fp16.  cos/sin are the caller's fp32
@@ -34,6 +36,8 @@ struct RkArgs {
   const float* sin;
   int start;
   __half* q_out;      // [B, S, Hq, D]
+  __half* k_out;      // [B, S, Hkv, D] or null
+  __half* v_out;
   int B, S, Hq, Hkv;
 };
 
@@ -84,27 +88,35 @@ __global__ void __launch_bounds__(256) prefill_rope_kv_kernel(const RkArgs a) {
                                    ((size_t)(h - a.Hq) * a.cap + a.start + s) * D;
       *reinterpret_cast<uint4*>(dst + d0) = o1;
       *reinterpret_cast<uint4*>(dst + DH + d0) = o2;
+      if (h >= a.Hq && a.k_out) {
+        __half* ko = a.k_out + ((size_t)t * a.Hkv + (h - a.Hq)) * D;
+        *reinterpret_cast<uint4*>(ko + d0) = o1;
+        *reinterpret_cast<uint4*>(ko + DH + d0) = o2;
+      }
     } else {
       const int jv = j - rot, g = jv / VP, d0 = 8 * (jv % VP);
       const uint4 u = *reinterpret_cast<const uint4*>(row + (size_t)(a.Hq + a.Hkv + g) * D + d0);
       *reinterpret_cast<uint4*>(a.vc + (size_t)b * a.cache_bstride +
                                 ((size_t)g * a.cap + a.start + s) * D + d0) = u;
+      if (a.v_out) *reinterpret_cast<uint4*>(a.v_out + ((size_t)t * a.Hkv + g) * D + d0) = u;
     }
   }
 }
 
 int launch_prefill_rope_kv(const __half* qkv, int64_t qkv_stride, __half* kc, __half* vc,
                            int64_t cache_bstride, int cap, const float* cos, const float* sin,
-                           int start, __half* q_out, int B, int S, int Hq, int Hkv, int D,
-                           cudaStream_t s) {
+                           int start, __half* q_out, __half* k_out, __half* v_out, int B,
+                           int S, int Hq, int Hkv, int D, cudaStream_t s) {
   if (B < 0 || S < 0 || Hq < 1 || Hkv < 1 || cap < 1 || start < 0) return DDQ_ERR_SHAPE;
   if (D != 64 && D != 128) return DDQ_ERR_SHAPE;
   if ((int64_t)start + S > cap) return DDQ_ERR_SHAPE;
   if (B == 0 || S == 0) return DDQ_OK;
   if (!aligned16(qkv) || qkv_stride % 8 != 0 || !aligned16(kc) || !aligned16(vc) ||
-      cache_bstride % 8 != 0 || !aligned16(cos) || !aligned16(sin) || !aligned16(q_out))
+      cache_bstride % 8 != 0 || !aligned16(cos) || !aligned16(sin) || !aligned16(q_out) ||
+      (k_out && !aligned16(k_out)) || (v_out && !aligned16(v_out)))
     return DDQ_ERR_ALIGNMENT;
-  RkArgs a{qkv, qkv_stride, kc, vc, cache_bstride, cap, cos, sin, start, q_out, B, S, Hq, Hkv};
+  RkArgs a{qkv,   qkv_stride, kc,    vc, cache_bstride, cap, cos, sin,
+           start, q_out,      k_out, v_out, B, S, Hq, Hkv};
   const int per_tok = (Hq + Hkv) * (D / 16) + Hkv * (D / 8);
   const int64_t total = (int64_t)B * S * per_tok;
   const int sms = device_sm_count(current_device());

@@ -271,13 +271,14 @@ class Engine:
             return self._mlp_block(x, self.linear(o.reshape(B, S, nh * hd), L["o"]), L)
         if pos is None and self.linear_kind == "fp8" and hd in (64, 128):
             # prefill chunk: RoPE of q and k and the cache write in one kernel;
-            # q comes back token-major, k and v are read from the cache rows
-            kc = cache.k[li, b0:b0 + B]
-            vc = cache.v[li, b0:b0 + B]
-            q = attention.prefill_rope_kv(qkv, kc, vc, cos, sin, start, nh, nkv, hd)
-            o = F.scaled_dot_product_attention(q.transpose(1, 2), kc[:, :, start:start + S],
-                                               vc[:, :, start:start + S], is_causal=True,
-                                               scale=scale, enable_gqa=True)
+            # q, k, v come back token-major (attention strides independent of
+            # the cache capacity)
+            q, k, v = attention.prefill_rope_kv(qkv, cache.k[li, b0:b0 + B],
+                                                cache.v[li, b0:b0 + B], cos, sin, start, nh,
+                                                nkv, hd, kv_out=True)
+            o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2),
+                                               v.transpose(1, 2), is_causal=True, scale=scale,
+                                               enable_gqa=True)
             o = o.transpose(1, 2).reshape(B, S, nh * hd)
             return self._mlp_block(x, self.linear(o, L["o"]), L)
         q = qkv[..., : nh * hd].reshape(B, S, nh, hd).transpose(1, 2)

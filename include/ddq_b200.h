@@ -164,14 +164,18 @@ int ddq_decode_attention(const void* qkv, int64_t qkv_stride, void* k_cache, voi
  *   k_cache, v_cache  fp16 [B, Hkv, capacity, D], batch stride in elements
  *   cos, sin  fp32 [S, D]: the rotary rows of positions start .. start + S - 1
  *   q_out  fp16 [B, S, Hq, D] (contiguous)
+ *   k_out, v_out  fp16 [B, S, Hkv, D] (contiguous) or NULL: token-major copies
+ *          of the new key and value rows (attention inputs whose strides do not
+ *          depend on the cache capacity)
  * Writes q_out[b, s, h] = rope(q_h), cache[b, g, start + s] = (rope(k_g), v_g)
- * with rope(x) = x cos + rotate_half(x) sin in fp32, rounded to fp16.
+ * (and k_out[b, s, g], v_out[b, s, g]) with rope(x) = x cos + rotate_half(x) sin
+ * in fp32, rounded to fp16.
  * D = 64 or 128; start + S <= capacity; every pointer 16-byte aligned.
  */
 int ddq_prefill_rope_kv(const void* qkv, int64_t qkv_stride, void* k_cache, void* v_cache,
                         int64_t cache_batch_stride, int64_t capacity, const float* cos,
-                        const float* sin, int64_t start, void* q_out, int64_t B, int64_t S,
-                        int64_t Hq, int64_t Hkv, int64_t D, void* stream);
+                        const float* sin, int64_t start, void* q_out, void* k_out, void* v_out,
+                        int64_t B, int64_t S, int64_t Hq, int64_t Hkv, int64_t D, void* stream);
 
 /*
  * Residual add + RMSNorm over rows of H (H % 8 == 0, 16-byte aligned rows):

@@ -139,10 +139,12 @@ def test_prefill_rope_kv_is_the_fp32_torch_rope(cuda_device, B, S, nh, nkv, hd, 
     q_ref = rope(qkv[..., : nh * hd].reshape(B, S, nh, hd).transpose(1, 2))
     k_ref = rope(qkv[..., nh * hd:(nh + nkv) * hd].reshape(B, S, nkv, hd).transpose(1, 2))
     v_ref = qkv[..., (nh + nkv) * hd:].reshape(B, S, nkv, hd).transpose(1, 2)
-    q = attention.prefill_rope_kv(qkv, kc, vc, cos, sin, start, nh, nkv, hd)
+    q, k, v = attention.prefill_rope_kv(qkv, kc, vc, cos, sin, start, nh, nkv, hd, kv_out=True)
     torch.cuda.synchronize()
-    assert q.shape == (B, S, nh, hd)
+    assert q.shape == (B, S, nh, hd) and k.shape == v.shape == (B, S, nkv, hd)
     assert torch.equal(q.transpose(1, 2), q_ref)
+    assert torch.equal(k.transpose(1, 2), k_ref) and torch.equal(v.transpose(1, 2), v_ref)
+    assert torch.equal(attention.prefill_rope_kv(qkv, kc, vc, cos, sin, start, nh, nkv, hd), q)
     assert torch.equal(kc[:, :, start:start + S], k_ref)
     assert torch.equal(vc[:, :, start:start + S], v_ref)
     # rows outside the chunk are untouched
