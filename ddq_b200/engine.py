@@ -131,7 +131,7 @@ class Engine:
         hd = cfg.head_dim
         inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, hd, 2, dtype=torch.float32) / hd))
         self._inv_freq = inv.to(self.device)
-        self._split_bufs: dict = {}   # (tokens, hidden) -> reusable split-activation buffers
+        self._split_bufs: dict = {}   # (tokens, hidden, stream) -> reusable split buffers
         self._rope_cache = {}
         self._graphs = {}
 
@@ -313,7 +313,9 @@ class Engine:
         B, S, H = x.shape
         hd, nh, nkv = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads
         eps = cfg.rms_norm_eps
-        bufs = self._split_bufs.setdefault((B, H), [None, None])
+        # per stream: decode chains on different streams may run at the same time
+        key = (B, H, torch.cuda.current_stream(x.device).cuda_stream)
+        bufs = self._split_bufs.setdefault(key, [None, None])
         x, bufs[0] = norm.add_rmsnorm_split(x.contiguous(), L["in_norm"], eps, delta, bufs[0])
         p = L["qkv"]
         qkv = gemm_fp8.f8_forward_planes(bufs[0], p.wq, p.scales, p.bias)

@@ -39,12 +39,14 @@ def _stream_ptr(device: torch.device) -> int:
 
 
 def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    """Zero-filled per-device scratch, grown on demand and then reused.
+    """Zero-filled scratch per (device, current stream), grown on demand and
+    then reused.
 
     The kernels leave the counters in it at zero after each call, so one
-    workspace serves every call ordered on a stream.
+    workspace serves every call ordered on a stream; calls running on
+    different streams at the same time get different workspaces.
     """
-    key = (device.type, device.index)
+    key = (device.type, device.index, torch.cuda.current_stream(device).cuda_stream)
     buf = _workspaces.get(key)
     if buf is None or buf.numel() < nbytes:
         buf = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)

@@ -9,6 +9,11 @@ on a sleep kernel so that every launch is queued before the first one runs
 and the events time the GPU alone.  Prints one JSON line.
 
     python -m ddq_b200.profile --m 64 --n 9728 --k 896 --iters 50
+
+With ``--attention`` it times the decode-step attention kernel instead
+(``ddq_decode_attention`` at the engine's shapes, rotating KV-cache copies):
+
+    python -m ddq_b200.profile --attention --batch 64 --pos 640 --iters 20
 """
 from __future__ import annotations
 
@@ -18,12 +23,66 @@ import math
 
 import torch
 
-from . import _lib, gemm_fp8, lm_head
+from . import _lib, attention, gemm_fp8, lm_head
 
 
 def algorithmic_bytes(M, N, K, bias=False, lm=False):
     out = 8 * M if lm else 2 * M * N
     return N * K + 4 * N + (4 * N if bias else 0) + 2 * M * K + out
+
+
+def attention_bytes(B, Hq, Hkv, D, pos):
+    """K and V rows 0..pos read, q/k/v in, o out, the new K/V row written."""
+    return (2 * B * Hkv * (pos + 1) * D * 2 + B * (Hq + 2 * Hkv) * D * 2 + B * Hq * D * 2
+            + 2 * B * Hkv * D * 2)
+
+
+def run_attention(a, dev):
+    B, Hq, Hkv, D, cap, pos = a.batch, a.heads, a.kv_heads, a.head_dim, a.cap, a.pos
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    per = 2 * B * Hkv * cap * D * 2
+    copies = a.copies or max(2, math.ceil(2.2 * l2 / per))
+    g = torch.Generator(device=dev).manual_seed(0)
+    caches = [(torch.randn(B, Hkv, cap, D, generator=g, device=dev).half(),
+               torch.randn(B, Hkv, cap, D, generator=g, device=dev).half()) for _ in range(copies)]
+    qkv = torch.randn(B, (Hq + 2 * Hkv) * D, generator=g, device=dev).half()
+    inv = 1.0 / (1e6 ** (torch.arange(0, D, 2, dtype=torch.float32, device=dev) / D))
+    f = float(pos) * inv
+    cos, sin = torch.cat([f, f]).cos(), torch.cat([f, f]).sin()
+    p = torch.tensor([pos], dtype=torch.int64, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def launch(i):
+        kc, vc = caches[i % copies]
+        attention.decode_attention(qkv, kc, vc, cos, sin, p, Hq, Hkv, D, D ** -0.5)
+
+    for i in range(a.warmup):
+        launch(i)
+    torch.cuda.synchronize(dev)
+    torch.cuda._sleep(int(2e8))  # every launch below is queued before the first runs
+    if a.chain:
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(stream)
+        for i in range(a.iters):
+            launch(a.warmup + i)
+        c1.record(stream)
+        torch.cuda.synchronize(dev)
+        t = [c0.elapsed_time(c1) * 1e3 / a.iters]
+    else:
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(a.iters)]
+        for i, (e0, e1) in enumerate(evs):
+            e0.record(stream)
+            launch(a.warmup + i)
+            e1.record(stream)
+        torch.cuda.synchronize(dev)
+        t = sorted(e0.elapsed_time(e1) * 1e3 for e0, e1 in evs)
+    med = t[len(t) // 2]
+    nb = attention_bytes(B, Hq, Hkv, D, pos)
+    print(json.dumps({"kernel": "decode_attention", "B": B, "Hq": Hq, "Hkv": Hkv, "D": D,
+                      "pos": pos, "cap": cap, "copies": copies,
+                      "mode": "chain" if a.chain else "events", "us_median": round(med, 3),
+                      "bytes": nb, "gbs_median": round(nb / (med * 1e-6) / 1e9, 1)}))
 
 
 def main(argv=None):
@@ -44,8 +103,19 @@ def main(argv=None):
                     help="time a trivial one-thread kernel instead (launch + event floor)")
     ap.add_argument("--trace", action="store_true",
                     help="also run one launch with the per-CTA phase trace and summarise it")
+    ap.add_argument("--attention", action="store_true",
+                    help="time the decode-step attention kernel instead of a GEMM")
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--pos", type=int, default=640)
+    ap.add_argument("--cap", type=int, default=768)
+    ap.add_argument("--heads", type=int, default=14)
+    ap.add_argument("--kv-heads", type=int, default=2)
+    ap.add_argument("--head-dim", type=int, default=64)
     a = ap.parse_args(argv)
     dev = torch.device("cuda", torch.cuda.current_device())
+    if a.attention:
+        run_attention(a, dev)
+        return
     L = _lib.load()
     M, N, K = a.m, a.n, a.k
     l2 = torch.cuda.get_device_properties(dev).L2_cache_size

@@ -232,3 +232,25 @@ def test_decode_calls_of_many_shapes_share_one_workspace(g):
         torch.cuda.synchronize()
         err = o.normwise_rel_err(y.cpu().numpy(), o.f8_forward(x, wq, s, b))
         assert err <= TIGHT, (M, N, K, err)
+
+
+def test_concurrent_streams_get_their_own_workspace(cuda_device):
+    """Decode GEMMs issued on two streams at once (each with its own activation
+    planes in a workspace) must not share scratch: both results equal the
+    single-stream ones."""
+    from ddq_b200 import gemm_fp8
+    g = torch.Generator(device="cuda").manual_seed(21)
+    wq, s = gemm_fp8.quantize(torch.randn(4864, 896, generator=g, device="cuda") * 0.02)
+    xs = [torch.randn(16, 896, generator=g, device="cuda").half() for _ in range(2)]
+    ref = [gemm_fp8.f8_forward(x, wq, s) for x in xs]
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    outs = [[], []]
+    torch.cuda.synchronize()
+    for _ in range(20):
+        for i in range(2):
+            with torch.cuda.stream(streams[i]):
+                outs[i].append(gemm_fp8.f8_forward(xs[i], wq, s))
+    torch.cuda.synchronize()
+    for i in range(2):
+        for y in outs[i]:
+            assert torch.equal(y, ref[i])
