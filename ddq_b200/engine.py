@@ -132,6 +132,10 @@ class Engine:
         inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, hd, 2, dtype=torch.float32) / hd))
         self._inv_freq = inv.to(self.device)
         self._split_bufs: dict = {}   # (tokens, hidden, stream) -> reusable split buffers
+        # decode steps of >= 32 sequences run as this many independent slices
+        # on their own streams (the step is latency-bound; the slices overlap)
+        self.decode_chains = 2
+        self._chain_streams: List[torch.cuda.Stream] = []
         self._rope_cache = {}
         self._graphs = {}
 
@@ -350,6 +354,30 @@ class Engine:
             x, delta = self._layer(li, x, delta, cache, b0, cos, sin, pos, start)
         return self.add_rmsnorm(x, self.final_norm, delta)[1]
 
+    def decode_hidden(self, tok: torch.Tensor, cache: KVCache, pos: torch.Tensor) -> torch.Tensor:
+        """Final-normed hidden state [B, H] of one decode step of tok [B, 1] at
+        `pos`.  With `decode_chains` > 1 and at least 32 sequences, the batch is
+        cut into that many slices, each run on its own stream; the sequences are
+        independent, so only the streams' joins order them."""
+        B = tok.shape[0]
+        n = self.decode_chains
+        if n <= 1 or B < 32 or B % n:
+            return self.hidden(tok, cache, 0, 0, pos)[:, -1, :]
+        per = B // n
+        main = torch.cuda.current_stream(self.device)
+        while len(self._chain_streams) < n:
+            self._chain_streams.append(torch.cuda.Stream(self.device))
+        streams = self._chain_streams[:n]
+        outs = []
+        for i, s in enumerate(streams):
+            s.wait_stream(main)
+            with torch.cuda.stream(s):
+                outs.append(self.hidden(tok[i * per:(i + 1) * per], cache, i * per, 0,
+                                        pos)[:, -1, :])
+        for s in streams:
+            main.wait_stream(s)
+        return torch.cat(outs)
+
     def greedy(self, h: torch.Tensor) -> torch.Tensor:
         """Greedy token of each row of h [M, H] (fused lm_head argmax, or the oracle)."""
         if self.linear_kind == "fp8":
@@ -398,8 +426,7 @@ class Engine:
         nxt = torch.empty(B, dtype=torch.int64, device=self.device)
 
         def step():
-            h = self.hidden(tok, cache, 0, 0, pos)
-            nxt.copy_(self.greedy(h[:, -1, :]))
+            nxt.copy_(self.greedy(self.decode_hidden(tok, cache, pos)))
 
         graph = None
         if use_graph and self.linear_kind == "fp8":
