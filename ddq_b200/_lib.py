@@ -27,6 +27,10 @@ _SIGNATURES = {
     "ddq_w8a16_gemm_swiglu_workspace_size": (ctypes.c_size_t, [_c_int64, _c_int64, _c_int64]),
     "ddq_w8a16_gemm_swiglu": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, _vp, _c_int64,
                                              _c_int64, _c_int64, _vp, ctypes.c_size_t, _vp]),
+    "ddq_decode_attention_split": (ctypes.c_int, [_vp, _c_int64, _vp, _vp, _c_int64, _c_int64,
+                                                  _vp, _vp, _vp, _vp, _c_int64, _vp, _vp,
+                                                  _c_int64, _c_int64, _c_int64, _c_int64,
+                                                  ctypes.c_float, _vp]),
     "ddq_prefill_rope_kv": (ctypes.c_int, [_vp, _c_int64, _vp, _vp, _c_int64, _c_int64, _vp, _vp,
                                            _c_int64, _vp, _vp, _vp, _c_int64, _c_int64, _c_int64,
                                            _c_int64, _c_int64, _vp]),

@@ -12,17 +12,13 @@ from __future__ import annotations
 
 import torch
 
+from typing import Optional
+
 from . import _lib
+from .norm import SplitActivations
 
 
-def decode_attention(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
-                     cos: torch.Tensor, sin: torch.Tensor, pos: torch.Tensor,
-                     num_heads: int, num_kv_heads: int, head_dim: int,
-                     scale: float) -> torch.Tensor:
-    """qkv fp16 [B, (Hq + 2 Hkv) * D] (one token per sequence); k_cache/v_cache
-    fp16 [B, Hkv, capacity, D] (batch dim may be strided); cos/sin fp32 [D] for
-    this position; pos int64 [1] on the device.  Returns o fp16 [B, Hq * D] and
-    updates the caches at ``pos``."""
+def _check_decode(qkv, k_cache, v_cache, cos, sin, pos, num_heads, num_kv_heads, head_dim):
     def need(cond, msg):
         if not cond:
             raise RuntimeError(msg)
@@ -44,6 +40,19 @@ def decode_attention(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Te
          cos.numel() == head_dim and sin.numel() == head_dim, "decode_attention: fp32 cos/sin [D]")
     need(pos.is_cuda and pos.dtype == torch.int64 and pos.numel() == 1,
          "decode_attention: pos must be an int64 CUDA scalar")
+    return B, cos, sin
+
+
+def decode_attention(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                     cos: torch.Tensor, sin: torch.Tensor, pos: torch.Tensor,
+                     num_heads: int, num_kv_heads: int, head_dim: int,
+                     scale: float) -> torch.Tensor:
+    """qkv fp16 [B, (Hq + 2 Hkv) * D] (one token per sequence); k_cache/v_cache
+    fp16 [B, Hkv, capacity, D] (batch dim may be strided); cos/sin fp32 [D] for
+    this position; pos int64 [1] on the device.  Returns o fp16 [B, Hq * D] and
+    updates the caches at ``pos``."""
+    B, cos, sin = _check_decode(qkv, k_cache, v_cache, cos, sin, pos, num_heads, num_kv_heads,
+                                head_dim)
     out = torch.empty((B, num_heads * head_dim), dtype=torch.float16, device=qkv.device)
     with torch.cuda.device(qkv.device):
         st = _lib.load().ddq_decode_attention(
@@ -53,6 +62,33 @@ def decode_attention(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Te
             torch.cuda.current_stream(qkv.device).cuda_stream)
     _lib.check(st, "decode_attention")
     return out
+
+
+def decode_attention_split(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                           cos: torch.Tensor, sin: torch.Tensor, pos: torch.Tensor,
+                           num_heads: int, num_kv_heads: int, head_dim: int, scale: float,
+                           act: Optional[SplitActivations] = None, with_out: bool = False):
+    """``decode_attention`` whose output is the o projection's operand
+    (``ddq_decode_attention_split``): o's three e4m3 planes and token scales,
+    for ``gemm_fp8.f8_forward_planes``, bit for bit what the GEMM's own split
+    of fp16 o gives.  ``act`` reuses buffers of the same shape; ``with_out``
+    also returns fp16 o.  Returns (act, o or None)."""
+    B, cos, sin = _check_decode(qkv, k_cache, v_cache, cos, sin, pos, num_heads, num_kv_heads,
+                                head_dim)
+    K = num_heads * head_dim
+    if act is None or act.M != B or act.H != K:
+        act = SplitActivations(torch.empty((3, B, K), dtype=torch.uint8, device=qkv.device),
+                               torch.empty((B,), dtype=torch.float32, device=qkv.device), B, K)
+    out = torch.empty((B, K), dtype=torch.float16, device=qkv.device) if with_out else None
+    with torch.cuda.device(qkv.device):
+        st = _lib.load().ddq_decode_attention_split(
+            qkv.data_ptr(), qkv.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
+            k_cache.stride(0), k_cache.shape[2], cos.data_ptr(), sin.data_ptr(), pos.data_ptr(),
+            out.data_ptr() if out is not None else None, K, act.planes.data_ptr(),
+            act.xscale.data_ptr(), B, num_heads, num_kv_heads, head_dim, float(scale),
+            torch.cuda.current_stream(qkv.device).cuda_stream)
+    _lib.check(st, "decode_attention_split")
+    return act, out
 
 
 def prefill_rope_kv(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,

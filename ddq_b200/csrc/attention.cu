@@ -52,6 +52,8 @@ struct AtArgs {
   int Hq, Hkv;
   float scale;
   int trace;             // debug flag bit 1: phase stamps (see ddq_read_trace)
+  uint8_t* planes;       // split output: three e4m3 planes [3][B][Hq * D] (or null)
+  float* xscale;         // and the token scales 2^-e [B]
 };
 
 template <int D>
@@ -273,7 +275,10 @@ struct AmSmem {
   __align__(16) __half knew[64];  // the new cache row (patched into its chunk's tile)
   __align__(16) __half vnew[64];
   float m[AM_NW][AT_GMAX], l[AM_NW][AT_GMAX];
+  float amax_w[AM_NW];   // split output: each head's |o| maximum
+  float amax_r[8];       // and each CTA's of the cluster (one per KV head)
   unsigned long long full[AM_NW * AM_DEPTH];
+  unsigned long long bar_amax;  // the other CTAs' maxima have arrived
   int abort_flag;
 };
 
@@ -308,7 +313,13 @@ __device__ __forceinline__ uint32_t am_h2(float a, float b) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-template <int G>
+// SPLIT: instead of (or besides) fp16 o, emit the o projection's B operand:
+// the three e4m3 planes of the token's o row under a power-of-two scale, as
+// the decode GEMM's split pre-pass would make them from fp16 o.  The row of a
+// token spans its Hkv CTAs, launched as one cluster: each pushes its |o|
+// maximum to the others (4 bytes into their shared memory, counted on their
+// barrier) and splits its own heads.
+template <int G, bool SPLIT>
 __global__ void __launch_bounds__(AM_NW * 32, 1)
     decode_attention_mma_kernel(const __grid_constant__ CUtensorMap tm_k,
                                 const __grid_constant__ CUtensorMap tm_v, const AtArgs a,
@@ -327,6 +338,10 @@ __global__ void __launch_bounds__(AM_NW * 32, 1)
   __half* vc = a.vc + (size_t)b * a.cache_bstride + (size_t)g * a.cap * D;
   if (threadIdx.x == 0) {
     for (int s = 0; s < AM_NW * AM_DEPTH; ++s) ptx::mbar_init(ptx::smem_u32(&sm.full[s]), 1);
+    if (SPLIT) {
+      ptx::mbar_init(ptx::smem_u32(&sm.bar_amax), 1);
+      ptx::mbar_arrive_expect_tx(ptx::smem_u32(&sm.bar_amax), (uint32_t)(4 * (a.Hkv - 1)));
+    }
     sm.abort_flag = 0;
     ptx::fence_mbar_init();
     ptx::prefetch_tmap(&tm_k);
@@ -375,6 +390,9 @@ __global__ void __launch_bounds__(AM_NW * 32, 1)
   const int last = nchunks - 1;  // the chunk that holds the new row
   const uint32_t ring0 = ptx::smem_u32(&sm.ring[0][0][0]);
   __syncthreads();  // barriers initialised
+  // split output: the cluster's barriers are ready before any CTA pushes
+  // (the matching wait comes after the merge)
+  if (SPLIT) ptx::cluster_arrive_relaxed();
 
   auto issue = [&](int c) {  // chunk c into its slot of this warp's ring
     const int s = warp * AM_DEPTH + (c / AM_NW) % AM_DEPTH;
@@ -560,6 +578,7 @@ __global__ void __launch_bounds__(AM_NW * 32, 1)
   // warp h merges head h: lane w < 8 holds warp w's max and sum, every lane
   // two head dimensions; the weights are summed in warp order
   static_assert(AT_GMAX <= AM_NW, "one warp per query head in the merge");
+  float2 oz = make_float2(0.f, 0.f);  // this lane's two fp16-rounded o values (split output)
   if (warp < G) {
     const int h = warp;
     const float mw = lane < AM_NW ? sm.m[lane][h] : -FLT_MAX;
@@ -579,13 +598,68 @@ __global__ void __launch_bounds__(AM_NW * 32, 1)
       n0 = fmaf(av.x, c, n0);
       n1 = fmaf(av.y, c, n1);
     }
-    __half* dst = a.out + (size_t)b * a.out_stride + (size_t)(g * G + h) * D + 2 * lane;
     const __half2 o2 = __floats2half2_rn(n0 / den, n1 / den);
-    if ((reinterpret_cast<uintptr_t>(dst) & 3u) == 0) {
-      *reinterpret_cast<__half2*>(dst) = o2;
-    } else {  // caller's output row stride is odd
-      dst[0] = __low2half(o2);
-      dst[1] = __high2half(o2);
+    if (a.out) {
+      __half* dst = a.out + (size_t)b * a.out_stride + (size_t)(g * G + h) * D + 2 * lane;
+      if ((reinterpret_cast<uintptr_t>(dst) & 3u) == 0) {
+        *reinterpret_cast<__half2*>(dst) = o2;
+      } else {  // caller's output row stride is odd
+        dst[0] = __low2half(o2);
+        dst[1] = __high2half(o2);
+      }
+    }
+    if (SPLIT) {
+      oz = __half22float2(o2);
+      const float am = warp_max(fmaxf(fabsf(oz.x), fabsf(oz.y)));
+      if (lane == 0) sm.amax_w[warp] = am;
+    }
+  }
+  if (SPLIT) {
+    // ---- the o projection's operand: row maximum over the cluster, then
+    // the same three-plane split as the GEMM's pre-pass, on fp16 o
+    __syncthreads();
+    ptx::cluster_wait();
+    const uint32_t rank = ptx::cluster_ctarank();
+    const uint32_t bar = ptx::smem_u32(&sm.bar_amax);
+    if (threadIdx.x == 0) {
+      float cta = 0.f;
+      for (int w = 0; w < G; ++w) cta = fmaxf(cta, sm.amax_w[w]);
+      sm.amax_r[rank] = cta;
+      const uint32_t slot = ptx::smem_u32(&sm.amax_r[rank]);
+      for (int r = 0; r < a.Hkv; ++r)
+        if (r != (int)rank)
+          ptx::st_async_b32(ptx::mapa_shared(slot, (uint32_t)r), __float_as_uint(cta),
+                            ptx::mapa_shared(bar, (uint32_t)r));
+    }
+    __syncthreads();
+    // never skipped: no CTA may leave while another can still store into it
+    // (after an abort this is a bounded drain)
+    bool got = a.Hkv == 1 || ptx::mbar_wait_cluster(bar, 0u, timeout_ns, &sm.abort_flag);
+    if (!got) {
+      const long long t0 = clock64();
+      while (!ptx::mbar_try_wait_cluster(bar, 0u)) {
+        if (clock64() - t0 > (long long)(timeout_ns * 2ull)) break;
+      }
+    }
+    if (got && warp < G) {
+      float amax = 0.f;
+      for (int r = 0; r < a.Hkv; ++r) amax = fmaxf(amax, sm.amax_r[r]);
+      const int e = split_shift(amax);
+      const float up = ldexpf(1.f, e);
+      const float z0 = oz.x * up, z1 = oz.y * up;  // exact: power-of-two scale
+      const uint16_t b1 = float2_to_e4m3x2(z0, z1);
+      const float2 d1 = e4m3x2_to_float2(b1);
+      const float r0 = z0 - d1.x, r1 = z1 - d1.y;
+      const uint16_t b2 = float2_to_e4m3x2(r0, r1);
+      const float2 d2 = e4m3x2_to_float2(b2);
+      const uint16_t b3 = float2_to_e4m3x2(r0 - d2.x, r1 - d2.y);
+      const size_t K = (size_t)a.Hq * D;
+      const size_t plane = (size_t)gridDim.x / a.Hkv * K;
+      uint8_t* dst = a.planes + (size_t)b * K + (size_t)(g * G + warp) * D + 2 * lane;
+      *reinterpret_cast<uint16_t*>(dst) = b1;
+      *reinterpret_cast<uint16_t*>(dst + plane) = b2;
+      *reinterpret_cast<uint16_t*>(dst + 2 * plane) = b3;
+      if (rank == 0 && threadIdx.x == 0) a.xscale[b] = ldexpf(1.f, -e);
     }
   }
   if (threadIdx.x == 0 && sm.abort_flag) record_device_error(DDQ_ERR_TIMEOUT);
@@ -624,24 +698,33 @@ int at_cache_map(CUtensorMap* m, const void* base, int cap, int Hkv, int B, int6
 
 int launch_decode_attention(const __half* qkv, int64_t qkv_stride, __half* kc, __half* vc,
                             int64_t cache_bstride, int cap, const float* cos, const float* sin,
-                            const int64_t* pos, __half* out, int64_t out_stride, int B, int Hq,
-                            int Hkv, int D, float scale, unsigned long long timeout_ns,
-                            int debug_flags, cudaStream_t s) {
+                            const int64_t* pos, __half* out, int64_t out_stride, uint8_t* planes,
+                            float* xscale, int B, int Hq, int Hkv, int D, float scale,
+                            unsigned long long timeout_ns, int debug_flags, cudaStream_t s) {
   if (B < 1 || Hkv < 1 || Hq < Hkv || Hq % Hkv != 0 || Hq / Hkv > AT_GMAX || cap < 1)
     return DDQ_ERR_SHAPE;
   if (D != 64 && D != 128) return DDQ_ERR_SHAPE;
+  const bool split = planes != nullptr;
+  // the split output: 64-wide heads, one cluster of Hkv CTAs per token (portable size)
+  if (split && (D != 64 || Hkv > 8 || !xscale)) return DDQ_ERR_SHAPE;
+  if (!split && !out) return DDQ_ERR_INVALID_ARGUMENT;
   if (!aligned16(kc) || !aligned16(vc) || (cache_bstride % 8) != 0) return DDQ_ERR_ALIGNMENT;
+  if (split && !aligned16(planes)) return DDQ_ERR_ALIGNMENT;
   AtArgs a{qkv, qkv_stride, kc, vc, cache_bstride, cap, cos, sin, pos, out, out_stride, Hq, Hkv,
-           scale, (debug_flags & 2) != 0 ? 1 : 0};
+           scale, (debug_flags & 2) != 0 ? 1 : 0, planes, xscale};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(B * Hkv));
   cfg.blockDim = dim3(at_warps(D) * 32);
   cfg.stream = s;
-  cudaLaunchAttribute at;
-  at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at.val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
-  cfg.attrs = &at;
-  cfg.numAttrs = 1;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  at[1].id = cudaLaunchAttributeClusterDimension;
+  at[1].val.clusterDim.x = (unsigned)Hkv;
+  at[1].val.clusterDim.y = 1;
+  at[1].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = split ? 2 : 1;
   cudaError_t e;
   if (D == 64) {
     // TMA-streamed tensor-core variant (the cache must be 16-byte aligned per batch)
@@ -652,21 +735,27 @@ int launch_decode_attention(const __half* qkv, int64_t qkv_stride, __half* kc, _
     if (st) return st;
     const int dev = current_device();
     if (dev < 0 || dev >= 64) return DDQ_ERR_DEVICE;
-    static bool attr_set[AT_GMAX][64] = {};
+    static bool attr_set[2][AT_GMAX][64] = {};
     const int smem = (int)sizeof(AmSmem) + 1024;
     cfg.blockDim = dim3(AM_NW * 32);
     cfg.dynamicSmemBytes = smem;
+    auto go = [&](auto kern, int gi) -> int {
+      if (!attr_set[split][gi][dev]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+            cudaSuccess)
+          return DDQ_ERR_LAUNCH;
+        attr_set[split][gi][dev] = true;
+      }
+      e = cudaLaunchKernelEx(&cfg, kern, tk, tv, a, timeout_ns);
+      return DDQ_OK;
+    };
+    int rc = DDQ_OK;
     switch (Hq / Hkv) {
-#define DDQ_AT_G(G_)                                                                     \
-  case G_:                                                                               \
-    if (!attr_set[G_ - 1][dev]) {                                                        \
-      if (cudaFuncSetAttribute(decode_attention_mma_kernel<G_>,                          \
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=     \
-          cudaSuccess)                                                                   \
-        return DDQ_ERR_LAUNCH;                                                           \
-      attr_set[G_ - 1][dev] = true;                                                      \
-    }                                                                                    \
-    e = cudaLaunchKernelEx(&cfg, decode_attention_mma_kernel<G_>, tk, tv, a, timeout_ns); \
+#define DDQ_AT_G(G_)                                                                          \
+  case G_:                                                                                    \
+    rc = split ? go(decode_attention_mma_kernel<G_, true>, G_ - 1)                            \
+               : go(decode_attention_mma_kernel<G_, false>, G_ - 1);                          \
+    if (rc) return rc;                                                                        \
     break;
       DDQ_AT_G(1) DDQ_AT_G(2) DDQ_AT_G(3) DDQ_AT_G(4)
       DDQ_AT_G(5) DDQ_AT_G(6) DDQ_AT_G(7) DDQ_AT_G(8)

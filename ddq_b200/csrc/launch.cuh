@@ -60,9 +60,9 @@ int launch_prefill_rope_kv(const __half* qkv, int64_t qkv_stride, __half* kc, __
 // Decode-step attention with RoPE and the KV-cache write fused (attention.cu).
 int launch_decode_attention(const __half* qkv, int64_t qkv_stride, __half* kc, __half* vc,
                             int64_t cache_bstride, int cap, const float* cos, const float* sin,
-                            const int64_t* pos, __half* out, int64_t out_stride, int B, int Hq,
-                            int Hkv, int D, float scale, unsigned long long timeout_ns,
-                            int debug_flags, cudaStream_t s);
+                            const int64_t* pos, __half* out, int64_t out_stride, uint8_t* planes,
+                            float* xscale, int B, int Hq, int Hkv, int D, float scale,
+                            unsigned long long timeout_ns, int debug_flags, cudaStream_t s);
 // Residual add + RMSNorm, optionally followed by the three-plane split of the
 // result for a decode GEMM (norm.cu).
 int launch_add_rmsnorm_split(const __half* x, const __half* delta, const float* w, float eps,

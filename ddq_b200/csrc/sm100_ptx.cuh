@@ -307,6 +307,14 @@ __device__ __forceinline__ void st_async_v4(uint32_t addr, float4 v, uint32_t re
       : "memory");
 }
 
+// 4-byte variant of st_async_v4.
+__device__ __forceinline__ void st_async_b32(uint32_t addr, uint32_t v, uint32_t remote_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(addr),
+      "r"(v), "r"(remote_bar)
+      : "memory");
+}
+
 // As mbar_wait, with cluster-scope acquire: for data that other CTAs of the
 // cluster wrote with st_async_v4.
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {

@@ -319,13 +319,20 @@ class Engine:
         eps = cfg.rms_norm_eps
         # per stream: decode chains on different streams may run at the same time
         key = (B, H, torch.cuda.current_stream(x.device).cuda_stream)
-        bufs = self._split_bufs.setdefault(key, [None, None])
+        bufs = self._split_bufs.setdefault(key, [None, None, None])
         x, bufs[0] = norm.add_rmsnorm_split(x.contiguous(), L["in_norm"], eps, delta, bufs[0])
         p = L["qkv"]
         qkv = gemm_fp8.f8_forward_planes(bufs[0], p.wq, p.scales, p.bias)
-        o = attention.decode_attention(qkv, cache.k[li, b0:b0 + B], cache.v[li, b0:b0 + B],
-                                       cos, sin, pos, nh, nkv, hd, hd ** -0.5)
-        attn = self.linear(o.reshape(B, S, nh * hd), L["o"])
+        if hd == 64 and nkv <= 8:  # attention emits the o projection's operand directly
+            bufs[2], _ = attention.decode_attention_split(
+                qkv, cache.k[li, b0:b0 + B], cache.v[li, b0:b0 + B], cos, sin, pos, nh, nkv, hd,
+                hd ** -0.5, bufs[2])
+            p = L["o"]
+            attn = gemm_fp8.f8_forward_planes(bufs[2], p.wq, p.scales, p.bias).reshape(x.shape)
+        else:
+            o = attention.decode_attention(qkv, cache.k[li, b0:b0 + B], cache.v[li, b0:b0 + B],
+                                           cos, sin, pos, nh, nkv, hd, hd ** -0.5)
+            attn = self.linear(o.reshape(B, S, nh * hd), L["o"])
         x, bufs[1] = norm.add_rmsnorm_split(x, L["post_norm"], eps, attn.contiguous(), bufs[1])
         wq, sc, b = L["gate_up"].gate_up_interleaved()
         z = gemm_fp8.f8_forward_planes(bufs[1], wq, sc, b, swiglu=True)

@@ -155,6 +155,22 @@ int ddq_decode_attention(const void* qkv, int64_t qkv_stride, void* k_cache, voi
                          void* stream);
 
 /*
+ * ddq_decode_attention with the o projection's operand as its output: the
+ * three e4m3 planes [3][B][Hq * D] of each token's o row under a power-of-two
+ * scale and the token scales 2^-e [B] (xscale), exactly as the decode GEMM's
+ * split pre-pass makes them from fp16 o, for ddq_w8a16_gemm_planes.  No
+ * reference counterpart (it removes the pre-pass between attention and the o
+ * projection).  out (fp16 o) is optional (NULL: not written).  D = 64,
+ * Hkv <= 8 (the Hkv CTAs of a token run as one thread-block cluster); planes
+ * 16-byte aligned.
+ */
+int ddq_decode_attention_split(const void* qkv, int64_t qkv_stride, void* k_cache, void* v_cache,
+                               int64_t cache_batch_stride, int64_t capacity, const float* cos,
+                               const float* sin, const int64_t* pos, void* out,
+                               int64_t out_stride, uint8_t* planes, float* xscale, int64_t B,
+                               int64_t Hq, int64_t Hkv, int64_t D, float scale, void* stream);
+
+/*
  * Prefill rotary embedding and KV-cache write for a chunk of S tokens per
  * sequence starting at cache position `start`.  Replaces, for a prefill
  * chunk, the RoPE kernel on q and k (RoPe_d.cu:12-68, called from

@@ -151,3 +151,34 @@ def test_prefill_rope_kv_is_the_fp32_torch_rope(cuda_device, B, S, nh, nkv, hd, 
     assert torch.equal(kc[:, :, :start], kc0[:, :, :start])
     assert torch.equal(kc[:, :, start + S:], kc0[:, :, start + S:])
     assert torch.equal(vc[:, :, start + S:], vc0[:, :, start + S:])
+
+
+@pytest.mark.parametrize("B,nh,nkv,cap,pos", [
+    (64, 14, 2, 768, 600), (3, 16, 8, 100, 57), (5, 4, 1, 40, 31), (2, 6, 2, 1100, 1099)])
+def test_decode_attention_split_feeds_the_o_projection_exactly(cuda_device, B, nh, nkv, cap, pos):
+    """ddq_decode_attention_split: its fp16 o equals ddq_decode_attention's, and the
+    o projection on its planes equals the o projection on fp16 o bit for bit
+    (the GEMM's own split pre-pass of o)."""
+    from ddq_b200 import attention, gemm_fp8
+    hd = 64
+    g = torch.Generator(device="cuda").manual_seed(B * 7 + pos)
+    qkv = torch.randn(B, (nh + 2 * nkv) * hd, generator=g, device="cuda").half()
+    kc = torch.randn(B, nkv, cap, hd, generator=g, device="cuda").half()
+    vc = torch.randn(B, nkv, cap, hd, generator=g, device="cuda").half()
+    inv = 1.0 / (1e6 ** (torch.arange(0, hd, 2, dtype=torch.float32, device="cuda") / hd))
+    f = float(pos) * inv
+    cos, sin = torch.cat([f, f]).cos(), torch.cat([f, f]).sin()
+    p = torch.tensor([pos], dtype=torch.int64, device="cuda")
+    o = attention.decode_attention(qkv, kc, vc, cos, sin, p, nh, nkv, hd, 0.125)
+    act, o2 = attention.decode_attention_split(qkv, kc, vc, cos, sin, p, nh, nkv, hd, 0.125,
+                                               with_out=True)
+    act_only, none = attention.decode_attention_split(qkv, kc, vc, cos, sin, p, nh, nkv, hd,
+                                                      0.125)
+    torch.cuda.synchronize()
+    assert none is None and torch.equal(o, o2)
+    assert torch.equal(act.planes, act_only.planes) and torch.equal(act.xscale, act_only.xscale)
+    wq, s = gemm_fp8.quantize(torch.randn(896, nh * hd, generator=g, device="cuda") * 0.02)
+    y_ref = gemm_fp8.f8_forward(o, wq, s)
+    y = gemm_fp8.f8_forward_planes(act, wq, s)
+    torch.cuda.synchronize()
+    assert torch.equal(y, y_ref)
