@@ -103,7 +103,7 @@ extern "C" size_t ddq_w8a16_gemm_workspace_size(int64_t M, int64_t N, int64_t K)
   const int dev = current_device();
   const int sms = dev >= 0 ? device_sm_count(dev) : -1;
   if (M <= kDecodeMaxM) return dec_plan(M, N, K, sms > 0 ? sms : 148).ws_bytes;
-  if (pf_shape(M, N)) return pf_workspace_bytes(N, K);
+  if (pf_shape(M, N)) return 2 * pf_workspace_bytes(N, K);  // two alternating buffers
   return tc_plan(M, N, K, sms > 0 ? sms : 148).ws_bytes;
 }
 
@@ -142,7 +142,7 @@ extern "C" size_t ddq_w8a16_gemm_swiglu_workspace_size(int64_t M, int64_t I, int
   const int dev = current_device();
   const int sms = dev >= 0 ? device_sm_count(dev) : -1;
   if (M <= kDecodeMaxM) return dec_plan(M, 2 * I, K, sms > 0 ? sms : 148, true).ws_bytes;
-  return pf_workspace_bytes(2 * I, K);
+  return 2 * pf_workspace_bytes(2 * I, K);  // two alternating buffers
 }
 
 extern "C" int ddq_w8a16_gemm_swiglu(const void* x, const uint8_t* wq_gu, const float* scales_gu,

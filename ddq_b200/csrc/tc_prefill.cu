@@ -31,6 +31,7 @@
 
 #include <cstring>
 #include <mutex>
+#include <unordered_map>
 
 #include "common.cuh"
 #include "launch.cuh"
@@ -112,10 +113,16 @@ __device__ __forceinline__ void pf_expand16(const uint4& v, uint4* dst) {
   dst[1] = make_uint4(h[4], h[5], h[6], h[7]);
 }
 
+// early: w16 is a buffer the previous GEMM does not read (consecutive calls
+// alternate two), so the expansion runs before the grid dependency resolves
+// and only waits before it exits (its completion then still implies the
+// previous kernel's).  Otherwise w16 may still be read by the previous GEMM:
+// wait first.
 __global__ void __launch_bounds__(256) e4m3_to_f16_kernel(const uint8_t* __restrict__ wq,
-                                                          __half* __restrict__ w16, size_t n16) {
+                                                          __half* __restrict__ w16, size_t n16,
+                                                          int early) {
   ptx::pdl_launch_dependents();
-  ptx::pdl_wait();  // w16 may still be read by the previous GEMM
+  if (!early) ptx::pdl_wait();
   const uint4* src = reinterpret_cast<const uint4*>(wq);
   uint4* dst = reinterpret_cast<uint4*>(w16);
   const size_t stride = (size_t)gridDim.x * blockDim.x;
@@ -128,6 +135,7 @@ __global__ void __launch_bounds__(256) e4m3_to_f16_kernel(const uint8_t* __restr
     for (int u = 0; u < 4; ++u) pf_expand16(v[u], dst + 2 * (i + u * stride));
   }
   for (; i < n16; i += stride) pf_expand16(__ldcs(src + i), dst + 2 * i);
+  if (early) ptx::pdl_wait();
 }
 
 // SWIGLU: the weight is a 16-row interleave of gate and up (rows 32 b + i =
@@ -185,12 +193,15 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   if (threadIdx.x == 0) trace_stamp(tr, 1);
-  if (threadIdx.x == 0) ptx::pdl_launch_dependents();
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       ptx::pdl_wait();  // x and w16 come from earlier kernels
+      // dependents launch only now: a following expansion may then write the
+      // other workspace buffer, whose last reader (the GEMM before this one)
+      // has finished once this grid's dependency has resolved
+      ptx::pdl_launch_dependents();
       int g = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
@@ -432,6 +443,36 @@ int pf_pick_bn(int M, int N, int sms) {
 
 size_t pf_workspace_bytes(int64_t N, int64_t K) { return (size_t)N * (size_t)K * 2; }
 
+namespace {
+// Per workspace: which of its two fp16 buffers the next prefill call uses,
+// and whether the call before was a prefill call (only then may this call's
+// expansion write before the previous kernel has finished: a decode-shape
+// call keeps its activation planes at the start of the same workspace).
+struct PfWs {
+  int half = 0;
+  bool last_pf = true;  // nothing has used it yet
+};
+std::mutex g_pf_ws_mu;
+std::unordered_map<const void*, PfWs> g_pf_ws;
+}  // namespace
+
+void ws_note_other_use(const void* ws) {
+  if (!ws) return;
+  std::lock_guard<std::mutex> lock(g_pf_ws_mu);
+  g_pf_ws[ws].last_pf = false;
+}
+
+// The buffer (0 or 1) for this prefill call, and whether its expansion may
+// run ahead of the previous kernel.
+static int pf_take_buffer(const void* ws, bool* early) {
+  std::lock_guard<std::mutex> lock(g_pf_ws_mu);
+  PfWs& st = g_pf_ws[ws];
+  *early = st.last_pf;
+  st.last_pf = true;
+  st.half ^= 1;
+  return st.half;
+}
+
 int launch_pf(const __half* x, const uint8_t* wq, const float* scales, const void* bias,
               int bias_dtype, __half* y, int M, int N, int K, void* ws, size_t ws_bytes,
               unsigned long long timeout_ns, int debug_flags, cudaStream_t s, bool swiglu) {
@@ -444,7 +485,20 @@ int launch_pf(const __half* x, const uint8_t* wq, const float* scales, const voi
       (N % 8) != 0)
     return DDQ_ERR_ALIGNMENT;
   if (swiglu && N % 32 != 0) return DDQ_ERR_SHAPE;
-  __half* w16 = reinterpret_cast<__half*>(ws);
+  // a workspace of two buffers at fixed offsets (0 and half the workspace,
+  // whatever the shape, so that calls of different shapes never overlap):
+  // consecutive calls alternate them, so this call's expansion need not wait
+  // for the previous GEMM
+  const size_t need = pf_workspace_bytes(N, K);
+  const size_t half = (ws_bytes / 2) & ~static_cast<size_t>(255);
+  bool early = false;
+  size_t off = 0;
+  if (need <= half) {
+    off = (size_t)pf_take_buffer(ws, &early) * half;
+  } else {
+    ws_note_other_use(ws);  // the single buffer: always wait for the previous kernel
+  }
+  __half* w16 = reinterpret_cast<__half*>(static_cast<uint8_t*>(ws) + off);
   // 1) exact e4m3 -> fp16 expansion of the weights
   {
     const size_t n16 = (size_t)N * (size_t)K / 16;
@@ -457,7 +511,8 @@ int launch_pf(const __half* x, const uint8_t* wq, const float* scales, const voi
     cudaLaunchAttribute at = pdl_attr();
     cfg.attrs = &at;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, e4m3_to_f16_kernel, wq, w16, n16) != cudaSuccess) {
+    if (cudaLaunchKernelEx(&cfg, e4m3_to_f16_kernel, wq, w16, n16, early ? 1 : 0) !=
+        cudaSuccess) {
       cudaGetLastError();
       return DDQ_ERR_LAUNCH;
     }

@@ -73,8 +73,10 @@ int ddq_quantize_e4m3(const void* w, int w_dtype, int64_t N, int64_t K,
  * Bytes of device workspace ddq_w8a16_gemm needs for this shape (0 if none).
  * Decode shapes (M <= 64) keep the activations split into three e4m3 planes
  * and the per-token scales there; prefill shapes (M >= 128 by default) keep
- * the weight expanded to fp16 (N * K * 2 bytes).  The contents need no
- * initialisation.  One workspace sized for the largest shape serves any
+ * the weight expanded to fp16 (N * K * 2 bytes; the size reported is two such
+ * buffers, which consecutive calls alternate so that a call's expansion does
+ * not wait for the previous GEMM; one buffer also works, without that
+ * overlap).  The contents need no initialisation.  One workspace sized for the largest shape serves any
  * sequence of shapes; calls sharing it must be ordered on one stream.  The
  * pointer must be 256-byte aligned.
  */

@@ -254,3 +254,45 @@ def test_concurrent_streams_get_their_own_workspace(cuda_device):
     for i in range(2):
         for y in outs[i]:
             assert torch.equal(y, ref[i])
+
+
+def test_prefill_and_decode_calls_chained_on_one_workspace(cuda_device):
+    """Prefill-shape calls alternate the two fp16 buffers of a shared workspace
+    and expand their weight before the previous kernel has finished; decode-
+    shape calls keep their planes at the start of the same workspace.  Issued
+    back to back in a mixed order with no synchronisation between them, every
+    result equals the same call made alone."""
+    from ddq_b200 import _lib, gemm_fp8
+    lib = _lib.load()
+    g = torch.Generator(device="cuda").manual_seed(31)
+    shapes = [(512, 1152, 896), (256, 4864, 896), (16, 896, 896), (512, 896, 4864),
+              (1024, 896, 896), (8, 1152, 896), (64, 896, 4864), (384, 9728, 896),
+              (256, 1152, 896), (512, 896, 896)]
+    calls = []
+    for M, N, K in shapes:
+        wq, s = gemm_fp8.quantize(torch.randn(N, K, generator=g, device="cuda") * 0.02)
+        x = torch.randn(M, K, generator=g, device="cuda").half()
+        calls.append((x, wq, s, M, N, K))
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def run(x, wq, s, M, N, K, ws, nbytes):
+        y = torch.empty(M, N, dtype=torch.float16, device="cuda")
+        st = lib.ddq_w8a16_gemm(x.data_ptr(), wq.data_ptr(), s.data_ptr(), None, _lib.DTYPE_NONE,
+                                y.data_ptr(), M, N, K, ws.data_ptr() if ws is not None else None,
+                                nbytes, stream)
+        assert st == 0, _lib.status_string(st)
+        return y
+
+    ref = []
+    for c in calls:  # each alone, with its own workspace, synchronised
+        n = lib.ddq_w8a16_gemm_workspace_size(c[3], c[4], c[5])
+        ws = torch.zeros(max(n, 256), dtype=torch.uint8, device="cuda")
+        ref.append(run(*c, ws, n))
+        torch.cuda.synchronize()
+    need = max(lib.ddq_w8a16_gemm_workspace_size(c[3], c[4], c[5]) for c in calls)
+    ws = torch.zeros(need, dtype=torch.uint8, device="cuda")
+    for rep in range(3):
+        outs = [run(*c, ws, need) for c in calls]   # back to back, one stream
+        torch.cuda.synchronize()
+        for (M, N, K), y, r in zip(shapes, outs, ref):
+            assert torch.equal(y, r), (rep, M, N, K)
