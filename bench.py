@@ -279,7 +279,7 @@ def run_ours(args, rank, world, device):
     torch.cuda.empty_cache()
     prefill = None if args.skip_extra else run_prefill(args, device, world, peaks)
     lmhead = None if args.skip_extra else run_lm_head(args, device, world, peaks)
-    generation = None if args.skip_extra else run_generation(args, device, rank, world)
+    generation = None if args.skip_extra else run_generation(args, device, rank, world, peaks)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -402,7 +402,7 @@ def run_lm_head(args, device, world, peaks):
     return out
 
 
-def run_generation(args, device, rank, world):
+def run_generation(args, device, rank, world, peaks):
     """Config 5: greedy generation, 64 prompts x 512 random ids, 256 new tokens,
     data-parallel replicas (64 / world prompts per GPU), random-init weights."""
     from ddq_b200.engine import Config, Engine
@@ -428,13 +428,26 @@ def run_generation(args, device, rank, world):
     torch.cuda.synchronize(device)
     prefill_ms = reduce_max(e0.elapsed_time(e1), world, device)
     total = per * world * args.gen_new_tokens
+    # one decode step's algorithmic HBM bytes on a GPU: every projection weight
+    # with its scales and biases, the lm_head, and the K/V rows attended to (the
+    # step's mean context, S + new/2 positions)
+    L, Hkv, D = cfg.num_hidden_layers, cfg.num_key_value_heads, cfg.head_dim
+    layer_w = sum(N * K + 4 * N + (4 * N if b else 0) for _, K, N, b in PROJS)
+    lm_w = cfg.vocab_size * cfg.hidden_size + 4 * cfg.vocab_size
+    ctx = args.gen_prompt_len + args.gen_new_tokens / 2
+    kv = L * 2 * per * Hkv * ctx * D * 2
+    step_bytes_gpu = L * layer_w + lm_w + kv
+    step_ms = (ms - prefill_ms) / max(1, args.gen_new_tokens - 1)
     del eng
     torch.cuda.empty_cache()
     return {"workload": f"config5: {per * world} prompts x {args.gen_prompt_len} random ids, "
                         f"{args.gen_new_tokens} greedy tokens, replicas x{world}",
             "tok_s": round(total / (ms * 1e-3), 1), "ms": round(ms, 1),
             "prefill_ms": round(prefill_ms, 1),
-            "decode_ms_per_step": round((ms - prefill_ms) / max(1, args.gen_new_tokens - 1), 3),
+            "decode_ms_per_step": round(step_ms, 3),
+            "decode_step_hbm_bytes_per_gpu": int(step_bytes_gpu),
+            "decode_roofline_frac": round(step_bytes_gpu / (step_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                                          4),
             "tokens": int(total), "checksum": int(toks.sum().item()) % 1000003}
 
 
