@@ -201,6 +201,104 @@ __global__ void __launch_bounds__(256) add_rmsnorm_split_kernel(
   }
 }
 
+// The same with one row per CTA of 128 threads (H <= 2048: at most two
+// 16-byte chunks per thread), for the few rows of a decode step: four times
+// the threads on each row.  The sum of squares is reduced in the one-warp
+// kernels' order (chunk partials; lane L adds chunks L, L + 32, ... in turn,
+// then the same butterfly), so h is bit-identical to add_rmsnorm's.
+constexpr int NR_THREADS = 128;
+__global__ void __launch_bounds__(NR_THREADS) add_rmsnorm_split_row_kernel(
+    const __half* x, const __half* __restrict__ delta, const float* __restrict__ w, float eps,
+    __half* x_out, __half* __restrict__ h, uint8_t* __restrict__ planes,
+    float* __restrict__ xscale, int M, int H) {
+  constexpr int CPT = 2;
+  const int row = blockIdx.x, t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int nch = H / 8;
+  __shared__ float part[32 * NM_REG_CHUNKS];  // per-chunk sums of squares
+  __shared__ float red[2][NR_THREADS / 32];
+  float4 wr[CPT][2];
+#pragma unroll
+  for (int j = 0; j < CPT; ++j) {
+    const int c = t + NR_THREADS * j;
+    if (c < nch) {  // the norm weight does not come from the previous kernel
+      wr[j][0] = __ldg(reinterpret_cast<const float4*>(w + 8 * c));
+      wr[j][1] = __ldg(reinterpret_cast<const float4*>(w + 8 * c) + 1);
+    }
+  }
+  ptx::pdl_wait();
+  ptx::pdl_launch_dependents();
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * H);
+  const uint4* dr = delta ? reinterpret_cast<const uint4*>(delta + (size_t)row * H) : nullptr;
+  uint4* xo = x_out ? reinterpret_cast<uint4*>(x_out + (size_t)row * H) : nullptr;
+  uint4 v[CPT];
+#pragma unroll
+  for (int j = 0; j < CPT; ++j) {
+    const int c = t + NR_THREADS * j;
+    if (c < nch) {
+      v[j] = dr ? nm_add8(xr[c], dr[c]) : xr[c];
+      if (xo) xo[c] = v[j];
+      part[c] = nm_sumsq8(v[j]);
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < NM_REG_CHUNKS; ++j)
+      if (lane + 32 * j < nch) ss += part[lane + 32 * j];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) red[0][0] = ss;
+  }
+  __syncthreads();
+  const float r = rsqrtf(red[0][0] / (float)H + eps);
+  float amax = 0.f;
+#pragma unroll
+  for (int j = 0; j < CPT; ++j) {
+    const int c = t + NR_THREADS * j;
+    if (c < nch) {
+      v[j] = nm_scale8w(v[j], r, wr[j][0], wr[j][1]);
+      if (h) reinterpret_cast<uint4*>(h + (size_t)row * H)[c] = v[j];
+      const __half2* hv = reinterpret_cast<const __half2*>(&v[j]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(hv[i]);
+        amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+      }
+    }
+  }
+  amax = warp_max(amax);
+  if (lane == 0) red[1][warp] = amax;
+  __syncthreads();
+  amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < NR_THREADS / 32; ++i) amax = fmaxf(amax, red[1][i]);
+  const int e = split_shift(amax);
+  const float up = ldexpf(1.f, e);
+  if (t == 0) xscale[row] = ldexpf(1.f, -e);
+  const size_t plane = (size_t)M * H;
+  uint8_t* p1 = planes + (size_t)row * H;
+#pragma unroll
+  for (int j = 0; j < CPT; ++j) {
+    const int c = t + NR_THREADS * j;
+    if (c < nch) {
+      const __half2* hv = reinterpret_cast<const __half2*>(&v[j]);
+      float z[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(hv[i]);
+        z[2 * i] = f.x * up;  // exact: power-of-two scale
+        z[2 * i + 1] = f.y * up;
+      }
+      uint2 a, b, cc;
+      split8(z, a, b, cc);
+      *reinterpret_cast<uint2*>(p1 + (size_t)c * 8) = a;
+      *reinterpret_cast<uint2*>(p1 + plane + (size_t)c * 8) = b;
+      *reinterpret_cast<uint2*>(p1 + 2 * plane + (size_t)c * 8) = cc;
+    }
+  }
+}
+
 int launch_add_rmsnorm_split(const __half* x, const __half* delta, const float* w, float eps,
                              __half* x_out, __half* h, uint8_t* planes, float* xscale, int M,
                              int H, cudaStream_t s) {
@@ -210,16 +308,18 @@ int launch_add_rmsnorm_split(const __half* x, const __half* delta, const float* 
       (x_out && !aligned16(x_out)) || (h && !aligned16(h)) || !aligned16(planes))
     return DDQ_ERR_ALIGNMENT;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)((M + 7) / 8));
-  cfg.blockDim = dim3(256);
+  // few rows (a decode step): one row per CTA; many rows: one row per warp
+  const bool per_cta = M <= 256;
+  cfg.gridDim = dim3(per_cta ? (unsigned)M : (unsigned)((M + 7) / 8));
+  cfg.blockDim = dim3(per_cta ? NR_THREADS : 256);
   cfg.stream = s;
   cudaLaunchAttribute at;
   at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at.val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = &at;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, add_rmsnorm_split_kernel, x, delta, w, eps, x_out, h, planes,
-                         xscale, M, H) != cudaSuccess) {
+  if (cudaLaunchKernelEx(&cfg, per_cta ? add_rmsnorm_split_row_kernel : add_rmsnorm_split_kernel,
+                         x, delta, w, eps, x_out, h, planes, xscale, M, H) != cudaSuccess) {
     cudaGetLastError();
     return DDQ_ERR_LAUNCH;
   }
