@@ -206,7 +206,9 @@ __global__ void __launch_bounds__(256) add_rmsnorm_split_kernel(
 // the threads on each row.  The sum of squares is reduced in the one-warp
 // kernels' order (chunk partials; lane L adds chunks L, L + 32, ... in turn,
 // then the same butterfly), so h is bit-identical to add_rmsnorm's.
+// SPLIT = false: h only (the add_rmsnorm of a decode step).
 constexpr int NR_THREADS = 128;
+template <bool SPLIT>
 __global__ void __launch_bounds__(NR_THREADS) add_rmsnorm_split_row_kernel(
     const __half* x, const __half* __restrict__ delta, const float* __restrict__ w, float eps,
     __half* x_out, __half* __restrict__ h, uint8_t* __restrict__ planes,
@@ -267,6 +269,7 @@ __global__ void __launch_bounds__(NR_THREADS) add_rmsnorm_split_row_kernel(
       }
     }
   }
+  if (!SPLIT) return;
   amax = warp_max(amax);
   if (lane == 0) red[1][warp] = amax;
   __syncthreads();
@@ -318,7 +321,8 @@ int launch_add_rmsnorm_split(const __half* x, const __half* delta, const float* 
   at.val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = &at;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, per_cta ? add_rmsnorm_split_row_kernel : add_rmsnorm_split_kernel,
+  if (cudaLaunchKernelEx(&cfg,
+                         per_cta ? add_rmsnorm_split_row_kernel<true> : add_rmsnorm_split_kernel,
                          x, delta, w, eps, x_out, h, planes, xscale, M, H) != cudaSuccess) {
     cudaGetLastError();
     return DDQ_ERR_LAUNCH;
@@ -334,16 +338,21 @@ int launch_add_rmsnorm(const __half* x, const __half* delta, const float* w, flo
       (x_out && !aligned16(x_out)) || !aligned16(h))
     return DDQ_ERR_ALIGNMENT;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)((M + 7) / 8));
-  cfg.blockDim = dim3(256);
+  // few rows of at most 2048 (a decode step): one row per CTA; else one per warp
+  const bool per_cta = M <= 256 && H <= 32 * NM_REG_CHUNKS * 8 && H % 16 == 0;
+  cfg.gridDim = dim3(per_cta ? (unsigned)M : (unsigned)((M + 7) / 8));
+  cfg.blockDim = dim3(per_cta ? NR_THREADS : 256);
   cfg.stream = s;
   cudaLaunchAttribute at;
   at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at.val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = &at;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel, x, delta, w, eps, x_out, h, M, H) !=
-      cudaSuccess) {
+  const cudaError_t e =
+      per_cta ? cudaLaunchKernelEx(&cfg, add_rmsnorm_split_row_kernel<false>, x, delta, w, eps,
+                                   x_out, h, (uint8_t*)nullptr, (float*)nullptr, M, H)
+              : cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel, x, delta, w, eps, x_out, h, M, H);
+  if (e != cudaSuccess) {
     cudaGetLastError();
     return DDQ_ERR_LAUNCH;
   }
