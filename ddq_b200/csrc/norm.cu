@@ -67,6 +67,10 @@ __device__ __forceinline__ uint4 nm_scale8w(const uint4& a, float r, const float
 
 constexpr int NM_REG_CHUNKS = 8;  // 16-byte chunks per lane kept in registers
 
+// RC: chunks per lane kept in registers (4 for rows of up to 1024: half the
+// registers, twice the CTAs per SM).  Every RC sums a lane's chunks in the same
+// order, so the result does not depend on it.
+template <int RC>
 __global__ void __launch_bounds__(256) add_rmsnorm_kernel(const __half* x,
                                                           const __half* __restrict__ delta,
                                                           const float* __restrict__ w, float eps,
@@ -81,11 +85,11 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(const __half* x,
   const uint4* dr = delta ? reinterpret_cast<const uint4*>(delta + (size_t)row * H) : nullptr;
   uint4* xo = x_out ? reinterpret_cast<uint4*>(x_out + (size_t)row * H) : nullptr;
   uint4* hr = reinterpret_cast<uint4*>(h + (size_t)row * H);
-  const bool in_regs = nch <= 32 * NM_REG_CHUNKS;
-  uint4 v[NM_REG_CHUNKS];
+  const bool in_regs = nch <= 32 * RC;
+  uint4 v[RC];
   float ss = 0.f;
 #pragma unroll
-  for (int j = 0; j < NM_REG_CHUNKS; ++j) {
+  for (int j = 0; j < RC; ++j) {
     const int c = lane + 32 * j;
     if (in_regs && c < nch) {
       v[j] = dr ? nm_add8(xr[c], dr[c]) : xr[c];
@@ -105,7 +109,7 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(const __half* x,
   const float r = rsqrtf(ss / (float)H + eps);
   if (in_regs) {
 #pragma unroll
-    for (int j = 0; j < NM_REG_CHUNKS; ++j) {
+    for (int j = 0; j < RC; ++j) {
       const int c = lane + 32 * j;
       if (c < nch) hr[c] = nm_scale8(v[j], r, w + 8 * c);
     }
@@ -351,7 +355,10 @@ int launch_add_rmsnorm(const __half* x, const __half* delta, const float* w, flo
   const cudaError_t e =
       per_cta ? cudaLaunchKernelEx(&cfg, add_rmsnorm_split_row_kernel<false>, x, delta, w, eps,
                                    x_out, h, (uint8_t*)nullptr, (float*)nullptr, M, H)
-              : cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel, x, delta, w, eps, x_out, h, M, H);
+          : H / 8 <= 128
+              ? cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel<4>, x, delta, w, eps, x_out, h, M, H)
+              : cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel<NM_REG_CHUNKS>, x, delta, w, eps,
+                                   x_out, h, M, H);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return DDQ_ERR_LAUNCH;

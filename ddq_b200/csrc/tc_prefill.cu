@@ -450,23 +450,30 @@ namespace {
 // call keeps its activation planes at the start of the same workspace).
 struct PfWs {
   int half = 0;
-  bool last_pf = true;  // nothing has used it yet
+  bool last_pf = false;  // unknown history: wait, as with a single buffer
 };
 std::mutex g_pf_ws_mu;
 std::unordered_map<const void*, PfWs> g_pf_ws;
+// Forgetting a workspace is always safe (its next call waits), so the table is
+// simply cleared if a caller cycles through very many workspaces.
+constexpr size_t kPfWsMax = 4096;
+PfWs& pf_ws_entry(const void* ws) {
+  if (g_pf_ws.size() >= kPfWsMax && g_pf_ws.find(ws) == g_pf_ws.end()) g_pf_ws.clear();
+  return g_pf_ws[ws];
+}
 }  // namespace
 
 void ws_note_other_use(const void* ws) {
   if (!ws) return;
   std::lock_guard<std::mutex> lock(g_pf_ws_mu);
-  g_pf_ws[ws].last_pf = false;
+  pf_ws_entry(ws).last_pf = false;
 }
 
 // The buffer (0 or 1) for this prefill call, and whether its expansion may
 // run ahead of the previous kernel.
 static int pf_take_buffer(const void* ws, bool* early) {
   std::lock_guard<std::mutex> lock(g_pf_ws_mu);
-  PfWs& st = g_pf_ws[ws];
+  PfWs& st = pf_ws_entry(ws);
   *early = st.last_pf;
   st.last_pf = true;
   st.half ^= 1;
