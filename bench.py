@@ -411,7 +411,7 @@ def run_generation(args, device, rank, world, peaks):
     per = max(1, args.gen_prompts // world)
     g = torch.Generator(device=device).manual_seed(1000 + rank)
     prompts = torch.randint(0, cfg.vocab_size, (per, args.gen_prompt_len), generator=g, device=device)
-    eng.generate(prompts[:min(per, 8)], 4)           # warm-up (kernel attributes, graphs)
+    eng.generate(prompts, 4)   # warm-up on the same shapes (kernel attributes, attention plans)
     torch.cuda.synchronize(device)
     if world > 1:
         torch.distributed.barrier()

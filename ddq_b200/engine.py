@@ -409,12 +409,15 @@ class Engine:
 
     # ------------------------------------------------------------------ generation
     @torch.no_grad()
-    def generate(self, prompts: torch.Tensor, max_new_tokens: int, prefill_chunk: int = 8,
+    def generate(self, prompts: torch.Tensor, max_new_tokens: int, prefill_chunk: int = 64,
                  use_graph: bool = True, teacher: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Greedy generation for a batch of equal-length prompts [B, S] -> tokens [B, max_new].
 
         Prefill runs in chunks of `prefill_chunk` sequences (M = chunk * S tokens per
-        GEMM); decode runs all B sequences at once (M = B).  With `teacher` [B, max_new]
+        GEMM; the eager prefill launches ~300 kernels per chunk, so few large
+        chunks keep the host ahead of the GPU); decode runs all B sequences at
+        once (M = B), one captured step per token with its bookkeeping on the
+        device.  With `teacher` [B, max_new]
         the next input at each step is the teacher's token instead of the generated
         one (used to compare against the oracle step by step); the returned tokens
         are still this engine's greedy picks.
@@ -429,34 +432,38 @@ class Engine:
             out[b0:b0 + chunk.shape[0], 0] = self.greedy(h[:, -1, :])
         if max_new_tokens == 1:
             return out
+        # One decode step, entirely on the device: t counts the tokens already
+        # emitted (t = 0 .. max_new - 2); the step reads token t (the previous
+        # pick, or the teacher's), runs at position S + t and writes its pick
+        # to out[:, t + 1].  The host only replays the captured step.
+        src = out if teacher is None else teacher
+        t = torch.zeros(1, dtype=torch.int64, device=self.device)
         tok = torch.empty(B, 1, dtype=torch.int64, device=self.device)
         pos = torch.empty(1, dtype=torch.int64, device=self.device)
-        nxt = torch.empty(B, dtype=torch.int64, device=self.device)
 
         def step():
-            nxt.copy_(self.greedy(self.decode_hidden(tok, cache, pos)))
+            tok.copy_(src.index_select(1, t))
+            torch.add(t, S, out=pos)
+            nxt = self.greedy(self.decode_hidden(tok, cache, pos))
+            out.index_copy_(1, t + 1, nxt[:, None])
+            t.add_(1)
 
         graph = None
         if use_graph and self.linear_kind == "fp8":
-            tok.copy_(out[:, :1] if teacher is None else teacher[:, :1])
-            pos.fill_(S)
             s = torch.cuda.Stream(self.device)
             s.wait_stream(torch.cuda.current_stream(self.device))
             with torch.cuda.stream(s):
                 step()  # warm-up outside capture (kernel attributes, workspaces)
             torch.cuda.current_stream(self.device).wait_stream(s)
+            t.zero_()   # the warm-up step is redone by the first replay (same cache row)
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
                 step()
-        for t in range(1, max_new_tokens):
-            src = out[:, t - 1:t] if teacher is None else teacher[:, t - 1:t]
-            tok.copy_(src)
-            pos.fill_(S + t - 1)
+        for _ in range(1, max_new_tokens):
             if graph is not None:
                 graph.replay()
             else:
                 step()
-            out[:, t] = nxt
         if graph is not None:
             del graph
         return out
