@@ -456,9 +456,17 @@ class Engine:
                 step()  # warm-up outside capture (kernel attributes, workspaces)
             torch.cuda.current_stream(self.device).wait_stream(s)
             t.zero_()   # the warm-up step is redone by the first replay (same cache row)
+            # captured on a side stream without the device-wide synchronisation
+            # of the torch.cuda.graph context: the host records the step while
+            # the GPU still runs the prefill and the warm-up
             graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
-                step()
+            cap = torch.cuda.Stream(self.device)
+            with torch.cuda.stream(cap):
+                graph.capture_begin()
+                try:
+                    step()
+                finally:
+                    graph.capture_end()
         for _ in range(1, max_new_tokens):
             if graph is not None:
                 graph.replay()
