@@ -130,14 +130,13 @@ class Engine:
         self.lm_head: FP8Linear = weights["lm_head"]  # e4m3 copy of the embedding
         hd = cfg.head_dim
         inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, hd, 2, dtype=torch.float32) / hd))
-        self._inv_freq = inv.to(self.device)
+        self._inv_freq2 = torch.cat([inv, inv]).to(self.device)  # both halves of a head
         self._split_bufs: dict = {}   # (tokens, hidden, stream) -> reusable split buffers
         # decode steps run as this many independent slices of >= 32 sequences
         # on their own streams (the step is latency-bound; the slices overlap;
         # measured: 64 = 2 x 32 beats 1 x 64 and 4 x 16, 1 x 32 beats 2 x 16)
         self.decode_chains = 2
         self._chain_streams: List[torch.cuda.Stream] = []
-        self._rope_cache = {}
         self._graphs = {}
 
     # ------------------------------------------------------------------ construction
@@ -234,8 +233,10 @@ class Engine:
         return x, self.rmsnorm(x, w)
 
     def rope_tables(self, positions: torch.Tensor):
-        f = positions.float()[:, None] * self._inv_freq[None, :]
-        emb = torch.cat([f, f], dim=-1)
+        """cos/sin [S, D] of rotate-half RoPE: fp32(position) * inv_freq for both
+        halves of the head (one multiply, the same values as concatenating the
+        half-width product with itself)."""
+        emb = positions[:, None] * self._inv_freq2[None, :]
         return emb.cos(), emb.sin()
 
     @staticmethod
