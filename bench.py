@@ -279,6 +279,7 @@ def run_ours(args, rank, world, device):
     torch.cuda.empty_cache()
     prefill = None if args.skip_extra else run_prefill(args, device, world, peaks)
     lmhead = None if args.skip_extra else run_lm_head(args, device, world, peaks)
+    config1 = None if args.skip_extra else run_config1(args, device, world, peaks)
     generation = None if args.skip_extra else run_generation(args, device, rank, world, peaks)
 
     cpu = None
@@ -300,6 +301,7 @@ def run_ours(args, rank, world, device):
                    "parallelism": f"replicas x{world}"},
         "per_m_gate_up": per_m,
         "prefill": prefill,
+        "config1": config1,
         "lm_head": lmhead,
         "generation": generation,
         "roofline": roofline,
@@ -356,6 +358,48 @@ def run_prefill(args, device, world, peaks):
             "frac_of_bf16_peak_per_gpu": round(per_gpu / peaks["bf16_tflops"], 4),
             "peak_tflops": peaks["bf16_tflops"], "peak_source": peaks["source"],
             "kernel": "e4m3_to_f16_kernel + w8a16_pf_kernel (exact weight expansion, tcgen05 kind::f16)"}
+
+
+def run_config1(args, device, world, peaks):
+    """Config 1: one W8A16 GEMM, x fp16 [16, 896] ~ N(0, 1), W [4864, 896] ~ N(0, 0.02)
+    quantized to e4m3 with per-row scales, no bias; per call in a replayed CUDA
+    graph of 64 calls over 64 weight copies (more than twice L2, so every call
+    reads its weight from HBM)."""
+    from ddq_b200 import gemm_fp8
+    M, N, K = 16, 4864, 896
+    g = torch.Generator(device=device).manual_seed(11)
+    ncopy = 64  # 64 x 4.36 MB > 2 x L2
+    copies = [gemm_fp8.quantize(torch.randn(N, K, generator=g, device=device) * 0.02)
+              for _ in range(ncopy)]
+    x = torch.randn(M, K, generator=g, device=device).half()
+    reps = 64
+    side = torch.cuda.Stream(device)
+
+    def calls():
+        for i in range(reps):
+            gemm_fp8.f8_forward(x, *copies[i % ncopy])
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        calls()
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        calls()
+    for _ in range(2):
+        graph.replay()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(3):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize(device)
+    del graph, copies
+    us = reduce_max(e0.elapsed_time(e1), world, device) * 1e3 / (3 * reps)
+    nb = N * K + 4 * N + 2 * M * K + 2 * M * N
+    return {"workload": "config1: M=16, 896->4864, no bias", "us": round(us, 2),
+            "gbs": round(nb / (us * 1e-6) / 1e9, 1),
+            "frac_of_hbm_peak": round(nb / (us * 1e-6) / 1e9 / peaks["hbm_gbs"], 4)}
 
 
 def run_lm_head(args, device, world, peaks):
