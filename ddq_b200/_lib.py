@@ -30,7 +30,7 @@ _SIGNATURES = {
     "ddq_decode_attention_split": (ctypes.c_int, [_vp, _c_int64, _vp, _vp, _c_int64, _c_int64,
                                                   _vp, _vp, _vp, _vp, _c_int64, _vp, _vp,
                                                   _c_int64, _c_int64, _c_int64, _c_int64,
-                                                  ctypes.c_float, _vp]),
+                                                  ctypes.c_float, ctypes.c_int, _vp]),
     "ddq_prefill_rope_kv": (ctypes.c_int, [_vp, _c_int64, _vp, _vp, _c_int64, _c_int64, _vp, _vp,
                                            _c_int64, _vp, _vp, _vp, _c_int64, _c_int64, _c_int64,
                                            _c_int64, _c_int64, _vp]),

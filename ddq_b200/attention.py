@@ -67,12 +67,16 @@ def decode_attention(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Te
 def decode_attention_split(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                            cos: torch.Tensor, sin: torch.Tensor, pos: torch.Tensor,
                            num_heads: int, num_kv_heads: int, head_dim: int, scale: float,
-                           act: Optional[SplitActivations] = None, with_out: bool = False):
+                           act: Optional[SplitActivations] = None, with_out: bool = False,
+                           kv_ready: bool = False):
     """``decode_attention`` whose output is the o projection's operand
     (``ddq_decode_attention_split``): o's three e4m3 planes and token scales,
     for ``gemm_fp8.f8_forward_planes``, bit for bit what the GEMM's own split
     of fp16 o gives.  ``act`` reuses buffers of the same shape; ``with_out``
-    also returns fp16 o.  Returns (act, o or None)."""
+    also returns fp16 o.  ``kv_ready`` promises that ``pos`` and the cache rows
+    before it were final before the previous kernel on the stream started (a
+    decode loop, where earlier steps wrote them): the kernel then loads them
+    while that kernel still runs.  Returns (act, o or None)."""
     B, cos, sin = _check_decode(qkv, k_cache, v_cache, cos, sin, pos, num_heads, num_kv_heads,
                                 head_dim)
     K = num_heads * head_dim
@@ -86,7 +90,7 @@ def decode_attention_split(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: to
             k_cache.stride(0), k_cache.shape[2], cos.data_ptr(), sin.data_ptr(), pos.data_ptr(),
             out.data_ptr() if out is not None else None, K, act.planes.data_ptr(),
             act.xscale.data_ptr(), B, num_heads, num_kv_heads, head_dim, float(scale),
-            torch.cuda.current_stream(qkv.device).cuda_stream)
+            1 if kv_ready else 0, torch.cuda.current_stream(qkv.device).cuda_stream)
     _lib.check(st, "decode_attention_split")
     return act, out
 

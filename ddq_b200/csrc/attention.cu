@@ -54,6 +54,8 @@ struct AtArgs {
   int trace;             // debug flag bit 1: phase stamps (see ddq_read_trace)
   uint8_t* planes;       // split output: three e4m3 planes [3][B][Hq * D] (or null)
   float* xscale;         // and the token scales 2^-e [B]
+  int kv_ready;          // pos and the cache rows before it are final before the
+                         // previous kernel starts: load them ahead of the grid wait
 };
 
 template <int D>
@@ -346,7 +348,7 @@ __global__ void __launch_bounds__(AM_NW * 32, 1)
     ptx::fence_mbar_init();
     ptx::prefetch_tmap(&tm_k);
     ptx::prefetch_tmap(&tm_v);
-  } else if (threadIdx.x == 32) {
+  } else if (threadIdx.x == 32 && !a.kv_ready) {
     // L2 prefetch of rows 0..pos while the previous kernel finishes; the
     // position read here may be stale, which only makes the hint less useful
     const int64_t ph = *a.pos;
@@ -359,6 +361,34 @@ __global__ void __launch_bounds__(AM_NW * 32, 1)
       }
     }
   }
+  const uint32_t ring0 = ptx::smem_u32(&sm.ring[0][0][0]);
+  auto issue = [&](int c) {  // chunk c into its slot of this warp's ring
+    const int s = warp * AM_DEPTH + (c / AM_NW) % AM_DEPTH;
+    const uint32_t full = ptx::smem_u32(&sm.full[s]);
+    const uint32_t dst = ring0 + (uint32_t)(s * 2 * AM_CHUNK);
+    ptx::mbar_arrive_expect_tx(full, 2u * AM_CHUNK);
+    ptx::tma_load_4d(dst, &tm_k, 0, c * AM_ROWS, g, b, full);
+    ptx::tma_load_4d(dst + AM_CHUNK, &tm_v, 0, c * AM_ROWS, g, b, full);
+  };
+  // With kv_ready the position and every cache row this step reads (except
+  // the new one, patched in shared memory below) were final before the
+  // previous kernel started: the first ring of chunks streams in while that
+  // kernel still runs.
+  int64_t p_early = -1;
+  bool early = false;
+  if (a.kv_ready) {
+    __syncthreads();  // barriers initialised
+    p_early = *a.pos;
+    if (p_early >= 0 && p_early < a.cap) {
+      early = true;
+      const int n0 = ((int)p_early + AM_ROWS) / AM_ROWS;  // chunks of rows 0..pos
+      if (lane == 0)
+        for (int i = 0; i < AM_DEPTH; ++i) {
+          const int c = warp + i * AM_NW;
+          if (c < n0) issue(c);
+        }
+    }
+  }
   ptx::pdl_wait();  // qkv comes from the previous kernel; earlier cache rows are complete
   if (threadIdx.x == 0) trace_stamp(tr, 1);
   // one memory round trip: the position, this group's q / k / v values and
@@ -367,7 +397,7 @@ __global__ void __launch_bounds__(AM_NW * 32, 1)
   constexpr int NT = AM_NW * 32;
   constexpr int NRI = ((G + 1) * DH + NT - 1) / NT;  // rotary pairs per thread
   float x1[NRI], x2[NRI], c1[NRI], s1[NRI], c2[NRI], s2[NRI];
-  const int64_t p = *a.pos;
+  const int64_t p = a.kv_ready ? p_early : *a.pos;
 #pragma unroll
   for (int r = 0; r < NRI; ++r) {
     const int i = threadIdx.x + r * NT;
@@ -388,24 +418,15 @@ __global__ void __launch_bounds__(AM_NW * 32, 1)
   const int L = (int)p + 1;
   const int nchunks = (L + AM_ROWS - 1) / AM_ROWS;
   const int last = nchunks - 1;  // the chunk that holds the new row
-  const uint32_t ring0 = ptx::smem_u32(&sm.ring[0][0][0]);
   __syncthreads();  // barriers initialised
   // split output: the cluster's barriers are ready before any CTA pushes
   // (the matching wait comes after the merge)
   if (SPLIT) ptx::cluster_arrive_relaxed();
 
-  auto issue = [&](int c) {  // chunk c into its slot of this warp's ring
-    const int s = warp * AM_DEPTH + (c / AM_NW) % AM_DEPTH;
-    const uint32_t full = ptx::smem_u32(&sm.full[s]);
-    const uint32_t dst = ring0 + (uint32_t)(s * 2 * AM_CHUNK);
-    ptx::mbar_arrive_expect_tx(full, 2u * AM_CHUNK);
-    ptx::tma_load_4d(dst, &tm_k, 0, c * AM_ROWS, g, b, full);
-    ptx::tma_load_4d(dst + AM_CHUNK, &tm_v, 0, c * AM_ROWS, g, b, full);
-  };
   // every chunk can be requested now: the new row is not read back from the
   // cache (its stale copy in the last chunk's tile is overwritten in shared
   // memory), so the copies overlap the rotary embedding below
-  if (lane == 0)
+  if (lane == 0 && !early)
     for (int i = 0; i < AM_DEPTH; ++i) {
       const int c = warp + i * AM_NW;
       if (c < nchunks) issue(c);
@@ -700,7 +721,8 @@ int launch_decode_attention(const __half* qkv, int64_t qkv_stride, __half* kc, _
                             int64_t cache_bstride, int cap, const float* cos, const float* sin,
                             const int64_t* pos, __half* out, int64_t out_stride, uint8_t* planes,
                             float* xscale, int B, int Hq, int Hkv, int D, float scale,
-                            unsigned long long timeout_ns, int debug_flags, cudaStream_t s) {
+                            unsigned long long timeout_ns, int debug_flags, int flags,
+                            cudaStream_t s) {
   if (B < 1 || Hkv < 1 || Hq < Hkv || Hq % Hkv != 0 || Hq / Hkv > AT_GMAX || cap < 1)
     return DDQ_ERR_SHAPE;
   if (D != 64 && D != 128) return DDQ_ERR_SHAPE;
@@ -711,7 +733,7 @@ int launch_decode_attention(const __half* qkv, int64_t qkv_stride, __half* kc, _
   if (!aligned16(kc) || !aligned16(vc) || (cache_bstride % 8) != 0) return DDQ_ERR_ALIGNMENT;
   if (split && !aligned16(planes)) return DDQ_ERR_ALIGNMENT;
   AtArgs a{qkv, qkv_stride, kc, vc, cache_bstride, cap, cos, sin, pos, out, out_stride, Hq, Hkv,
-           scale, (debug_flags & 2) != 0 ? 1 : 0, planes, xscale};
+           scale, (debug_flags & 2) != 0 ? 1 : 0, planes, xscale, (flags & 1) != 0 ? 1 : 0};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(B * Hkv));
   cfg.blockDim = dim3(at_warps(D) * 32);

@@ -206,7 +206,7 @@ extern "C" int ddq_decode_attention(const void* qkv, int64_t qkv_stride, void* k
       reinterpret_cast<const __half*>(qkv), qkv_stride, reinterpret_cast<__half*>(k_cache),
       reinterpret_cast<__half*>(v_cache), cache_batch_stride, (int)capacity, cos, sin, pos,
       reinterpret_cast<__half*>(out), out_stride, nullptr, nullptr, (int)B, (int)Hq, (int)Hkv,
-      (int)D, scale, g_wait_timeout_ns, g_debug_flags, reinterpret_cast<cudaStream_t>(stream));
+      (int)D, scale, g_wait_timeout_ns, g_debug_flags, 0, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int ddq_decode_attention_split(const void* qkv, int64_t qkv_stride, void* k_cache,
@@ -214,7 +214,8 @@ extern "C" int ddq_decode_attention_split(const void* qkv, int64_t qkv_stride, v
                                           int64_t capacity, const float* cos, const float* sin,
                                           const int64_t* pos, void* out, int64_t out_stride,
                                           uint8_t* planes, float* xscale, int64_t B, int64_t Hq,
-                                          int64_t Hkv, int64_t D, float scale, void* stream) {
+                                          int64_t Hkv, int64_t D, float scale, int flags,
+                                          void* stream) {
   if (B < 0 || Hq < 0 || Hkv < 0 || D < 0 || capacity < 0) return DDQ_ERR_SHAPE;
   if (B == 0) return DDQ_OK;
   if (!qkv || !k_cache || !v_cache || !cos || !sin || !pos || !planes || !xscale)
@@ -227,7 +228,8 @@ extern "C" int ddq_decode_attention_split(const void* qkv, int64_t qkv_stride, v
       reinterpret_cast<const __half*>(qkv), qkv_stride, reinterpret_cast<__half*>(k_cache),
       reinterpret_cast<__half*>(v_cache), cache_batch_stride, (int)capacity, cos, sin, pos,
       reinterpret_cast<__half*>(out), out_stride, planes, xscale, (int)B, (int)Hq, (int)Hkv,
-      (int)D, scale, g_wait_timeout_ns, g_debug_flags, reinterpret_cast<cudaStream_t>(stream));
+      (int)D, scale, g_wait_timeout_ns, g_debug_flags, flags,
+      reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int ddq_add_rmsnorm(const void* x, const void* delta, const float* w, float eps,

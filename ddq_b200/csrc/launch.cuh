@@ -65,7 +65,8 @@ int launch_decode_attention(const __half* qkv, int64_t qkv_stride, __half* kc, _
                             int64_t cache_bstride, int cap, const float* cos, const float* sin,
                             const int64_t* pos, __half* out, int64_t out_stride, uint8_t* planes,
                             float* xscale, int B, int Hq, int Hkv, int D, float scale,
-                            unsigned long long timeout_ns, int debug_flags, cudaStream_t s);
+                            unsigned long long timeout_ns, int debug_flags, int flags,
+                            cudaStream_t s);
 // Residual add + RMSNorm, optionally followed by the three-plane split of the
 // result for a decode GEMM (norm.cu).
 int launch_add_rmsnorm_split(const __half* x, const __half* delta, const float* w, float eps,

@@ -326,9 +326,10 @@ class Engine:
         p = L["qkv"]
         qkv = gemm_fp8.f8_forward_planes(bufs[0], p.wq, p.scales, p.bias)
         if hd == 64 and nkv <= 8:  # attention emits the o projection's operand directly
+            # the position and the cache rows before it come from earlier steps
             bufs[2], _ = attention.decode_attention_split(
                 qkv, cache.k[li, b0:b0 + B], cache.v[li, b0:b0 + B], cos, sin, pos, nh, nkv, hd,
-                hd ** -0.5, bufs[2])
+                hd ** -0.5, bufs[2], kv_ready=True)
             p = L["o"]
             attn = gemm_fp8.f8_forward_planes(bufs[2], p.wq, p.scales, p.bias).reshape(x.shape)
         else:

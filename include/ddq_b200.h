@@ -164,13 +164,17 @@ int ddq_decode_attention(const void* qkv, int64_t qkv_stride, void* k_cache, voi
  * reference counterpart (it removes the pre-pass between attention and the o
  * projection).  out (fp16 o) is optional (NULL: not written).  D = 64,
  * Hkv <= 8 (the Hkv CTAs of a token run as one thread-block cluster); planes
- * 16-byte aligned.
+ * 16-byte aligned.  flags bit 0 (kv_ready): the caller guarantees that *pos
+ * and the cache rows before it were final before the kernel issued just
+ * before this call on the stream started (as in a decode loop, where earlier
+ * steps wrote them); the kernel then loads them while that kernel still runs.
  */
 int ddq_decode_attention_split(const void* qkv, int64_t qkv_stride, void* k_cache, void* v_cache,
                                int64_t cache_batch_stride, int64_t capacity, const float* cos,
                                const float* sin, const int64_t* pos, void* out,
                                int64_t out_stride, uint8_t* planes, float* xscale, int64_t B,
-                               int64_t Hq, int64_t Hkv, int64_t D, float scale, void* stream);
+                               int64_t Hq, int64_t Hkv, int64_t D, float scale, int flags,
+                               void* stream);
 
 /*
  * Prefill rotary embedding and KV-cache write for a chunk of S tokens per

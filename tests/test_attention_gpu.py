@@ -174,9 +174,14 @@ def test_decode_attention_split_feeds_the_o_projection_exactly(cuda_device, B, n
                                                with_out=True)
     act_only, none = attention.decode_attention_split(qkv, kc, vc, cos, sin, p, nh, nkv, hd,
                                                       0.125)
+    # the position and earlier cache rows are final here: loading them ahead
+    # of the grid wait changes nothing
+    act_early, o3 = attention.decode_attention_split(qkv, kc, vc, cos, sin, p, nh, nkv, hd,
+                                                     0.125, with_out=True, kv_ready=True)
     torch.cuda.synchronize()
-    assert none is None and torch.equal(o, o2)
+    assert none is None and torch.equal(o, o2) and torch.equal(o, o3)
     assert torch.equal(act.planes, act_only.planes) and torch.equal(act.xscale, act_only.xscale)
+    assert torch.equal(act.planes, act_early.planes) and torch.equal(act.xscale, act_early.xscale)
     wq, s = gemm_fp8.quantize(torch.randn(896, nh * hd, generator=g, device="cuda") * 0.02)
     y_ref = gemm_fp8.f8_forward(o, wq, s)
     y = gemm_fp8.f8_forward_planes(act, wq, s)
