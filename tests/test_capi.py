@@ -73,3 +73,54 @@ def test_missing_library_raises_instead_of_falling_back(monkeypatch, tmp_path):
     monkeypatch.setenv("DDQ_B200_LIB", str(tmp_path / "nope.so"))
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         _lib.load()
+
+
+def test_argument_validation_of_the_fused_operators_without_gpu(lib):
+    """The decode/prefill operators reject bad arguments with status codes before
+    any CUDA call (pointers below are placeholders that are never dereferenced:
+    16-byte aligned A, misaligned U)."""
+    A, U = 256, 258
+    OK, INVALID, SHAPE, ALIGN = 0, 1, 2, 3
+    # ddq_prefill_rope_kv(qkv, qkv_stride, kc, vc, bstride, cap, cos, sin, start,
+    #                     q_out, k_out, v_out, B, S, Hq, Hkv, D, stream)
+    hq, hkv, d, cap = 14, 2, 64, 16
+    w, bs = (hq + 2 * hkv) * d, hkv * cap * d
+
+    def rope(qkv=A, start=0, S=8, B=2, D=d, q=A):
+        return lib.ddq_prefill_rope_kv(qkv, w, A, A, bs, cap, A, A, start, q, None, None,
+                                       B, S, hq, hkv, D, None)
+    assert lib.ddq_prefill_rope_kv(None, w, None, None, bs, cap, None, None, 0, None, None, None,
+                                   -1, 8, hq, hkv, d, None) == SHAPE
+    assert lib.ddq_prefill_rope_kv(None, w, None, None, bs, cap, None, None, 0, None, None, None,
+                                   0, 8, hq, hkv, d, None) == OK
+    assert lib.ddq_prefill_rope_kv(None, w, None, None, bs, cap, None, None, 0, None, None, None,
+                                   2, 8, hq, hkv, d, None) == INVALID
+    assert rope(start=10) == SHAPE          # start + S beyond the capacity
+    assert rope(D=96) == SHAPE              # 64- or 128-wide heads only
+    assert rope(qkv=U) == ALIGN
+    assert rope(q=U) == ALIGN
+    # ddq_decode_attention_split(qkv, qkv_stride, kc, vc, bstride, cap, cos, sin, pos, out,
+    #                            out_stride, planes, xscale, B, Hq, Hkv, D, scale, flags, stream)
+
+    def attn(planes=A, Hq=hq, Hkv=hkv, D=d, B=2):
+        wd = (Hq + 2 * Hkv) * D
+        return lib.ddq_decode_attention_split(A, wd, A, A, Hkv * cap * D, cap, A, A, A, None,
+                                              Hq * D, planes, A, B, Hq, Hkv, D, 0.125, 0, None)
+    assert attn(B=-1) == SHAPE
+    assert lib.ddq_decode_attention_split(None, w, None, None, bs, cap, None, None, None, None,
+                                          hq * d, None, None, 0, hq, hkv, d, 0.125, 0, None) == OK
+    assert attn(planes=None) == INVALID
+    assert attn(D=128) == SHAPE             # the split output is for 64-wide heads
+    assert attn(Hq=16, Hkv=16) == SHAPE     # one cluster of at most 8 KV heads per token
+    assert attn(planes=U) == ALIGN
+    # ddq_add_rmsnorm_split(x, delta, w, eps, x_out, h, planes, xscale, M, H, stream)
+    assert lib.ddq_add_rmsnorm_split(A, None, A, 1e-6, None, None, A, A, -1, 896, None) == SHAPE
+    assert lib.ddq_add_rmsnorm_split(None, None, None, 1e-6, None, None, None, None, 0, 896,
+                                     None) == OK
+    assert lib.ddq_add_rmsnorm_split(A, None, None, 1e-6, None, None, A, A, 4, 896, None) == INVALID
+    assert lib.ddq_add_rmsnorm_split(A, None, A, 1e-6, None, None, A, A, 4, 904, None) == SHAPE
+    assert lib.ddq_add_rmsnorm_split(U, None, A, 1e-6, None, None, A, A, 4, 896, None) == ALIGN
+    # ddq_w8a16_gemm_planes(planes, xscale, wq, scales, bias, bias_dtype, y, M, N, K, swiglu, stream)
+    assert lib.ddq_w8a16_gemm_planes(A, A, A, A, None, 0, A, 65, 896, 896, 0, None) == SHAPE
+    assert lib.ddq_w8a16_gemm_planes(A, A, A, A, None, 9, A, 16, 896, 896, 0, None) == INVALID
+    assert lib.ddq_w8a16_gemm_planes(A, A, U, A, None, 0, A, 16, 896, 896, 0, None) == ALIGN
