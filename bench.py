@@ -496,9 +496,12 @@ def run_generation(args, device, rank, world, peaks):
 
 
 def launches_per_step(calls):
-    """Kernels of this library per step: a decode-shape GEMM (M <= 64) is the
-    activation-split pre-pass plus the GEMM."""
-    return sum(2 if c[6] <= 64 else 1 for c in calls)
+    """Kernels of this library per step, as the library reports them per shape:
+    one for a GEMM of <= 16 tokens that the thin kernel takes, two (activation
+    split + GEMM) for the other decode shapes."""
+    from ddq_b200 import _lib
+    L = _lib.load()
+    return sum(L.ddq_w8a16_gemm_kernel_count(c[6], c[7], c[8]) for c in calls)
 
 
 def run_e2e(args, wl, device, world):

@@ -20,6 +20,7 @@ _SIGNATURES = {
     "ddq_version": (ctypes.c_int, []),
     "ddq_quantize_e4m3": (ctypes.c_int, [_vp, ctypes.c_int, _c_int64, _c_int64, _vp, _vp, _vp]),
     "ddq_w8a16_gemm_workspace_size": (ctypes.c_size_t, [_c_int64, _c_int64, _c_int64]),
+    "ddq_w8a16_gemm_kernel_count": (ctypes.c_int, [_c_int64, _c_int64, _c_int64]),
     "ddq_w8a16_gemm": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, _vp, _c_int64, _c_int64,
                                       _c_int64, _vp, ctypes.c_size_t, _vp]),
     "ddq_w8a16_gemm_noalloc": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, _vp, _c_int64,

@@ -57,6 +57,23 @@ int tc_min_m() {
 }
 constexpr int64_t kDecodeMaxM = 64;
 
+// Up to this many tokens a GEMM whose weight slice and activations per SM are
+// small (thin.cu's limits) runs the shared-memory-resident mma.sync kernel
+// instead of the e4m3 decode kernel.
+// DDQ_THIN_MAX_M overrides (0 switches it off) for benchmarking.
+int64_t thin_max_m() {
+  static const int64_t v = [] {
+    const char* e = std::getenv("DDQ_THIN_MAX_M");
+    return e ? (int64_t)std::atoll(e) : (int64_t)16;
+  }();
+  return v;
+}
+bool thin_shape(int64_t M, int64_t N, int64_t K) {
+  if (M > thin_max_m()) return false;
+  const int dev = current_device();
+  return dev >= 0 && thin_eligible(M, N, K, device_sm_count(dev));
+}
+
 // From this many tokens on, a GEMM expands the weights to fp16 once and runs
 // the fp16 tensor-core GEMM (tc_prefill.cu); between kDecodeMaxM and this the
 // in-kernel conversion of tc_gemm.cu is cheaper.  DDQ_PF_MIN_M overrides.
@@ -122,6 +139,8 @@ extern "C" int ddq_w8a16_gemm(const void* x, const uint8_t* wq, const float* sca
   const __half* xh = reinterpret_cast<const __half*>(x);
   __half* yh = reinterpret_cast<__half*>(y);
   if (tc_eligible(x, wq, K) && M >= tc_min_m()) {
+    if (thin_shape(M, N, K))
+      return launch_thin(xh, wq, scales, bias, bias_dtype, yh, (int)M, (int)N, (int)K, s);
     if (M <= kDecodeMaxM)
       return launch_dec(xh, wq, scales, bias, bias_dtype, yh, nullptr, 0, (int)M, (int)N, (int)K,
                         workspace, workspace_bytes, g_wait_timeout_ns, g_debug_flags, s);
@@ -135,6 +154,14 @@ extern "C" int ddq_w8a16_gemm(const void* x, const uint8_t* wq, const float* sca
   const bool fast = tc_eligible(x, wq, K) && K <= 12288;
   if (!fast) return launch_generic(xh, wq, scales, bias, bias_dtype, yh, M, N, K, s);
   return launch_skinny(xh, wq, scales, bias, bias_dtype, yh, (int)M, (int)N, (int)K, s);
+}
+
+extern "C" int ddq_w8a16_gemm_kernel_count(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  if (K % 16 != 0 || M < tc_min_m()) return 1;
+  if (thin_shape(M, N, K)) return 1;
+  if (M <= kDecodeMaxM || pf_shape(M, N)) return 2;  // split + GEMM / expansion + GEMM
+  return 1;
 }
 
 extern "C" size_t ddq_w8a16_gemm_swiglu_workspace_size(int64_t M, int64_t I, int64_t K) {

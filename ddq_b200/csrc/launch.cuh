@@ -45,6 +45,12 @@ int launch_dec(const __half* x, const uint8_t* wq, const float* scales, const vo
                int N, int K, void* ws, size_t ws_bytes, unsigned long long timeout_ns,
                int debug_flags, cudaStream_t s, bool swiglu = false,
                const uint8_t* ext_planes = nullptr, const float* ext_xscale = nullptr);
+// 1..16 tokens, K % 64 == 0: each SM's weight slice resident in shared memory
+// before the grid dependency, mma.sync on fp16 activations (thin.cu).  No
+// workspace.  thin_eligible says whether launch_thin takes the shape.
+bool thin_eligible(int64_t M, int64_t N, int64_t K, int sms);
+int launch_thin(const __half* x, const uint8_t* wq, const float* scales, const void* bias,
+                int bias_dtype, __half* y, int M, int N, int K, cudaStream_t s);
 // Prefill shapes: exact e4m3 -> fp16 weight expansion into the workspace
 // (N * K * 2 bytes), then the fp16 tensor-core GEMM (tc_prefill.cu).
 size_t pf_workspace_bytes(int64_t N, int64_t K);

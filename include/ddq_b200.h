@@ -91,6 +91,14 @@ size_t ddq_w8a16_gemm_workspace_size(int64_t M, int64_t N, int64_t K);
  * bias type, gemm_FP8_d.cu:191) or _F32.
  * Requirements: M >= 0, N >= 1, K >= 1; the fast paths need K % 16 == 0 and
  * 16-byte aligned x / wq (a generic CUDA kernel covers the rest).
+ * Kernels by shape: M <= 16 with K % 64 == 0, M * K * 2 <= 10 KB of
+ * activations and at most 40 KB of weight per SM (one CTA per SM, 8-row
+ * tiles; e.g. the Qwen2.5-0.5B q/k/v, o and down projections at M = 1):
+ * one kernel, fp16 activations on mma.sync, the workspace unused; other
+ * M <= 64: the activation-split pre-pass plus the e4m3 tcgen05 GEMM; larger
+ * M: the prefill kernels.  Summation order differs between these kernels, so the
+ * same row can round differently at different M (all within the fp32
+ * tolerance); each kernel is bitwise reproducible.
  */
 int ddq_w8a16_gemm(const void* x, const uint8_t* wq, const float* scales,
                    const void* bias, int bias_dtype, void* y,
@@ -98,14 +106,24 @@ int ddq_w8a16_gemm(const void* x, const uint8_t* wq, const float* scales,
                    void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Number of kernels one ddq_w8a16_gemm call of this shape (16-byte aligned
+ * x / wq) launches on the current device: 1 or 2.  A diagnostic for launch
+ * counts in benchmarks; no reference counterpart.
+ */
+int ddq_w8a16_gemm_kernel_count(int64_t M, int64_t N, int64_t K);
+
+/*
  * Allocation-free variant of ddq_w8a16_gemm for decode shapes.  It has no
  * counterpart in the reference; it exists for callers that cannot allocate
  * device memory where they call a projection (a host that pre-plans and owns
  * every allocation, a serving runtime that bans cudaMalloc on its request
- * path, code recording a CUDA graph).  Same inputs, output and math as
- * ddq_w8a16_gemm on the same shapes, but the scratch lives in a 1 MiB
- * device array inside the library (held by every GPU that loads it, until
- * the process exits) instead of a caller workspace.
+ * path, code recording a CUDA graph).  Same inputs and output as
+ * ddq_w8a16_gemm; it always runs the activation split + e4m3 decode kernel
+ * (ddq_w8a16_gemm's kernel for these shapes except the ones its thin kernel
+ * takes, where the two agree within the fp32 tolerance, not bit for bit).
+ * The scratch lives in a 1 MiB device array inside the library (held by
+ * every GPU that loads it, until the process exits) instead of a caller
+ * workspace.
  * Limits: 1 <= M <= 64, K % 16 == 0, 16-byte aligned x and wq, and
  * 3*M*K (rounded up to 256) + 4*M <= 1048576 bytes; larger sizes return
  * DDQ_ERR_WORKSPACE (M > 64 or K % 16 != 0: DDQ_ERR_SHAPE).

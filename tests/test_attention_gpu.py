@@ -11,6 +11,24 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
+def decode_kernel_gemm(x, wq, s, b=None):
+    """The activation-split pre-pass + e4m3 decode kernel on fp16 activations,
+    whatever kernel ``f8_forward`` picks for the shape (the allocation-free
+    entry point always takes that path)."""
+    from ddq_b200 import _lib
+    lib = _lib.load()
+    x = x.contiguous()
+    M, K = x.shape
+    N = wq.shape[0]
+    y = torch.empty(M, N, dtype=torch.float16, device=x.device)
+    st = lib.ddq_w8a16_gemm_noalloc(x.data_ptr(), wq.data_ptr(), s.data_ptr(),
+                                    b.data_ptr() if b is not None else None,
+                                    _lib.DTYPE_F32 if b is not None else _lib.DTYPE_NONE,
+                                    y.data_ptr(), M, N, K, torch.cuda.current_stream().cuda_stream)
+    assert st == 0, _lib.status_string(st)
+    return y
+
+
 def reference(qkv, kc, vc, cos, sin, pos, nh, nkv, hd, scale):
     B = qkv.shape[0]
     q = qkv[:, : nh * hd].reshape(B, nh, hd).float()
@@ -157,8 +175,8 @@ def test_prefill_rope_kv_is_the_fp32_torch_rope(cuda_device, B, S, nh, nkv, hd, 
     (64, 14, 2, 768, 600), (3, 16, 8, 100, 57), (5, 4, 1, 40, 31), (2, 6, 2, 1100, 1099)])
 def test_decode_attention_split_feeds_the_o_projection_exactly(cuda_device, B, nh, nkv, cap, pos):
     """ddq_decode_attention_split: its fp16 o equals ddq_decode_attention's, and the
-    o projection on its planes equals the o projection on fp16 o bit for bit
-    (the GEMM's own split pre-pass of o)."""
+    o projection on its planes equals the decode kernel's o projection on fp16
+    o bit for bit (the GEMM's own split pre-pass of o)."""
     from ddq_b200 import attention, gemm_fp8
     hd = 64
     g = torch.Generator(device="cuda").manual_seed(B * 7 + pos)
@@ -183,7 +201,7 @@ def test_decode_attention_split_feeds_the_o_projection_exactly(cuda_device, B, n
     assert torch.equal(act.planes, act_only.planes) and torch.equal(act.xscale, act_only.xscale)
     assert torch.equal(act.planes, act_early.planes) and torch.equal(act.xscale, act_early.xscale)
     wq, s = gemm_fp8.quantize(torch.randn(896, nh * hd, generator=g, device="cuda") * 0.02)
-    y_ref = gemm_fp8.f8_forward(o, wq, s)
+    y_ref = decode_kernel_gemm(o, wq, s)
     y = gemm_fp8.f8_forward_planes(act, wq, s)
     torch.cuda.synchronize()
     assert torch.equal(y, y_ref)
