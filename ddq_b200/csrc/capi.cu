@@ -57,9 +57,8 @@ int tc_min_m() {
 }
 constexpr int64_t kDecodeMaxM = 64;
 
-// Up to this many tokens a GEMM whose weight slice and activations per SM are
-// small (thin.cu's limits) runs the shared-memory-resident mma.sync kernel
-// instead of the e4m3 decode kernel.
+// Up to this many tokens a GEMM whose shape thin.cu takes runs the
+// shared-memory-resident mma.sync kernel instead of the e4m3 decode kernel.
 // DDQ_THIN_MAX_M overrides (0 switches it off) for benchmarking.
 int64_t thin_max_m() {
   static const int64_t v = [] {
@@ -67,11 +66,6 @@ int64_t thin_max_m() {
     return e ? (int64_t)std::atoll(e) : (int64_t)16;
   }();
   return v;
-}
-bool thin_shape(int64_t M, int64_t N, int64_t K) {
-  if (M > thin_max_m()) return false;
-  const int dev = current_device();
-  return dev >= 0 && thin_eligible(M, N, K, device_sm_count(dev));
 }
 
 // From this many tokens on, a GEMM expands the weights to fp16 once and runs
@@ -89,6 +83,14 @@ bool pf_shape(int64_t M, int64_t N) { return M > kDecodeMaxM && M >= pf_min_m() 
 // Test hooks (ddq_set_debug): bounded-wait limit and fault-injection flags.
 unsigned long long g_wait_timeout_ns = 1000000000ull;  // 1 s
 int g_debug_flags = 0;
+
+// The thin kernel has no fault-injection hook, so while a test sets
+// injection flags the shapes it would take run the decode kernel.
+bool thin_shape(int64_t M, int64_t N, int64_t K) {
+  if (M > thin_max_m() || g_debug_flags != 0) return false;
+  const int dev = current_device();
+  return dev >= 0 && thin_eligible(M, N, K, device_sm_count(dev));
+}
 
 bool tc_eligible(const void* x, const void* wq, int64_t K) {
   return K > 0 && (K % 16 == 0) && aligned16(x) && aligned16(wq);
@@ -140,7 +142,8 @@ extern "C" int ddq_w8a16_gemm(const void* x, const uint8_t* wq, const float* sca
   __half* yh = reinterpret_cast<__half*>(y);
   if (tc_eligible(x, wq, K) && M >= tc_min_m()) {
     if (thin_shape(M, N, K))
-      return launch_thin(xh, wq, scales, bias, bias_dtype, yh, (int)M, (int)N, (int)K, s);
+      return launch_thin(xh, wq, scales, bias, bias_dtype, yh, (int)M, (int)N, (int)K,
+                         g_wait_timeout_ns, s);
     if (M <= kDecodeMaxM)
       return launch_dec(xh, wq, scales, bias, bias_dtype, yh, nullptr, 0, (int)M, (int)N, (int)K,
                         workspace, workspace_bytes, g_wait_timeout_ns, g_debug_flags, s);

@@ -15,17 +15,18 @@
 // busies 76 of 148 SMs and can start only a ring's depth of the stream
 // before the dependency resolves.  Here:
 //   * the weight is cut into 8-row tiles spread evenly over one CTA per SM
-//     (up to 16 tiles each); a CTA copies its whole slice (rows x K bytes,
-//     at most 40 KB) into shared memory with cp.async before
-//     griddepcontrol.wait, which leaves room for the next kernel's CTA on the
-//     same SM, so that it starts its own copy while this one computes;
-//   * after the wait: the M x K fp16 activations (L2, at most 10 KB) into
-//     shared memory, then per (tile, 64-wide K block) one 16-byte weight
-//     load, 16 exact e4m3 -> fp16 conversions and 4 MMAs, tokens on the MMA
-//     rows (zero rows past M), the tile's 8 weight rows on the MMA columns;
+//     (up to 16 tiles each); a CTA copies its whole slice (rows x K bytes)
+//     into shared memory before griddepcontrol.wait, one bulk copy (TMA
+//     engine, no multicast) per row counted on an mbarrier; where the slice
+//     and activations leave room, the next kernel's CTA shares the SM and
+//     starts its own copy while this one computes;
+//   * after the wait: the M x K fp16 activations (L2), one bulk copy per
+//     token row, then per (tile, 64-wide K block) one 16-byte weight load,
+//     16 exact e4m3 -> fp16 conversions and 4 MMAs, tokens on the MMA rows
+//     (zero rows past M), the tile's 8 weight rows on the MMA columns;
 //   * no activation split pre-pass (fp16 activations are used as they are),
-//     no spin-wait of any kind (cp.async.wait_all and griddepcontrol.wait
-//     always complete), no workspace.
+//     no workspace; both mbarrier waits are bounded (DDQ_ERR_TIMEOUT in the
+//     device error word, no output, on expiry).
 //
 // K order inside a 64-wide block: lane quad position t holds the 16
 // consecutive k at 16t .. 16t+15 of its token row (A operand) and of its
@@ -39,6 +40,8 @@
 // row scale (exact).  The eight warps split the (tile, K block) units
 // round-robin, write their partial sums to shared memory and the epilogue
 // adds them in warp order, so results are bitwise reproducible.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "launch.cuh"
 #include "sm100_ptx.cuh"
@@ -50,14 +53,15 @@ constexpr int TH_WARPS = 8;
 constexpr int TH_THREADS = TH_WARPS * 32;
 constexpr int TH_MAX_TILES = 16;     // 8-row tiles per CTA (accumulator registers)
 constexpr int TH_SMEM_MAX = 232448;  // 227 KB opt-in limit per CTA
-// Shapes taken: per CTA at most this much weight slice and activations.
-// Staged by per-thread cp.async (16 B each), larger slices and activation
-// blocks were measured slower than the e4m3 decode kernel (M = 1 gate/up,
-// 64.5 KB slice: 7.2 vs 6.9 us; M = 8: 9.8 vs 6.6 us; M = 8 down, 78 KB of
-// activations: 11.1 vs 6.9 us), smaller ones faster (M = 1 qkv, 7 KB + 1.8 KB:
-// 3.8 vs 5.7 us; M = 1 down, 38.9 KB + 9.7 KB: 4.9 vs 6.6 us).
-constexpr int64_t TH_W_MAX = 40 * 1024;
-constexpr int64_t TH_X_MAX = 10 * 1024;
+// Shapes taken: at most this many (8-row tile, 64-wide K block) units per
+// CTA, or any unit count at M <= 2, as long as shared memory holds the slice
+// and the activations.  Per call in a replayed chain, against the split +
+// e4m3 decode kernel: the Qwen2.5 q/k/v, o and down projections win at every
+// M from 1 to 16 (14-76 units; e.g. M = 16 down 3.95 vs 6.02 us, M = 16
+// 4864 x 896 4.16 vs 5.33 us); gate/up (126 units) wins at M = 1 (5.05 vs
+// 5.43 us) and loses from M = 8 on (5.52 vs 5.39 us; M = 16 6.24 vs 5.44 us),
+// where the per-CTA conversion and MMA work is on the critical path.
+constexpr int64_t TH_MAX_UNITS = 96;
 
 struct ThinArgs {
   const __half* x;
@@ -67,18 +71,21 @@ struct ThinArgs {
   int bias_dtype;
   __half* y;
   int M, N, K;
-  int tiles;        // ceil(N / 8)
-  int off_x, off_sc, off_bi, off_red;  // shared-memory offsets (bytes)
+  int tiles;                 // ceil(N / 8)
+  int sw, sx;                // shared-memory row strides (bytes) of weights and activations
+  int off_x, off_sc, off_bi, off_red, off_bar;  // shared-memory offsets (bytes)
+  unsigned long long timeout_ns;
 };
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() {
-  asm volatile("cp.async.commit_group;" ::: "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.wait_all;" ::: "memory");
+// One bulk (TMA engine) copy global -> this CTA's shared memory, counted on
+// an mbarrier (no multicast).  16-byte aligned addresses, size % 16 == 0.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
+                                         uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
 }
 __device__ __forceinline__ uint4 lds128(uint32_t a) {
   uint4 v;
@@ -86,9 +93,6 @@ __device__ __forceinline__ uint4 lds128(uint32_t a) {
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "r"(a));
   return v;
-}
-__device__ __forceinline__ void sts128_zero(uint32_t a) {
-  asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0u) : "memory");
 }
 
 // d += A (16 x 16, row-major fragment a0..a3) * B (16 x 8, column fragment b0, b1)
@@ -102,14 +106,14 @@ __device__ __forceinline__ void th_mma(float* d, uint32_t a0, uint32_t a1, uint3
 }
 
 // Shared memory (bytes from the dynamic base):
-//   [0, ...)   weight slice: unit (tile tl, K block kb) = 512 B at
-//              (tl * KB + kb) * 512; lane g * 4 + t holds row tl * 8 + g,
-//              k = kb * 64 + 16 t .. + 15
-//   off_x      activations: 16 B at (((kb * 2 + h) * M + m) * 4 + t) * 16
-//              = x[m, kb * 64 + 16 t + 8 h .. + 7]
+//   [0, ...)   weight slice, row-major, row stride sw = K (+64 when K % 128
+//              == 0, so that rows g and g + 1 fall on different banks)
+//   off_x      activations, row-major fp16, row stride sx = 2K + 16 (rows
+//              g and g + 1 on different banks)
 //   off_sc     per-row scale * 256 (fp32), off_bi per-row bias (fp32)
 //   off_red    partial sums [warp][m][tile][8 rows] (fp32); aliases the
 //              weight and activation area, which is dead by then, when it fits
+//   off_bar    weight barrier, activation barrier, abort flag
 template <int NT>
 __global__ void __launch_bounds__(TH_THREADS) w8a16_thin_kernel(const ThinArgs a) {
   extern __shared__ __align__(16) uint8_t th_smem[];
@@ -121,35 +125,34 @@ __global__ void __launch_bounds__(TH_THREADS) w8a16_thin_kernel(const ThinArgs a
   const int ntl = tile1 - tile0;  // 1..NT (the launcher guarantees it)
   const int row0 = tile0 * 8, rows = ntl * 8;
   const int M = a.M, N = a.N, K = a.K;
-  const int KB = K >> 6, kc16 = K >> 4, kc8 = K >> 3;
-
-  // 1) the weight slice, before the dependency (weights are not written by
-  //    the kernel this one depends on)
-  for (int rl = warp; rl < rows; rl += TH_WARPS) {
-    const int n = row0 + rl;
-    const uint8_t* src = a.wq + (size_t)n * K;
-    const uint32_t rbase = sbase + (uint32_t)(((rl >> 3) * KB * 32 + (rl & 7) * 4) * 16);
-    for (int c = lane; c < kc16; c += 32) {
-      const uint32_t dst = rbase + (uint32_t)((((c >> 2) * 32) + (c & 3)) * 16);
-      if (n < N) cp_async16(dst, src + (size_t)c * 16);
-      else sts128_zero(dst);
-    }
+  const int KB = K >> 6;
+  const int valid = min(rows, N - row0);  // rows past N are never stored
+  const uint32_t bar_w = sbase + (uint32_t)a.off_bar, bar_x = bar_w + 8;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(th_smem + a.off_bar + 16);
+  volatile int* drain_flag = reinterpret_cast<volatile int*>(th_smem + a.off_bar + 20);
+  if (tid == 0) {
+    ptx::mbar_init(bar_w, 1);
+    ptx::mbar_init(bar_x, 1);
+    *abort_flag = 0;
+    *drain_flag = 0;
+    ptx::fence_mbar_init();
   }
-  cp_async_commit();
+  __syncthreads();
+
+  // 1) the weight slice, one bulk copy per row, before the dependency
+  //    (weights are not written by the kernel this one depends on)
+  if (tid == 0) ptx::mbar_arrive_expect_tx(bar_w, (uint32_t)(valid * K));
+  if (tid < valid)
+    bulk_g2s(sbase + (uint32_t)(tid * a.sw), a.wq + (size_t)(row0 + tid) * K, (uint32_t)K, bar_w);
 
   ptx::pdl_wait();  // x comes from the previous kernel
   ptx::pdl_launch_dependents();
 
-  // 2) activations (L2), row scales and biases
+  // 2) activations (L2), one bulk copy per token row; row scales and biases
   const uint32_t sx = sbase + (uint32_t)a.off_x;
-  for (int m = warp; m < M; m += TH_WARPS) {
-    const __half* src = a.x + (size_t)m * K;
-    for (int c = lane; c < kc8; c += 32) {
-      const int kb = c >> 3, t = (c & 7) >> 1, h = c & 1;
-      cp_async16(sx + (uint32_t)(((((kb * 2 + h) * M + m) * 4) + t) * 16), src + (size_t)c * 8);
-    }
-  }
-  cp_async_commit();
+  if (tid == 0) ptx::mbar_arrive_expect_tx(bar_x, (uint32_t)(M * K * 2));
+  if (tid < M)
+    bulk_g2s(sx + (uint32_t)(tid * a.sx), a.x + (size_t)tid * K, (uint32_t)(K * 2), bar_x);
   float* sc = reinterpret_cast<float*>(th_smem + a.off_sc);
   float* bi = reinterpret_cast<float*>(th_smem + a.off_bi);
   if (tid < rows) {
@@ -163,15 +166,27 @@ __global__ void __launch_bounds__(TH_THREADS) w8a16_thin_kernel(const ThinArgs a
     sc[tid] = s;
     bi[tid] = bv;
   }
-  cp_async_wait_all();
+  // bounded waits: on a timeout the CTA records DDQ_ERR_TIMEOUT, waits once
+  // more (bounded) for its copies and leaves without writing y
+  if (ptx::mbar_wait(bar_w, 0u, a.timeout_ns, abort_flag))
+    ptx::mbar_wait(bar_x, 0u, a.timeout_ns, abort_flag);
   __syncthreads();
+  if (*abort_flag) {
+    if (tid == 0) {
+      record_device_error(DDQ_ERR_TIMEOUT);
+      ptx::mbar_wait(bar_w, 0u, a.timeout_ns, drain_flag);
+      ptx::mbar_wait(bar_x, 0u, a.timeout_ns, drain_flag);
+    }
+    return;
+  }
 
   // 3) MMAs: warp w takes the units u = tl * KB + kb with u = w (mod 8)
   const int g = lane >> 2, t = lane & 3;
   const bool lo_ok = g < M, hi_ok = g + 8 < M;
-  const uint32_t xlo = sx + (uint32_t)((g * 4 + t) * 16);
-  const uint32_t xhi = sx + (uint32_t)(((g + 8) * 4 + t) * 16);
-  const uint32_t xstep = (uint32_t)(M * 64);  // bytes per (kb, h)
+  const uint32_t wrow = sbase + (uint32_t)(g * a.sw + t * 16);
+  const uint32_t wtile = (uint32_t)(8 * a.sw);
+  const uint32_t xlo = sx + (uint32_t)(g * a.sx + t * 32);
+  const uint32_t xhi = sx + (uint32_t)((g + 8) * a.sx + t * 32);
   float acc[NT][4];
 #pragma unroll
   for (int i = 0; i < NT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
@@ -180,15 +195,15 @@ __global__ void __launch_bounds__(TH_THREADS) w8a16_thin_kernel(const ThinArgs a
     if (tl < ntl) {
       int kb = (warp - (tl * KB) % TH_WARPS + TH_WARPS) % TH_WARPS;
       for (; kb < KB; kb += TH_WARPS) {
-        const uint4 wv = lds128(sbase + (uint32_t)(((tl * KB + kb) * 32 + lane) * 16));
+        const uint4 wv = lds128(wrow + (uint32_t)tl * wtile + (uint32_t)(kb * 64));
         uint4 l0 = make_uint4(0u, 0u, 0u, 0u), l1 = l0, h0 = l0, h1 = l0;
         if (lo_ok) {
-          l0 = lds128(xlo + (uint32_t)(kb * 2) * xstep);
-          l1 = lds128(xlo + (uint32_t)(kb * 2 + 1) * xstep);
+          l0 = lds128(xlo + (uint32_t)(kb * 128));
+          l1 = lds128(xlo + (uint32_t)(kb * 128 + 16));
         }
         if (hi_ok) {
-          h0 = lds128(xhi + (uint32_t)(kb * 2) * xstep);
-          h1 = lds128(xhi + (uint32_t)(kb * 2 + 1) * xstep);
+          h0 = lds128(xhi + (uint32_t)(kb * 128));
+          h1 = lds128(xhi + (uint32_t)(kb * 128 + 16));
         }
         th_mma(acc[tl], l0.x, h0.x, l0.y, h0.y, e4m3x2_to_half2_bits_x2m8(wv.x, 0x4140u),
                e4m3x2_to_half2_bits_x2m8(wv.x, 0x4342u));
@@ -230,10 +245,21 @@ __global__ void __launch_bounds__(TH_THREADS) w8a16_thin_kernel(const ThinArgs a
   }
 }
 
+// Unit limit of the shapes taken at M > 2 (DDQ_THIN_MAX_UNITS overrides it
+// for measurements).
+int64_t thin_max_units() {
+  static const int64_t v = [] {
+    const char* e = std::getenv("DDQ_THIN_MAX_UNITS");
+    return e ? (int64_t)std::atoll(e) : TH_MAX_UNITS;
+  }();
+  return v;
+}
+
 struct ThinPlan {
   bool ok;
   int grid, nt, smem;
-  int off_x, off_sc, off_bi, off_red;
+  int sw, sx;
+  int off_x, off_sc, off_bi, off_red, off_bar;
 };
 
 ThinPlan thin_plan(int64_t M, int64_t N, int64_t K, int sms) {
@@ -244,24 +270,30 @@ ThinPlan thin_plan(int64_t M, int64_t N, int64_t K, int sms) {
   const int64_t grid = tiles < sms ? tiles : sms;
   const int64_t ntl = (tiles + grid - 1) / grid;  // largest per-CTA tile count
   if (ntl > TH_MAX_TILES) return p;
-  const int64_t w_bytes = ntl * 8 * K;
-  const int64_t x_bytes = M * K * 2;
-  if (w_bytes > TH_W_MAX || x_bytes > TH_X_MAX) return p;
+  if (M > 2 && ntl * (K / 64) > thin_max_units()) return p;
+  const int64_t sw = K % 128 == 0 ? K + 64 : K;
+  const int64_t sx = 2 * K + 16;
+  const int64_t w_bytes = ntl * 8 * sw;
+  const int64_t x_bytes = M * sx;
   const int64_t off_sc = w_bytes + x_bytes;                    // multiple of 16
   const int64_t off_bi = off_sc + ntl * 8 * 4;
   const int64_t end = off_bi + ntl * 8 * 4;
   const int64_t red_bytes = (int64_t)TH_WARPS * M * ntl * 8 * 4;
   const int64_t off_red = red_bytes <= w_bytes + x_bytes ? 0 : end;
-  const int64_t total = off_red ? off_red + red_bytes : end;
+  const int64_t off_bar = off_red ? off_red + red_bytes : end;  // multiple of 16
+  const int64_t total = off_bar + 32;
   if (total > TH_SMEM_MAX) return p;
   p.ok = true;
   p.grid = (int)grid;
   p.nt = ntl <= 1 ? 1 : ntl <= 2 ? 2 : ntl <= 4 ? 4 : ntl <= 8 ? 8 : ntl <= 12 ? 12 : 16;
   p.smem = (int)total;
+  p.sw = (int)sw;
+  p.sx = (int)sx;
   p.off_x = (int)w_bytes;
   p.off_sc = (int)off_sc;
   p.off_bi = (int)off_bi;
   p.off_red = (int)off_red;
+  p.off_bar = (int)off_bar;
   return p;
 }
 
@@ -305,7 +337,8 @@ bool thin_eligible(int64_t M, int64_t N, int64_t K, int sms) {
 }
 
 int launch_thin(const __half* x, const uint8_t* wq, const float* scales, const void* bias,
-                int bias_dtype, __half* y, int M, int N, int K, cudaStream_t s) {
+                int bias_dtype, __half* y, int M, int N, int K, unsigned long long timeout_ns,
+                cudaStream_t s) {
   const int sms = device_sm_count(current_device());
   if (sms <= 0) return DDQ_ERR_DEVICE;
   const ThinPlan p = thin_plan(M, N, K, sms);
@@ -322,10 +355,14 @@ int launch_thin(const __half* x, const uint8_t* wq, const float* scales, const v
   a.N = N;
   a.K = K;
   a.tiles = (int)((N + 7) / 8);
+  a.sw = p.sw;
+  a.sx = p.sx;
   a.off_x = p.off_x;
   a.off_sc = p.off_sc;
   a.off_bi = p.off_bi;
   a.off_red = p.off_red;
+  a.off_bar = p.off_bar;
+  a.timeout_ns = timeout_ns;
   switch (p.nt) {
     case 1: return launch_thin_t<1>(p, a, s);
     case 2: return launch_thin_t<2>(p, a, s);

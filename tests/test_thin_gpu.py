@@ -4,8 +4,9 @@ ragged row counts, the smallest K, every per-CTA tile-count variant up to the
 limit of 16, every e4m3 code, the three bias types, chained calls under
 programmatic dependent launch and a CUDA graph, and the dispatch boundaries
 (the kernel count the library reports for a shape).  The kernel takes a
-shape when the activations are at most 10 KB and each SM's weight slice at
-most 40 KB."""
+shape of up to 16 tokens when each CTA holds at most 96 (8-row tile, 64-wide
+K block) units, or any number at 1-2 tokens, and shared memory holds its
+weight slice and the activations."""
 import numpy as np
 import pytest
 import torch
@@ -47,10 +48,8 @@ def sms():
 
 @pytest.mark.parametrize("M", range(1, 17))
 def test_every_token_count(g, lib, M):
-    """q/k/v at 1..16 tokens: the thin kernel up to 5 (5 x 896 x 2 bytes of
-    activations), the decode kernel from 6 on."""
     N, K = 1152, 896
-    assert lib.ddq_w8a16_gemm_kernel_count(M, N, K) == (1 if M <= 5 else 2)
+    assert lib.ddq_w8a16_gemm_kernel_count(M, N, K) == 1
     x, w, b = gen(M, N, K, seed=200 + M)
     wq, s = o.quantize(w)
     y = g.f8_forward(dev(x), dev(wq), dev(s), dev(b))
@@ -60,6 +59,10 @@ def test_every_token_count(g, lib, M):
 
 @pytest.mark.parametrize("M,N,K", [
     (1, 896, 4864),      # down at M = 1: 38.9 KB slice, 9.7 KB activations
+    (16, 896, 4864),     # down at M = 16: 156 KB of activations in shared memory
+    (1, 9728, 896),      # gate/up at M = 1: 126 units per CTA (taken at M <= 2)
+    (2, 9728, 896),
+    (16, 4864, 896),     # 70 units per CTA
     (5, 4864, 896),      # 5 tiles per CTA
     (2, 10656, 512),     # 9 tiles per CTA
     (2, 4000, 640),      # 4 tiles per CTA
@@ -95,10 +98,9 @@ def test_tile_limit_per_cta(g, lib):
 def test_dispatch_boundaries(lib):
     assert lib.ddq_w8a16_gemm_kernel_count(17, 1152, 256) == 2    # more than 16 tokens
     assert lib.ddq_w8a16_gemm_kernel_count(4, 1152, 912) == 2     # K % 64 != 0
-    assert lib.ddq_w8a16_gemm_kernel_count(6, 1152, 896) == 2     # 10.5 KB of activations
-    assert lib.ddq_w8a16_gemm_kernel_count(5, 1152, 896) == 1
-    assert lib.ddq_w8a16_gemm_kernel_count(1, 9728, 896) == 2     # 64.5 KB weight slice per SM
-    assert lib.ddq_w8a16_gemm_kernel_count(1, 896, 4864) == 1
+    assert lib.ddq_w8a16_gemm_kernel_count(2, 9728, 896) == 1     # 126 units, 2 tokens
+    assert lib.ddq_w8a16_gemm_kernel_count(3, 9728, 896) == 2     # 126 units, 3 tokens
+    assert lib.ddq_w8a16_gemm_kernel_count(16, 896, 8192) == 2    # activations exceed shared memory
     assert lib.ddq_w8a16_gemm_kernel_count(16, 1152, 40) == 1     # K % 16 != 0: CUDA-core kernel
     assert lib.ddq_w8a16_gemm_kernel_count(0, 1152, 896) == 0
 
@@ -152,8 +154,7 @@ def test_chained_calls_read_the_previous_output(g):
     """Each call consumes the previous call's output, issued back to back (the
     next kernel copies its weights while the previous one still runs); the
     results equal the same chain with a device synchronisation between calls,
-    bit for bit.  At 3 tokens the chain mixes the thin kernel and (for the
-    4864-wide input) the decode kernel; 16 and 17 tokens run the decode kernel."""
+    bit for bit.  3 and 16 tokens run the thin kernel, 17 the decode kernel."""
     torch.manual_seed(5)
     shapes = [(896, 896), (4864, 896), (896, 4864), (1152, 896)]
     for M in (3, 16, 17):
