@@ -91,12 +91,14 @@ size_t ddq_w8a16_gemm_workspace_size(int64_t M, int64_t N, int64_t K);
  * bias type, gemm_FP8_d.cu:191) or _F32.
  * Requirements: M >= 0, N >= 1, K >= 1; the fast paths need K % 16 == 0 and
  * 16-byte aligned x / wq (a generic CUDA kernel covers the rest).
- * Kernels by shape: M <= 16 with K % 64 == 0, M * K * 2 <= 10 KB of
- * activations and at most 40 KB of weight per SM (one CTA per SM, 8-row
- * tiles; e.g. the Qwen2.5-0.5B q/k/v, o and down projections at M = 1):
- * one kernel, fp16 activations on mma.sync, the workspace unused; other
- * M <= 64: the activation-split pre-pass plus the e4m3 tcgen05 GEMM; larger
- * M: the prefill kernels.  Summation order differs between these kernels, so the
+ * Kernels by shape: M <= 16 with K % 64 == 0, at most 16 tiles of 8 rows
+ * per SM, at most 96 (tile, 64-wide K block) units per SM unless M <= 2, and
+ * the per-SM weight slice plus the activations within shared memory (e.g.
+ * the Qwen2.5-0.5B q/k/v, o and down projections at M = 1..16, gate/up at
+ * M = 1..2): one kernel, fp16 activations on mma.sync, the workspace unused;
+ * other M <= 64: the activation-split pre-pass plus the e4m3 tcgen05 GEMM;
+ * larger M: the prefill kernels.  While ddq_set_debug's injection flags are
+ * set, the first group also takes the split + decode kernels.  Summation order differs between these kernels, so the
  * same row can round differently at different M (all within the fp32
  * tolerance); each kernel is bitwise reproducible.
  */
