@@ -7,11 +7,14 @@ down 4864->896}, e4m3 weights with fp32 per-channel scales drawn from
 N(0, 0.02), fp16 activations from N(0, 1), fp32 biases, run at
 M in {1, 8, 32, 64}.  q, k and v run as one 896->1152 projection (their
 weights stacked at load time, as the engine does; the weight bytes are the
-same), so a layer is 4 dependent GEMMs.  One step = the 24-layer set at each
-of the four M (384 GEMMs).  `value` is algorithmic bytes (weights + scales +
+same), so a layer is 4 GEMMs ordered on one stream (each starts its
+activation reads only after the previous one has completed, as dependent
+GEMMs do).  One pass = the 24-layer set at each of the four M (384 GEMMs);
+one step = SETS_PER_STEP passes, so that the timed region lasts long enough
+for the clock sampler.  `value` is algorithmic bytes (weights + scales +
 bias + activations in + outputs) per second over all ranks, in TB/s, with
 every input resident in HBM; the 357.8 MB of weights per pass exceed the
-126 MB L2, so every pass reads them from HBM.  The step is captured once in a
+126 MB L2, so every pass reads them from HBM.  The pass is captured once in a
 CUDA graph and replayed.
 
 `e2e` is the same metric through the public API (ddq_b200.gemm_fp8.f8_forward,
@@ -22,7 +25,9 @@ eagerly from Python.
 
 `--impl reference` times the reference semantics on the host cores (the CPU
 oracle in PyTorch: per-call dequantisation + fp32 matmul), which is the
-reference's CPU path for this metric.
+reference's CPU path for this metric; where a GPU and the reference's own
+CUDA operators (built from its sources into oracle/_ref) are present, that
+line also carries those kernels' times on the same shapes.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 """
@@ -52,6 +57,9 @@ PROJS = [("qkv", 896, 1152, True), ("o", 896, 896, False), ("gate_up", 896, 9728
          ("down", 4864, 896, False)]
 GATE_UP = 2  # index of gate/up in PROJS
 DECODE_M = (1, 8, 32, 64)
+SETS_PER_STEP = 32  # passes of the 384-GEMM set per timed step
+# ncu summary whose traffic line belongs to the roofline kernel below
+ROOFLINE_PROFILE = os.path.join(REPO, "profiles", "w8a16_dec_gateup_m64.md")
 
 
 def proj_bytes(M, K, N, bias):
@@ -197,7 +205,7 @@ def run_ours(args, rank, world, device):
         step(side.cuda_stream)
     torch.cuda.synchronize(device)
 
-    for _ in range(args.warmup):
+    for _ in range(args.warmup * SETS_PER_STEP):
         graph.replay()
     torch.cuda.synchronize(device)
     if world > 1:
@@ -206,7 +214,7 @@ def run_ours(args, rank, world, device):
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(device.index) as clk:
         ev0.record()
-        for _ in range(args.steps):
+        for _ in range(args.steps * SETS_PER_STEP):
             graph.replay()
         ev1.record()
         torch.cuda.synchronize(device)
@@ -215,7 +223,7 @@ def run_ours(args, rank, world, device):
     torch.cuda.synchronize(device)
     ms = ev0.elapsed_time(ev1)
     ms_max = reduce_max(ms, world, device)
-    sbytes = step_bytes()
+    sbytes = step_bytes() * SETS_PER_STEP
     value = sbytes * args.steps * world / (ms_max * 1e-3) / 1e12
 
     # ---- roofline of the dominant kernel: gate/up (58% of the bytes).  Its
@@ -258,15 +266,12 @@ def run_ours(args, rank, world, device):
 
     nb, avg = dom
     achieved = nb / (avg * 1e-3) / 1e9
-    # DRAM bytes per call (dram__bytes_read.sum + dram__bytes_write.sum of the
-    # split pre-pass and the GEMM) from one ncu --set full capture of this
-    # shape; profiles/w8a16_dec_gateup_m64.md has the command and the figures.
-    traffic = 8974336 + 120832
-    roofline = {"kernel": "w8a16_dec_kernel + xsplit_kernel (gate/up 896->9728, M=64)",
+    traffic, traffic_src = profile_traffic(ROOFLINE_PROFILE)
+    roofline = {"kernel": roofline_kernel_name(),
                 "bound": "hbm",
                 "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
-                "traffic": traffic, "bytes_per_launch": nb,
+                "traffic": traffic, "traffic_source": traffic_src, "bytes_per_launch": nb,
                 "timing": "average over a back-to-back chain of 96 calls, CUDA events on the launch stream"}
 
     # ---- e2e through the public API, host buffers, copies inside the timed region
@@ -278,7 +283,7 @@ def run_ours(args, rank, world, device):
     del wl, calls, graph
     torch.cuda.empty_cache()
     prefill = None if args.skip_extra else run_prefill(args, device, world, peaks)
-    lmhead = None if args.skip_extra else run_lm_head(args, device, world, peaks)
+    lmhead = None if args.skip_extra else run_lm_head(args, device, rank, world, peaks)
     config1 = None if args.skip_extra else run_config1(args, device, world, peaks)
     generation = None if args.skip_extra else run_generation(args, device, rank, world, peaks)
 
@@ -289,15 +294,18 @@ def run_ours(args, rank, world, device):
     line = {
         "metric": METRIC, "value": round(value, 4), "unit": "TB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
+        "ms_per_pass": round(ms_max / (args.steps * SETS_PER_STEP), 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e4m3xf16->f32",
         "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations; no dataset)",
         "config": {"workload": "config2: 24-layer decode projection set at M=1,8,32,64",
                    "layers": LAYERS, "M": list(DECODE_M),
                    "shapes": [f"{n} {k}->{nn}" + ("+bias" if b else "") for n, k, nn, b in PROJS],
                    "qkv": "q 896->896, k 896->128, v 896->128 (+bias) stacked into one GEMM",
-                   "bytes_per_step": sbytes, "gemms_per_step": n_gemms,
+                   "passes_per_step": SETS_PER_STEP, "bytes_per_step": sbytes,
+                   "gemms_per_pass": n_gemms,
                    "l2": "inputs larger than L2 (357.8 MB of weights per M pass > 126 MB)",
-                   "timing": "CUDA graph of one step, replayed; CUDA events; max over ranks",
+                   "timing": "CUDA graph of one pass, replayed SETS_PER_STEP times per step; "
+                             "CUDA events; max over ranks",
                    "parallelism": f"replicas x{world}"},
         "per_m_gate_up": per_m,
         "prefill": prefill,
@@ -306,7 +314,7 @@ def run_ours(args, rank, world, device):
         "generation": generation,
         "roofline": roofline,
         "e2e": e2e,
-        "gpu_launches": n_launches * args.steps,
+        "gpu_launches": n_launches * args.steps * SETS_PER_STEP,
         "clocks": clk.summary(),
         "cpu_baseline": cpu,
     }
@@ -402,25 +410,41 @@ def run_config1(args, device, world, peaks):
             "frac_of_hbm_peak": round(nb / (us * 1e-6) / 1e9 / peaks["hbm_gbs"], 4)}
 
 
-def run_lm_head(args, device, world, peaks):
-    """Config 4: fused lm_head 896 -> 151936 greedy argmax at M = 1, 16, 64 (one GPU's
-    full vocabulary; the vocab-sharded variant is exercised by the tests)."""
+def run_lm_head(args, device, rank, world, peaks):
+    """Config 4: fused lm_head 896 -> 151936 with greedy argmax at M = 1, 16, 64.
+
+    At N = 1 the whole vocabulary is on one GPU.  Under torchrun with N > 1
+    the vocabulary is sharded: rank r owns the contiguous rows
+    shard_range(V, r, N), runs the fused kernel on them, and the per-rank
+    packed (max, index) words are combined with one NCCL all-gather of M int64
+    per rank and an element-wise max (``lm_head.sharded_greedy``).  Reported
+    per M: the shard kernel per call (a replayed CUDA graph cycling through
+    copies of the shard that together exceed twice the L2, so every call reads
+    HBM), its HBM fraction, the all-gather per call and the whole sharded pick
+    per call (eager, CUDA events, max over ranks), and on rank 0 the number of
+    token ids that differ from the unsharded pick over the full vocabulary."""
+    import torch.distributed as dist
     from ddq_b200 import gemm_fp8, lm_head
     V = 151936
+    lo, hi = lm_head.shard_range(V, rank, world)
     g = torch.Generator(device=device).manual_seed(88)
-    copies = [gemm_fp8.quantize(torch.randn(V, HIDDEN, generator=g, device=device) * 0.02)
-              for _ in range(2)]
-    out = {}
+    w = torch.randn(V, HIDDEN, generator=g, device=device) * 0.02  # same draw on every rank
+    wq, sc = gemm_fp8.quantize(w[lo:hi].contiguous())
+    full = gemm_fp8.quantize(w) if (world > 1 and rank == 0) else None
+    del w
+    shard_bytes = (hi - lo) * HIDDEN
+    l2 = torch.cuda.get_device_properties(device).L2_cache_size
+    ncopy = max(2, -(-2 * l2 // shard_bytes) + 1)
+    copies = [(wq, sc)] + [(wq.clone(), sc.clone()) for _ in range(ncopy - 1)]
+    out = {"shards": world, "rows_per_shard": hi - lo, "weight_copies": ncopy}
     side = torch.cuda.Stream(device)
-    for M in (1, 16, 64):
-        x = torch.randn(M, HIDDEN, generator=g, device=device).half()
-        reps = 10
+    xs = {M: torch.randn(M, HIDDEN, generator=g, device=device).half() for M in (1, 16, 64)}
+    for M, x in xs.items():
+        reps = max(10, ncopy)
 
-        def calls():  # alternate two weight copies (2 x 136 MB > L2): every call reads HBM
+        def calls():
             for i in range(reps):
-                lm_head.lm_head_argmax(x, *copies[i % 2])
-        # timed as a replayed CUDA graph (as the engine runs it), so host-side
-        # Python overhead between calls does not count
+                lm_head.lm_head_argmax(x, *copies[i % ncopy], vocab_offset=lo)
         side.wait_stream(torch.cuda.current_stream(device))
         with torch.cuda.stream(side):
             calls()
@@ -439,10 +463,50 @@ def run_lm_head(args, device, world, peaks):
         torch.cuda.synchronize(device)
         del graph
         us = reduce_max(e0.elapsed_time(e1), world, device) * 1e3 / (3 * reps)
-        nb = V * HIDDEN + 4 * V + 2 * M * HIDDEN + 8 * M
-        out[str(M)] = {"us": round(us, 2), "gbs": round(nb / (us * 1e-6) / 1e9, 1),
-                       "frac_of_hbm_peak": round(nb / (us * 1e-6) / 1e9 / peaks["hbm_gbs"], 4)}
-    del copies
+        nb = shard_bytes + 4 * (hi - lo) + 2 * M * HIDDEN + 8 * M
+        rec = {"us": round(us, 2), "gbs": round(nb / (us * 1e-6) / 1e9, 1),
+               "frac_of_hbm_peak": round(nb / (us * 1e-6) / 1e9 / peaks["hbm_gbs"], 4),
+               "bytes_per_call": nb}
+        if world > 1:
+            # the exchange alone, then the whole sharded pick (kernel + all-gather + max)
+            _, packed = lm_head.lm_head_argmax(x, wq, sc, vocab_offset=lo)
+            gathered = torch.empty(world * M, dtype=torch.int64, device=device)
+            for _ in range(5):
+                dist.all_gather_into_tensor(gathered, packed)
+            torch.cuda.synchronize(device)
+            dist.barrier()
+            n = 50
+            e0.record()
+            for _ in range(n):
+                dist.all_gather_into_tensor(gathered, packed)
+            e1.record()
+            torch.cuda.synchronize(device)
+            rec["all_gather_us"] = round(reduce_max(e0.elapsed_time(e1), world, device)
+                                         * 1e3 / n, 2)
+            for _ in range(3):
+                ids = lm_head.sharded_greedy(x, wq, sc, lo)
+            torch.cuda.synchronize(device)
+            dist.barrier()
+            e0.record()
+            for _ in range(n):
+                ids = lm_head.sharded_greedy(x, wq, sc, lo)
+            e1.record()
+            torch.cuda.synchronize(device)
+            rec["sharded_pick_us"] = round(reduce_max(e0.elapsed_time(e1), world, device)
+                                           * 1e3 / n, 2)
+            if rank == 0:
+                ref_ids, _ = lm_head.lm_head_argmax(x, *full)
+                rec["mismatch_vs_unsharded"] = int((ids != ref_ids).sum())
+        out[str(M)] = rec
+    if world > 1:
+        m = [out[k] for k in ("1", "16", "64")]
+        limit = ("all-gather" if all(r["all_gather_us"] > r["us"] for r in m)
+                 else "shard kernel" if all(r["all_gather_us"] < r["us"] for r in m) else "mixed")
+        out["limited_by"] = limit
+        out["timing"] = ("shard kernel: replayed CUDA graph; all-gather and sharded pick: eager "
+                         "calls between CUDA events (host launch gaps included); max over ranks")
+    del copies, full
+    torch.cuda.empty_cache()
     return out
 
 
@@ -482,6 +546,9 @@ def run_generation(args, device, rank, world, peaks):
     kv = L * 2 * per * Hkv * ctx * D * 2
     step_bytes_gpu = L * layer_w + lm_w + kv
     step_ms = (ms - prefill_ms) / max(1, args.gen_new_tokens - 1)
+    parity = None
+    if world == 1 and not args.no_parity:
+        parity = generation_parity(eng, prompts, toks)
     del eng
     torch.cuda.empty_cache()
     return {"workload": f"config5: {per * world} prompts x {args.gen_prompt_len} random ids, "
@@ -492,7 +559,30 @@ def run_generation(args, device, rank, world, peaks):
             "decode_step_hbm_bytes_per_gpu": int(step_bytes_gpu),
             "decode_roofline_frac": round(step_bytes_gpu / (step_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
                                           4),
-            "tokens": int(total), "checksum": int(toks.sum().item()) % 1000003}
+            "tokens": int(total), "checksum": int(toks.sum().item()) % 1000003,
+            "parity": parity}
+
+
+def generation_parity(eng, prompts, toks):
+    """Greedy parity of the timed run's tokens against the reference semantics
+    (``ddq_b200.parity``): the oracle engine (fp32 projections of the same
+    dequantised weights, fp16 logits, lowest-index argmax) teacher-forced on
+    the same context at every step, and running free from the same prompts."""
+    from ddq_b200 import parity
+    from ddq_b200.engine import Engine
+    w = {"embed": eng.embed, "final_norm": eng.final_norm, "layers": eng.layers,
+         "lm_head": eng.lm_head}
+    oracle = Engine(eng.cfg, w, eng.device, linear="oracle")
+    tf = parity.teacher_forced_report(oracle, prompts, toks, max_listed=32)
+    free = parity.free_run_report(oracle, prompts, toks)
+    for layer in eng.layers:    # drop the oracle's fp32 weight copies
+        for p in layer.values():
+            if hasattr(p, "_wdeq"):
+                p._wdeq = None
+    eng.lm_head._wdeq = None
+    return {"teacher_forced": tf, "free_run": free,
+            "judge": "same graph with fp32 projections of the dequantised weights, fp16 logits, "
+                     "lowest-index argmax; margin = oracle fp16 logit of its pick minus of ours"}
 
 
 def launches_per_step(calls):
@@ -655,6 +745,7 @@ def run_reference(args, rank, world):
     value = nbytes * args.steps / dt / 1e12
     sample = ("each step = 1 of the 24 layers of the config-2 projection set at M=1,8,32,64 "
               "(14.9 MB of weights per M), PyTorch CPU oracle with per-call dequant")
+    gpu = reference_gpu_kernels()
     return {
         "impl": "reference", "metric": METRIC, "value": round(value, 6), "unit": "TB/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -668,7 +759,74 @@ def run_reference(args, rank, world):
                          "kind": "port", "sample": sample, "cpu": cpu_model()},
         "e2e": {"value": round(value, 6), "unit": "TB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
+        "reference_gpu_kernels": gpu,
     }
+
+
+def reference_gpu_kernels():
+    """The reference's own CUDA operators on this box's GPU, on the shapes this
+    repo's line reports: gemm_FP8_d.cu f8_forward (its W8A16 kernel,
+    gemm_FP8_d.cu:94-146, 171-210), gemm_d.cu forward (the engine's cuBLAS fp16
+    projection, gemm_d.cu:36-87) and sampler_d.cu forward (greedy argmax,
+    sampler_d.cu:51-70), compiled unmodified from the reference's sources for
+    sm_100 into oracle/_ref.  Each shape cycles through weight copies that
+    together exceed twice the L2; eager calls on the default stream (the
+    operators allocate their outputs and gemm_d's cuBLAS handle is not bound
+    to a stream) between CUDA events, after warm-up.  None when no GPU or no
+    prebuilt operators are present."""
+    if not torch.cuda.is_available():
+        return None
+    try:
+        from oracle.build_ref import available, load_ref
+        if not all(available(n) for n in ("ref_gemm_fp8", "ref_gemm_d", "ref_sampler")):
+            return {"unavailable": "reference operators not built into oracle/_ref"}
+        fp8, gd, smp = load_ref("ref_gemm_fp8"), load_ref("ref_gemm_d"), load_ref("ref_sampler")
+    except Exception as exc:  # an import failure is reported, not fatal to the CPU arm
+        return {"unavailable": f"loading the reference operators failed: {exc!r}"[:300]}
+    dev = torch.device("cuda", 0)
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    g = torch.Generator(device=dev).manual_seed(5)
+    out = {}
+
+    def timed(fn, reps):
+        for _ in range(3):
+            fn(0)
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(reps):
+            fn(i)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) * 1e3 / reps
+
+    for name, M, N, K in (("config1 M=16 896->4864", 16, 4864, 896),
+                          ("gate_up M=64 896->9728", 64, 9728, 896),
+                          ("gate_up M=4096 896->9728", 4096, 9728, 896)):
+        w16 = (torch.randn(N, K, generator=g, device=dev) * 0.02).half()
+        wq, scales = fp8.quantize(w16)
+        x = torch.randn(M, K, generator=g, device=dev).half()
+        nc = max(2, -(-2 * l2 // (N * K)) + 1)
+        q_copies = [(wq.clone(), scales.clone()) for _ in range(nc)]
+        h_copies = [w16.clone() for _ in range(max(2, -(-2 * l2 // (2 * N * K)) + 1))]
+        reps = 5 if M >= 4096 else 50
+        us_f8 = timed(lambda i: fp8.f8_forward(x, *q_copies[i % nc]), reps)
+        us_gd = timed(lambda i: gd.forward(x, h_copies[i % len(h_copies)], None), reps)
+        nb8 = N * K + 4 * N + 2 * M * K + 2 * M * N
+        nb16 = 2 * N * K + 2 * M * K + 2 * M * N
+        fl = 2 * M * N * K
+        out[name] = {
+            "f8_forward_us": round(us_f8, 2), "f8_forward_gbs": round(nb8 / us_f8 / 1e3, 1),
+            "f8_forward_tflops": round(fl / us_f8 / 1e6, 2),
+            "gemm_d_cublas_fp16_us": round(us_gd, 2), "gemm_d_gbs": round(nb16 / us_gd / 1e3, 1),
+            "gemm_d_tflops": round(fl / us_gd / 1e6, 2)}
+        del q_copies, h_copies, w16, wq, scales
+    lg = torch.randn(64, 1, 151936, generator=g, device=dev).half()
+    out["sampler argmax [64,1,151936]"] = {"us": round(timed(lambda i: smp.forward(lg), 50), 2)}
+    out["timing"] = ("eager calls, CUDA events on the default stream, weight copies > 2x L2; "
+                     "reference operators compiled unmodified for sm_100 (oracle/_ref)")
+    torch.cuda.empty_cache()
+    return out
 
 
 # ----------------------------------------------------------------------------- utils
@@ -682,6 +840,23 @@ def load_peaks():
     except (OSError, KeyError, ValueError):
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
                 "source": "fallback (profiling recipe)"}
+
+
+def roofline_kernel_name():
+    return "w8a16_dec_kernel + xsplit_kernel (gate/up 896->9728, M=64)"
+
+
+def profile_traffic(path):
+    """DRAM bytes per launch of the roofline kernel (dram__bytes_read.sum +
+    dram__bytes_write.sum from one ncu capture), read from the summary's
+    `traffic_bytes_per_launch:` line; (None, reason) if the summary lacks it."""
+    try:
+        for ln in open(path):
+            if ln.strip().startswith("traffic_bytes_per_launch:"):
+                return int(ln.split(":", 1)[1].strip().split()[0]), os.path.relpath(path, REPO)
+    except (OSError, ValueError):
+        pass
+    return None, f"no traffic_bytes_per_launch line in {os.path.relpath(path, REPO)}"
 
 
 def reduce_max(v, world, device):
@@ -706,6 +881,8 @@ def main():
     ap.add_argument("--gen-prompts", type=int, default=64)
     ap.add_argument("--gen-prompt-len", type=int, default=512)
     ap.add_argument("--gen-new-tokens", type=int, default=256)
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the greedy-parity check of the generation run (not timed)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

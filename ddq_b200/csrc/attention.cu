@@ -757,17 +757,13 @@ int launch_decode_attention(const __half* qkv, int64_t qkv_stride, __half* kc, _
     if (st) return st;
     const int dev = current_device();
     if (dev < 0 || dev >= 64) return DDQ_ERR_DEVICE;
-    static bool attr_set[2][AT_GMAX][64] = {};
+    static SmemAttrOnce attr[2][AT_GMAX];
     const int smem = (int)sizeof(AmSmem) + 1024;
     cfg.blockDim = dim3(AM_NW * 32);
     cfg.dynamicSmemBytes = smem;
     auto go = [&](auto kern, int gi) -> int {
-      if (!attr_set[split][gi][dev]) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-            cudaSuccess)
-          return DDQ_ERR_LAUNCH;
-        attr_set[split][gi][dev] = true;
-      }
+      const int ast = ensure_smem_attr(attr[split ? 1 : 0][gi], dev, kern, smem);
+      if (ast) return ast;
       e = cudaLaunchKernelEx(&cfg, kern, tk, tv, a, timeout_ns);
       return DDQ_OK;
     };

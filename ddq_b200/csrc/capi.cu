@@ -84,10 +84,12 @@ bool pf_shape(int64_t M, int64_t N) { return M > kDecodeMaxM && M >= pf_min_m() 
 unsigned long long g_wait_timeout_ns = 1000000000ull;  // 1 s
 int g_debug_flags = 0;
 
-// The thin kernel has no fault-injection hook, so while a test sets
-// injection flags the shapes it would take run the decode kernel.
+// The thin kernel has no fault-injection hook, so while a test sets the
+// injection flag (bit 0) or asks for the split + decode kernels (bit 2), the
+// shapes it would take run the decode kernel; the trace flag (bit 1) alone
+// keeps it (it writes phase stamps too).
 bool thin_shape(int64_t M, int64_t N, int64_t K) {
-  if (M > thin_max_m() || g_debug_flags != 0) return false;
+  if (M > thin_max_m() || (g_debug_flags & ~2) != 0) return false;
   const int dev = current_device();
   return dev >= 0 && thin_eligible(M, N, K, device_sm_count(dev));
 }
@@ -96,6 +98,9 @@ bool tc_eligible(const void* x, const void* wq, int64_t K) {
   return K > 0 && (K % 16 == 0) && aligned16(x) && aligned16(wq);
 }
 }  // namespace
+
+unsigned long long wait_timeout_ns() { return g_wait_timeout_ns; }
+int debug_flags() { return g_debug_flags; }
 
 }  // namespace ddq
 
@@ -143,7 +148,7 @@ extern "C" int ddq_w8a16_gemm(const void* x, const uint8_t* wq, const float* sca
   if (tc_eligible(x, wq, K) && M >= tc_min_m()) {
     if (thin_shape(M, N, K))
       return launch_thin(xh, wq, scales, bias, bias_dtype, yh, (int)M, (int)N, (int)K,
-                         g_wait_timeout_ns, s);
+                         g_wait_timeout_ns, s, g_debug_flags);
     if (M <= kDecodeMaxM)
       return launch_dec(xh, wq, scales, bias, bias_dtype, yh, nullptr, 0, (int)M, (int)N, (int)K,
                         workspace, workspace_bytes, g_wait_timeout_ns, g_debug_flags, s);

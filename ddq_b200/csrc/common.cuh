@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cfloat>
+#include <mutex>
 
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
@@ -130,5 +131,36 @@ int check_launch();
 bool pdl_enabled();
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Limit of every device-side bounded wait and the debug flags, as set by
+// ddq_set_debug (capi.cu).
+unsigned long long wait_timeout_ns();
+int debug_flags();
+
+// Raises a kernel's dynamic shared-memory limit once per device, safe under
+// concurrent first calls from several host threads (std::call_once per
+// device).  cudaFuncSetAttribute is not a stream operation, so the first
+// launch of each kernel on a device must come before any stream capture.
+// A failure is cleared from the runtime's error state and returned to every
+// later caller.
+constexpr int kMaxDev = 64;
+struct SmemAttrOnce {
+  std::once_flag once[kMaxDev];
+  int status[kMaxDev] = {};
+};
+template <typename Kernel>
+int ensure_smem_attr(SmemAttrOnce& o, int dev, Kernel kern, int bytes) {
+  if (dev < 0 || dev >= kMaxDev) return DDQ_ERR_DEVICE;
+  std::call_once(o.once[dev], [&] {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      o.status[dev] = DDQ_ERR_LAUNCH;
+    } else {
+      o.status[dev] = DDQ_OK;
+    }
+  });
+  return o.status[dev];
+}
 
 }  // namespace ddq

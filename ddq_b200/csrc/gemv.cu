@@ -280,16 +280,9 @@ static int launch_skinny_t(const __half* x, const uint8_t* wq, const float* scal
   if (smem > 200 * 1024) return DDQ_ERR_SHAPE;
   auto kern = gemv_skinny_kernel<MT, ARGMAX>;
   const int dev = current_device();
-  if (dev < 0 || dev >= 64) return DDQ_ERR_DEVICE;
-  // Raise the dynamic shared-memory limit once per device (not a stream
-  // operation, so the first call must come before any stream capture).
-  static bool attr_set[64] = {};
-  if (!attr_set[dev]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
-        cudaSuccess)
-      return DDQ_ERR_LAUNCH;
-    attr_set[dev] = true;
-  }
+  static SmemAttrOnce attr;
+  const int ast = ensure_smem_attr(attr, dev, kern, 200 * 1024);
+  if (ast) return ast;
   const int sms = device_sm_count(dev);
   if (sms <= 0) return DDQ_ERR_DEVICE;
   const int per_sm = smem <= 48 * 1024 ? 4 : (smem <= 100 * 1024 ? 2 : 1);

@@ -51,7 +51,7 @@ int launch_dec(const __half* x, const uint8_t* wq, const float* scales, const vo
 bool thin_eligible(int64_t M, int64_t N, int64_t K, int sms);
 int launch_thin(const __half* x, const uint8_t* wq, const float* scales, const void* bias,
                 int bias_dtype, __half* y, int M, int N, int K, unsigned long long timeout_ns,
-                cudaStream_t s);
+                cudaStream_t s, int debug_flags = 0);
 // Prefill shapes: exact e4m3 -> fp16 weight expansion into the workspace
 // (N * K * 2 bytes), then the fp16 tensor-core GEMM (tc_prefill.cu).
 size_t pf_workspace_bytes(int64_t N, int64_t K);

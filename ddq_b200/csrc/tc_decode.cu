@@ -934,15 +934,9 @@ int launch_dec_t(const DecPlan& p, const uint8_t* wq, const uint8_t* planes, DcA
                  cudaStream_t s) {
   using Lay = DcLayout<BT, ST, KB>;
   auto kern = w8a16_dec_kernel<BT, ST, KB, EPI>;
-  const int dev = current_device();
-  if (dev < 0 || dev >= 64) return DDQ_ERR_DEVICE;
-  static bool attr_set[64] = {};
-  if (!attr_set[dev]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::ALLOC) !=
-        cudaSuccess)
-      return DDQ_ERR_LAUNCH;
-    attr_set[dev] = true;
-  }
+  static SmemAttrOnce attr;
+  const int ast = ensure_smem_attr(attr, current_device(), kern, Lay::ALLOC);
+  if (ast) return ast;
   CUtensorMap tm_w, tm_x, tm_y;
   int st = dc_tmap(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, (uint64_t)a.K, (uint64_t)a.N,
                    (uint64_t)a.K, DC_AK, DC_BN, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -1111,23 +1105,50 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes]
 
 namespace {
 std::mutex g_noalloc_mu;
-void* g_noalloc_addr[64];  // device address of g_noalloc_scratch, per device
+// Device address of g_noalloc_scratch per device, with the context it was
+// looked up in: after cudaDeviceReset (or a released and re-created primary
+// context) the module is loaded again, possibly at another address, so a
+// change of context triggers a new lookup.
+struct NoallocAddr {
+  void* ctx;
+  void* addr;
+};
+NoallocAddr g_noalloc_addr[64];
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  return fn;
+}
 
 // The array's name in host code is only a host-side stand-in; the device
-// address comes from cudaGetSymbolAddress, asked once per device with that
-// device current.
+// address comes from cudaGetSymbolAddress, asked once per device (and again
+// after its context changed) with that device current.
 int noalloc_scratch(int dev, void** out) {
   if (dev < 0 || dev >= 64) return DDQ_ERR_DEVICE;
+  CtxGetCurrentFn get = ctx_get_current();
+  CUcontext ctx = nullptr;
+  if (!get || get(&ctx) != CUDA_SUCCESS) return DDQ_ERR_DEVICE;
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_addr[dev]) {
+  NoallocAddr& e = g_noalloc_addr[dev];
+  if (!e.addr || e.ctx != (void*)ctx) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) {
       cudaGetLastError();
       return DDQ_ERR_DEVICE;
     }
-    g_noalloc_addr[dev] = p;
+    e.addr = p;
+    e.ctx = (void*)ctx;
   }
-  *out = g_noalloc_addr[dev];
+  *out = e.addr;
   return DDQ_OK;
 }
 }  // namespace
@@ -1160,5 +1181,6 @@ extern "C" int ddq_w8a16_gemm_noalloc(const void* x, const uint8_t* wq, const fl
   if (st != DDQ_OK) return st;
   return launch_dec(reinterpret_cast<const __half*>(x), wq, scales, bias, bias_dtype,
                     reinterpret_cast<__half*>(y), nullptr, 0, (int)M, (int)N, (int)K, scratch,
-                    kNoAllocScratchBytes, 1000000000ull, 0, reinterpret_cast<cudaStream_t>(stream));
+                    kNoAllocScratchBytes, wait_timeout_ns(), debug_flags(),
+                    reinterpret_cast<cudaStream_t>(stream));
 }

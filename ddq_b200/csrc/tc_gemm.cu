@@ -652,15 +652,9 @@ int launch_tc_t(const TcPlan& p, const __half* x, const uint8_t* wq, TcArgs a, i
                 cudaStream_t s) {
   using Lay = TcLayout<BT, WS, AS, XS>;
   auto kern = w8a16_tc_kernel<BT, WS, AS, XS, ARGMAX>;
-  const int dev = current_device();
-  if (dev < 0 || dev >= 64) return DDQ_ERR_DEVICE;
-  static bool attr_set[64] = {};
-  if (!attr_set[dev]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::ALLOC) !=
-        cudaSuccess)
-      return DDQ_ERR_LAUNCH;
-    attr_set[dev] = true;
-  }
+  static SmemAttrOnce attr;
+  const int ast = ensure_smem_attr(attr, current_device(), kern, Lay::ALLOC);
+  if (ast) return ast;
   CUtensorMap tm_w, tm_x, tm_y;
   int st = make_tmap_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, (uint64_t)a.K, (uint64_t)a.N,
                         (uint64_t)a.K, TC_WK, TC_BN, CU_TENSOR_MAP_SWIZZLE_NONE);

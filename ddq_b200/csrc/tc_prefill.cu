@@ -526,13 +526,9 @@ int launch_pf(const __half* x, const uint8_t* wq, const float* scales, const voi
   }
   // 2) the fp16 GEMM
   auto kern = swiglu ? w8a16_pf_kernel<true> : w8a16_pf_kernel<false>;
-  static bool attr_set[2][64] = {};
-  if (!attr_set[swiglu][dev]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PfLayout::ALLOC) !=
-        cudaSuccess)
-      return DDQ_ERR_LAUNCH;
-    attr_set[swiglu][dev] = true;
-  }
+  static SmemAttrOnce attr[2];
+  const int ast = ensure_smem_attr(attr[swiglu ? 1 : 0], dev, kern, PfLayout::ALLOC);
+  if (ast) return ast;
   CUtensorMap tm_x, tm_w, tm_y;
   int st = pf_tmap(&tm_x, x, (uint64_t)K, (uint64_t)M, PF_BK, PF_BM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st) return st;

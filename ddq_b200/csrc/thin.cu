@@ -75,6 +75,7 @@ struct ThinArgs {
   int sw, sx;                // shared-memory row strides (bytes) of weights and activations
   int off_x, off_sc, off_bi, off_red, off_bar;  // shared-memory offsets (bytes)
   unsigned long long timeout_ns;
+  int trace;                 // debug flag bit 1: per-CTA phase stamps (trace_stamp)
 };
 
 // One bulk (TMA engine) copy global -> this CTA's shared memory, counted on
@@ -130,6 +131,8 @@ __global__ void __launch_bounds__(TH_THREADS) w8a16_thin_kernel(const ThinArgs a
   const uint32_t bar_w = sbase + (uint32_t)a.off_bar, bar_x = bar_w + 8;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(th_smem + a.off_bar + 16);
   volatile int* drain_flag = reinterpret_cast<volatile int*>(th_smem + a.off_bar + 20);
+  const bool tr = a.trace != 0;
+  if (tid == 0) trace_stamp(tr, 0);
   if (tid == 0) {
     ptx::mbar_init(bar_w, 1);
     ptx::mbar_init(bar_x, 1);
@@ -144,9 +147,11 @@ __global__ void __launch_bounds__(TH_THREADS) w8a16_thin_kernel(const ThinArgs a
   if (tid == 0) ptx::mbar_arrive_expect_tx(bar_w, (uint32_t)(valid * K));
   if (tid < valid)
     bulk_g2s(sbase + (uint32_t)(tid * a.sw), a.wq + (size_t)(row0 + tid) * K, (uint32_t)K, bar_w);
+  if (tid == 0) trace_stamp(tr, 2);
 
   ptx::pdl_wait();  // x comes from the previous kernel
   ptx::pdl_launch_dependents();
+  if (tid == 0) trace_stamp(tr, 3);
 
   // 2) activations (L2), one bulk copy per token row; row scales and biases
   const uint32_t sx = sbase + (uint32_t)a.off_x;
@@ -171,6 +176,7 @@ __global__ void __launch_bounds__(TH_THREADS) w8a16_thin_kernel(const ThinArgs a
   if (ptx::mbar_wait(bar_w, 0u, a.timeout_ns, abort_flag))
     ptx::mbar_wait(bar_x, 0u, a.timeout_ns, abort_flag);
   __syncthreads();
+  if (tid == 0) trace_stamp(tr, 5);
   if (*abort_flag) {
     if (tid == 0) {
       record_device_error(DDQ_ERR_TIMEOUT);
@@ -217,6 +223,7 @@ __global__ void __launch_bounds__(TH_THREADS) w8a16_thin_kernel(const ThinArgs a
     }
   }
   __syncthreads();  // weights and activations are dead: the partial sums may alias them
+  if (tid == 0) trace_stamp(tr, 4);
 
   // 4) partial sums [warp][m][tile][row], then the warp-ordered sum
   float* red = reinterpret_cast<float*>(th_smem + a.off_red);
@@ -241,6 +248,13 @@ __global__ void __launch_bounds__(TH_THREADS) w8a16_thin_kernel(const ThinArgs a
 #pragma unroll
       for (int w = 0; w < TH_WARPS; ++w) s += red[(size_t)w * per_w + i];
       a.y[(size_t)m * N + n] = __float2half_rn(fmaf(s, sc[rl], bi[rl]));
+    }
+  }
+  if (tr) {
+    __syncthreads();
+    if (tid == 0) {
+      trace_stamp(tr, 6);
+      trace_stamp(tr, 7);
     }
   }
 }
@@ -299,19 +313,10 @@ ThinPlan thin_plan(int64_t M, int64_t N, int64_t K, int sms) {
 
 template <int NT>
 int launch_thin_t(const ThinPlan& p, const ThinArgs& a, cudaStream_t s) {
-  const int dev = current_device();
-  if (dev < 0 || dev >= 64) return DDQ_ERR_DEVICE;
-  // Raise the dynamic shared-memory limit once per device (not a stream
-  // operation; the launch's own size still sets the occupancy).
-  static bool attr_set[64] = {};
-  if (!attr_set[dev]) {
-    if (cudaFuncSetAttribute(w8a16_thin_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             TH_SMEM_MAX) != cudaSuccess) {
-      cudaGetLastError();
-      return DDQ_ERR_LAUNCH;
-    }
-    attr_set[dev] = true;
-  }
+  // the launch's own size still sets the occupancy
+  static SmemAttrOnce attr;
+  const int ast = ensure_smem_attr(attr, current_device(), w8a16_thin_kernel<NT>, TH_SMEM_MAX);
+  if (ast) return ast;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)p.grid);
   cfg.blockDim = dim3(TH_THREADS);
@@ -338,7 +343,7 @@ bool thin_eligible(int64_t M, int64_t N, int64_t K, int sms) {
 
 int launch_thin(const __half* x, const uint8_t* wq, const float* scales, const void* bias,
                 int bias_dtype, __half* y, int M, int N, int K, unsigned long long timeout_ns,
-                cudaStream_t s) {
+                cudaStream_t s, int debug_flags) {
   const int sms = device_sm_count(current_device());
   if (sms <= 0) return DDQ_ERR_DEVICE;
   const ThinPlan p = thin_plan(M, N, K, sms);
@@ -363,6 +368,7 @@ int launch_thin(const __half* x, const uint8_t* wq, const float* scales, const v
   a.off_red = p.off_red;
   a.off_bar = p.off_bar;
   a.timeout_ns = timeout_ns;
+  a.trace = (debug_flags & 2) != 0;
   switch (p.nt) {
     case 1: return launch_thin_t<1>(p, a, s);
     case 2: return launch_thin_t<2>(p, a, s);

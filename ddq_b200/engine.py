@@ -22,9 +22,13 @@ attention -> O -> +residual -> RMSNorm -> gate/up -> SwiGLU -> down ->
   ``engine.py:346,352``) and each decode step is captured once in a CUDA
   graph and replayed.
 
-The other operators (RMSNorm, RoPE, attention, SwiGLU, the residual adds)
-are plain PyTorch here: they are not projection GEMMs.  Their arithmetic
-follows the reference kernels (fp32 math, fp16 storage).
+The other operators run on this library's kernels too: residual add +
+RMSNorm (``norm.add_rmsnorm``; on the decode path ``norm.add_rmsnorm_split``,
+which also emits the next GEMM's operand), the prefill RoPE + cache write
+(``attention.prefill_rope_kv``) and the decode attention above.  Prefill
+attention itself is ``scaled_dot_product_attention``.  Their arithmetic
+follows the reference kernels (fp32 math, fp16 storage); the plain-PyTorch
+versions of RMSNorm, RoPE and SwiGLU below serve the oracle engine.
 
 ``Engine(linear="oracle")`` swaps every projection for the reference
 semantics in fp32 (dequantised weight, fp32 matmul, fp16 output) and the

@@ -102,7 +102,8 @@ def main(argv=None):
     ap.add_argument("--empty", action="store_true",
                     help="time a trivial one-thread kernel instead (launch + event floor)")
     ap.add_argument("--trace", action="store_true",
-                    help="also run one launch with the per-CTA phase trace and summarise it")
+                    help="also run one launch with the per-CTA phase trace and summarise it "
+                         "(with --chain: the chain's last launch, traced in place)")
     ap.add_argument("--attention", action="store_true",
                     help="time the decode-step attention kernel instead of a GEMM")
     ap.add_argument("--batch", type=int, default=64)
@@ -172,7 +173,10 @@ def main(argv=None):
         c0, c1 = evs[0]
         c0.record(stream)
         for i in range(a.iters):
+            if a.trace and i == a.iters - 1:
+                L.ddq_set_debug(2, 0)   # trace the last launch of the chain, in place
             launch(a.warmup + i)
+        L.ddq_set_debug(0, 0)
         c1.record(stream)
         torch.cuda.synchronize(dev)
         per = c0.elapsed_time(c1) * 1e3 / a.iters
@@ -187,10 +191,11 @@ def main(argv=None):
     if a.trace:
         import ctypes
         import numpy as np
-        L.ddq_set_debug(2, 0)
-        launch(a.warmup + a.iters)       # cold weights (next copy in the rotation)
-        torch.cuda.synchronize(dev)
-        L.ddq_set_debug(0, 0)
+        if not a.chain:
+            L.ddq_set_debug(2, 0)
+            launch(a.warmup + a.iters)       # cold weights (next copy in the rotation)
+            torch.cuda.synchronize(dev)
+            L.ddq_set_debug(0, 0)
         buf = np.zeros((2048, 16), dtype=np.uint64)  # 16 stamp slots per CTA
         _lib.check(L.ddq_read_trace(buf.ctypes.data_as(ctypes.c_void_p), 2048,
                                     stream.cuda_stream), "read trace")
@@ -204,7 +209,11 @@ def main(argv=None):
             for j, nm in enumerate(names):
                 col = rel[:, j][used[:, j] > 0]
                 if len(col):
-                    trace[nm] = [round(float(np.median(col)), 3), round(float(col.max()), 3)]
+                    trace[nm] = [round(float(np.min(col)), 3), round(float(np.median(col)), 3),
+                                 round(float(col.max()), 3)]
+            w = rel[:, 3][used[:, 3] > 0]
+            if len(w):   # from the earliest grid-dependency resolution to the last exit
+                trace["after_dependency_us"] = round(float(rel[:, 7].max() - w.min()), 3)
     t = sorted(e0.elapsed_time(e1) * 1e3 for e0, e1 in evs)
     if a.chain:
         t = [per]

@@ -130,9 +130,12 @@ int ddq_w8a16_gemm_kernel_count(int64_t M, int64_t N, int64_t K);
  * 3*M*K (rounded up to 256) + 4*M <= 1048576 bytes; larger sizes return
  * DDQ_ERR_WORKSPACE (M > 64 or K % 16 != 0: DDQ_ERR_SHAPE).
  * The first call on a device looks up the array's device address (with that
- * device current); make that first call before any stream capture.  All
- * calls share the array: calls that may overlap on the GPU (different
- * streams, or several host threads) race - order them on one stream.
+ * device current), and so does the first call after the device's context
+ * changed (cudaDeviceReset); make those calls before any stream capture.
+ * Bounded waits use the limit and debug flags set by ddq_set_debug, as
+ * ddq_w8a16_gemm does.  All calls share the array: calls that may overlap on
+ * the GPU (different streams, or several host threads) race - order them on
+ * one stream.
  */
 int ddq_w8a16_gemm_noalloc(const void* x, const uint8_t* wq, const float* scales,
                            const void* bias, int bias_dtype, void* y,
@@ -304,7 +307,15 @@ int ddq_device_error(int* code, void* stream);
  * this process.  flags bit 0 makes the tensor-core kernel skip the
  * accumulator-ready signal, so its epilogue wait runs out and reports
  * DDQ_ERR_TIMEOUT through ddq_device_error() without faulting the GPU;
- * bit 1 turns on the phase trace read by ddq_read_trace().
+ * bit 1 turns on the phase trace read by ddq_read_trace(); bit 2 has no
+ * effect of its own.  While bit 0 or bit 2 is set, the shapes of the thin
+ * kernel run the split + decode kernels instead (bit 2 alone selects exactly
+ * that, e.g. to compare a fused producer's planes with the GEMM's own
+ * pre-pass).
+ * A wait that runs out is followed by a second bounded wait for the CTA's own
+ * copies in flight; should that one run out too, the CTA exits with copies
+ * outstanding and the context's further behaviour is undefined (it has not
+ * happened in any test: the copies read valid memory and complete).
  */
 int ddq_set_debug(int flags, uint64_t wait_timeout_ns);
 
@@ -315,7 +326,9 @@ int ddq_set_debug(int flags, uint64_t wait_timeout_ns);
  * weight tile landed (decode kernel: activation producer past the grid
  * dependency), 4 last MMA issued, 5 accumulator ready, 6 epilogue done,
  * 7 exit; decode kernel in split-K mode also 8 partials sent, 9 the other
- * ranks' partials received, 10 partials reduced; other slots stay 0.  This copies the
+ * ranks' partials received, 10 partials reduced; the thin kernel writes 0,
+ * 2 (weight copies issued), 3 (grid dependency resolved), 5 (weights and
+ * activations landed), 4 (MMAs done), 6 and 7; other slots stay 0.  This copies the
  * stamps of the first max_ctas CTAs (16 uint64 each) to host memory `dst`
  * and synchronises `stream`.
  */

@@ -28,7 +28,11 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF_OUT = os.path.join(HERE, "_ref")
-DEFAULT_REFERENCE = os.environ.get("DDQ_REFERENCE_DIR", "/root/reference")
+# The reference checkout: --reference, else DDQ_REFERENCE_DIR, else a
+# directory named "reference" beside this repository (absent on the GPU box,
+# which only imports the prebuilt modules).
+DEFAULT_REFERENCE = os.environ.get(
+    "DDQ_REFERENCE_DIR", os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
 
 MODULES = {
     "ref_gemm_fp8": "gemm_FP8_d.cu",

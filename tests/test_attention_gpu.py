@@ -10,23 +10,7 @@ import torch
 
 pytestmark = pytest.mark.gpu
 
-
-def decode_kernel_gemm(x, wq, s, b=None):
-    """The activation-split pre-pass + e4m3 decode kernel on fp16 activations,
-    whatever kernel ``f8_forward`` picks for the shape (the allocation-free
-    entry point always takes that path)."""
-    from ddq_b200 import _lib
-    lib = _lib.load()
-    x = x.contiguous()
-    M, K = x.shape
-    N = wq.shape[0]
-    y = torch.empty(M, N, dtype=torch.float16, device=x.device)
-    st = lib.ddq_w8a16_gemm_noalloc(x.data_ptr(), wq.data_ptr(), s.data_ptr(),
-                                    b.data_ptr() if b is not None else None,
-                                    _lib.DTYPE_F32 if b is not None else _lib.DTYPE_NONE,
-                                    y.data_ptr(), M, N, K, torch.cuda.current_stream().cuda_stream)
-    assert st == 0, _lib.status_string(st)
-    return y
+from gpu_helpers import decode_kernel_gemm  # noqa: E402
 
 
 def reference(qkv, kc, vc, cos, sin, pos, nh, nkv, hd, scale):

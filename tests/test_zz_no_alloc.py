@@ -8,7 +8,7 @@ match the ordinary entry point (ddq_w8a16_gemm via gemm_fp8.f8_forward, which
 takes its scratch from the caller) on two calls in a row - the second call
 finds the array holding the first call's contents - and reject sizes beyond
 the array.  This file sorts last so a stop-at-first-failure run has already
-run every other test."""
+run every other test; no other test calls this entry point."""
 import numpy as np
 import pytest
 import torch
