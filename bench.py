@@ -158,12 +158,14 @@ class DecodeWorkload:
     def launch_list(self):
         """Raw C-ABI argument tuples for every GEMM of one step (no allocation)."""
         from ddq_b200 import _lib
-        from ddq_b200.gemm_fp8 import workspace
         L = _lib.load()
-        # one workspace sized for the largest shape, allocated before any pointer is taken
+        # one workspace sized for the largest shape, allocated before any pointer is
+        # taken; the step's own (it is recorded into a CUDA graph, and the library
+        # never expands prefill weights early into a workspace a graph has used)
         need = max(L.ddq_w8a16_gemm_workspace_size(M, N, K) for M in DECODE_M
                    for _, K, N, _ in PROJS)
-        ws_all = workspace(self.device, need) if need else None
+        ws_all = torch.empty(need, dtype=torch.uint8, device=self.device) if need else None
+        self.ws = ws_all
         out = []
         for M in DECODE_M:
             for li, layer in enumerate(self.layers):

@@ -60,8 +60,9 @@ int launch_pf(const __half* x, const uint8_t* wq, const float* scales, const voi
               unsigned long long timeout_ns, int debug_flags, cudaStream_t s,
               bool swiglu = false);
 // A workspace was used by a call other than a double-buffered prefill GEMM
-// (the next prefill call on it must not expand ahead of the previous kernel).
-void ws_note_other_use(const void* ws);
+// (the next prefill call on it must not expand ahead of the previous kernel);
+// a call on a capturing stream also marks it as used in a CUDA graph.
+void ws_note_other_use(const void* ws, cudaStream_t s);
 // Prefill: RoPE of q and k, q in token-major layout, k/v into the cache (rope.cu).
 int launch_prefill_rope_kv(const __half* qkv, int64_t qkv_stride, __half* kc, __half* vc,
                            int64_t cache_bstride, int cap, const float* cos, const float* sin,

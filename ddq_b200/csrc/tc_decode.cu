@@ -1016,7 +1016,7 @@ int launch_dec(const __half* x, const uint8_t* wq, const float* scales, const vo
   if (M < 1 || M > 64) return DDQ_ERR_SHAPE;
   if (swiglu && (packed || N % 32 != 0)) return DDQ_ERR_SHAPE;
   const DecPlan p = dec_plan(M, N, K, sms, swiglu);
-  if (!ext_planes) ws_note_other_use(ws);
+  if (!ext_planes) ws_note_other_use(ws, s);
   uint8_t* planes;
   float* xscale;
   if (ext_planes) {  // the caller split the activations already

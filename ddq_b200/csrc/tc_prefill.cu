@@ -31,6 +31,7 @@
 
 #include <cstring>
 #include <mutex>
+#include <iterator>
 #include <unordered_map>
 
 #include "common.cuh"
@@ -445,37 +446,69 @@ size_t pf_workspace_bytes(int64_t N, int64_t K) { return (size_t)N * (size_t)K *
 
 namespace {
 // Per workspace: which of its two fp16 buffers the next prefill call uses,
-// and whether the call before was a prefill call (only then may this call's
-// expansion write before the previous kernel has finished: a decode-shape
-// call keeps its activation planes at the start of the same workspace).
+// and whether that call's expansion may write before the previous kernel has
+// finished.  That is safe only when the kernel just before it on the stream
+// is this library's prefill GEMM reading the other buffer (that GEMM lets its
+// dependents launch only after its own dependency, so the GEMM before it -
+// the other buffer's last reader - has finished).  The host can know that
+// only for calls made eagerly, in stream order, on a workspace whose calls
+// were never recorded into a CUDA graph: a replayed graph runs its kernels
+// between eager calls without the host seeing them.  Hence:
+//   * a call made while its stream is capturing never expands early, and
+//     marks the workspace "captured" for good (later eager calls on it never
+//     expand early either);
+//   * an eager call expands early only if the previous call on the workspace
+//     was an eager prefill call on a never-captured workspace.
+// A decode-shape call keeps its activation planes at the start of the same
+// workspace and resets the history (ws_note_other_use).  Forgetting an entry
+// is always safe (the next call waits), so the table is cleared if a caller
+// cycles through very many workspaces; a captured mark lost that way is
+// re-established only by the next capture, so the table is cleared only of
+// never-captured entries.
 struct PfWs {
   int half = 0;
-  bool last_pf = false;  // unknown history: wait, as with a single buffer
+  bool last_pf = false;   // unknown history: wait, as with a single buffer
+  bool captured = false;  // used inside a stream capture at least once
 };
 std::mutex g_pf_ws_mu;
 std::unordered_map<const void*, PfWs> g_pf_ws;
-// Forgetting a workspace is always safe (its next call waits), so the table is
-// simply cleared if a caller cycles through very many workspaces.
 constexpr size_t kPfWsMax = 4096;
 PfWs& pf_ws_entry(const void* ws) {
-  if (g_pf_ws.size() >= kPfWsMax && g_pf_ws.find(ws) == g_pf_ws.end()) g_pf_ws.clear();
+  if (g_pf_ws.size() >= kPfWsMax && g_pf_ws.find(ws) == g_pf_ws.end()) {
+    for (auto it = g_pf_ws.begin(); it != g_pf_ws.end();)
+      it = it->second.captured ? std::next(it) : g_pf_ws.erase(it);
+  }
   return g_pf_ws[ws];
+}
+
+bool stream_capturing(cudaStream_t s) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &cs) != cudaSuccess) {
+    cudaGetLastError();
+    return true;  // unknown: treat as captured (never early)
+  }
+  return cs != cudaStreamCaptureStatusNone;
 }
 }  // namespace
 
-void ws_note_other_use(const void* ws) {
+void ws_note_other_use(const void* ws, cudaStream_t s) {
   if (!ws) return;
+  const bool cap = stream_capturing(s);
   std::lock_guard<std::mutex> lock(g_pf_ws_mu);
-  pf_ws_entry(ws).last_pf = false;
+  PfWs& st = pf_ws_entry(ws);
+  st.last_pf = false;
+  st.captured = st.captured || cap;
 }
 
 // The buffer (0 or 1) for this prefill call, and whether its expansion may
 // run ahead of the previous kernel.
-static int pf_take_buffer(const void* ws, bool* early) {
+static int pf_take_buffer(const void* ws, cudaStream_t s, bool* early) {
+  const bool cap = stream_capturing(s);
   std::lock_guard<std::mutex> lock(g_pf_ws_mu);
   PfWs& st = pf_ws_entry(ws);
-  *early = st.last_pf;
-  st.last_pf = true;
+  st.captured = st.captured || cap;
+  *early = st.last_pf && !st.captured;
+  st.last_pf = !st.captured;
   st.half ^= 1;
   return st.half;
 }
@@ -501,9 +534,9 @@ int launch_pf(const __half* x, const uint8_t* wq, const float* scales, const voi
   bool early = false;
   size_t off = 0;
   if (need <= half) {
-    off = (size_t)pf_take_buffer(ws, &early) * half;
+    off = (size_t)pf_take_buffer(ws, s, &early) * half;
   } else {
-    ws_note_other_use(ws);  // the single buffer: always wait for the previous kernel
+    ws_note_other_use(ws, s);  // the single buffer: always wait for the previous kernel
   }
   __half* w16 = reinterpret_cast<__half*>(static_cast<uint8_t*>(ws) + off);
   // 1) exact e4m3 -> fp16 expansion of the weights

@@ -4,10 +4,15 @@
  * Every entry point takes raw device pointers, sizes and a CUDA stream
  * (passed as void*, i.e. a cudaStream_t; NULL = legacy default stream),
  * launches asynchronously on that stream and returns a ddq_status.  Nothing
- * here allocates device memory; nothing synchronises the device.  The
- * library keeps no mutable global state except per-device cached attributes
- * (SM count, the driver's tensor-map encoder) and the device error word
- * read by ddq_device_error().
+ * here allocates device memory; nothing synchronises the device.  Mutable
+ * global state: per-device cached attributes (SM count, the driver's
+ * tensor-map encoder, kernels' shared-memory limits), the device error word
+ * read by ddq_device_error(), the debug settings of ddq_set_debug(), and a
+ * host-side table keyed by workspace address that records, for prefill-shape
+ * calls, which of the workspace's two fp16 buffers the next call uses and
+ * whether the previous call on it was an eager prefill call (see
+ * ddq_w8a16_gemm_workspace_size).  All of it is guarded for concurrent host
+ * threads.
  *
  * Data formats (all row-major, contiguous):
  *   x      fp16  [M, K]   activations
@@ -74,11 +79,18 @@ int ddq_quantize_e4m3(const void* w, int w_dtype, int64_t N, int64_t K,
  * Decode shapes (M <= 64) keep the activations split into three e4m3 planes
  * and the per-token scales there; prefill shapes (M >= 128 by default) keep
  * the weight expanded to fp16 (N * K * 2 bytes; the size reported is two such
- * buffers, which consecutive calls alternate so that a call's expansion does
- * not wait for the previous GEMM; one buffer also works, without that
- * overlap).  The contents need no initialisation.  One workspace sized for the largest shape serves any
- * sequence of shapes; calls sharing it must be ordered on one stream.  The
- * pointer must be 256-byte aligned.
+ * buffers at fixed offsets, 0 and half the workspace, which consecutive
+ * prefill calls alternate; one buffer also works, without the overlap
+ * below).  The contents need no initialisation.  One workspace sized for the
+ * largest shape serves any sequence of shapes; calls sharing it must be
+ * ordered on one stream.  The pointer must be 256-byte aligned.
+ * Overlap: an eager prefill call (its stream not capturing) whose previous
+ * call on the same workspace was also an eager prefill call expands its
+ * weight before the previous kernel finishes (that kernel reads the other
+ * buffer).  A call made while its stream captures a CUDA graph never does,
+ * and marks the workspace: no later call on that address expands early,
+ * since a replayed graph runs kernels between eager calls that the library
+ * does not see.
  */
 size_t ddq_w8a16_gemm_workspace_size(int64_t M, int64_t N, int64_t K);
 

@@ -296,3 +296,98 @@ def test_prefill_and_decode_calls_chained_on_one_workspace(cuda_device):
         torch.cuda.synchronize()
         for (M, N, K), y, r in zip(shapes, outs, ref):
             assert torch.equal(y, r), (rep, M, N, K)
+
+
+def _pf_case(g, M, N, K):
+    from ddq_b200 import gemm_fp8
+    wq, s = gemm_fp8.quantize(torch.randn(N, K, generator=g, device="cuda") * 0.02)
+    return torch.randn(M, K, generator=g, device="cuda").half(), wq, s, M, N, K
+
+
+def _run_ws(c, ws, nbytes):
+    from ddq_b200 import _lib
+    lib = _lib.load()
+    x, wq, s, M, N, K = c
+    y = torch.empty(M, N, dtype=torch.float16, device="cuda")
+    st = lib.ddq_w8a16_gemm(x.data_ptr(), wq.data_ptr(), s.data_ptr(), None, _lib.DTYPE_NONE,
+                            y.data_ptr(), M, N, K, ws.data_ptr(), nbytes,
+                            torch.cuda.current_stream().cuda_stream)
+    assert st == 0, _lib.status_string(st)
+    return y
+
+
+def _alone(c):
+    from ddq_b200 import _lib
+    lib = _lib.load()
+    n = lib.ddq_w8a16_gemm_workspace_size(c[3], c[4], c[5])
+    ws = torch.zeros(max(n, 256), dtype=torch.uint8, device="cuda")
+    y = _run_ws(c, ws, n)
+    torch.cuda.synchronize()
+    return y
+
+
+def test_prefill_calls_replayed_in_a_graph_on_one_workspace(cuda_device):
+    """Three prefill calls (an odd number) and a decode call on one workspace,
+    captured in a CUDA graph and replayed three times back to back, with an
+    eager prefill call on the same workspace between two replays: every
+    result equals the same call made alone.  (A call recorded in a graph never
+    expands its weight ahead of the previous kernel, and a workspace once used
+    in a graph is never expanded into early by eager calls either: the host
+    cannot see what a replay runs between them.)"""
+    from ddq_b200 import _lib
+    lib = _lib.load()
+    g = torch.Generator(device="cuda").manual_seed(41)
+    cap = [_pf_case(g, 512, 1152, 896), _pf_case(g, 16, 896, 896), _pf_case(g, 512, 896, 4864),
+           _pf_case(g, 384, 9728, 896)]
+    eager = _pf_case(g, 512, 896, 896)
+    refs = [_alone(c) for c in cap]
+    ref_e = _alone(eager)
+    need = max(lib.ddq_w8a16_gemm_workspace_size(c[3], c[4], c[5]) for c in cap + [eager])
+    ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for c in cap:                       # warm-up outside the capture
+            _run_ws(c, ws, need)
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        outs = [_run_ws(c, ws, need) for c in cap]
+    got = []
+    for rep in range(3):
+        graph.replay()
+        got.append([o.clone() for o in outs])
+        if rep == 1:
+            got.append([_run_ws(eager, ws, need)])
+    torch.cuda.synchronize()
+    for rep, ys in enumerate(got):
+        want = [ref_e] if len(ys) == 1 else refs
+        for y, r in zip(ys, want):
+            assert torch.equal(y, r), rep
+    del graph
+
+
+def test_prefill_workspace_freed_and_reallocated_at_same_address(cuda_device):
+    """A workspace freed after a prefill call and re-allocated at the same
+    address (the caching allocator's stream-ordered reuse) serves the next
+    prefill calls correctly, though the host-side history of the address says
+    the previous call on it was a prefill call."""
+    from ddq_b200 import _lib
+    lib = _lib.load()
+    g = torch.Generator(device="cuda").manual_seed(43)
+    calls = [_pf_case(g, 512, 1152, 896), _pf_case(g, 512, 896, 4864), _pf_case(g, 256, 4864, 896)]
+    refs = [_alone(c) for c in calls]
+    need = max(lib.ddq_w8a16_gemm_workspace_size(c[3], c[4], c[5]) for c in calls)
+    torch.cuda.synchronize()
+    ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+    addr = ws.data_ptr()
+    outs = [_run_ws(calls[0], ws, need)]
+    del ws
+    ws2 = torch.empty(need, dtype=torch.uint8, device="cuda")
+    if ws2.data_ptr() != addr:
+        pytest.skip("the allocator did not reuse the address")
+    outs += [_run_ws(calls[1], ws2, need), _run_ws(calls[2], ws2, need)]
+    torch.cuda.synchronize()
+    for y, r in zip(outs, refs):
+        assert torch.equal(y, r)
