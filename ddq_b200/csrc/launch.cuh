@@ -52,6 +52,13 @@ bool thin_eligible(int64_t M, int64_t N, int64_t K, int sms);
 int launch_thin(const __half* x, const uint8_t* wq, const float* scales, const void* bias,
                 int bias_dtype, __half* y, int M, int N, int K, unsigned long long timeout_ns,
                 cudaStream_t s, int debug_flags = 0);
+// 1..16 tokens, K % 64 == 0: each CTA's contiguous weight slice resident in
+// shared memory (one bulk copy) before the grid dependency, weights on the
+// mma.sync A operand, dependents triggered at entry (rs.cu).  No workspace.
+bool rs_eligible(int64_t M, int64_t N, int64_t K, int sms);
+int launch_rs(const __half* x, const uint8_t* wq, const float* scales, const void* bias,
+              int bias_dtype, __half* y, int M, int N, int K, unsigned long long timeout_ns,
+              cudaStream_t s, int debug_flags = 0);
 // Prefill shapes: exact e4m3 -> fp16 weight expansion into the workspace
 // (N * K * 2 bytes), then the fp16 tensor-core GEMM (tc_prefill.cu).
 size_t pf_workspace_bytes(int64_t N, int64_t K);

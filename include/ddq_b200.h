@@ -319,11 +319,13 @@ int ddq_device_error(int* code, void* stream);
  * this process.  flags bit 0 makes the tensor-core kernel skip the
  * accumulator-ready signal, so its epilogue wait runs out and reports
  * DDQ_ERR_TIMEOUT through ddq_device_error() without faulting the GPU;
- * bit 1 turns on the phase trace read by ddq_read_trace(); bit 2 has no
- * effect of its own.  While bit 0 or bit 2 is set, the shapes of the thin
- * kernel run the split + decode kernels instead (bit 2 alone selects exactly
- * that, e.g. to compare a fused producer's planes with the GEMM's own
- * pre-pass).
+ * bit 1 turns on the phase trace read by ddq_read_trace(); bits 2 and 3
+ * have no effect of their own.  While bit 0 or bit 2 is set, the shapes of
+ * the resident-slice and thin kernels run the split + decode kernels instead
+ * (bit 2 alone selects exactly that, e.g. to compare a fused producer's
+ * planes with the GEMM's own pre-pass); while bit 3 is set, the
+ * resident-slice kernel's shapes go to the thin kernel where it takes them
+ * (to test that kernel).
  * A wait that runs out is followed by a second bounded wait for the CTA's own
  * copies in flight; should that one run out too, the CTA exits with copies
  * outstanding and the context's further behaviour is undefined (it has not

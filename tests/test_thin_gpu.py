@@ -1,4 +1,6 @@
-"""GPU parity tests of the 1..16-token GEMM kernel (``thin.cu``) against the
+"""GPU parity tests of the 1..16-token GEMM kernel (``thin.cu``; run with
+``ddq_set_debug`` bit 3, which gives it the shapes the resident-slice kernel
+would otherwise take) against the
 CPU oracle: the token counts it takes (and the decode kernel beyond them),
 ragged row counts, the smallest K, every per-CTA tile-count variant up to the
 limit of 16, every e4m3 code, the three bias types, chained calls under
@@ -40,6 +42,17 @@ def g(cuda_device):
 def lib(cuda_device):
     from ddq_b200 import _lib
     return _lib.load()
+
+
+@pytest.fixture(autouse=True)
+def thin_dispatch(cuda_device):
+    """ddq_set_debug bit 3: the shapes of the resident-slice kernel (rs.cu),
+    which ddq_w8a16_gemm tries first, go to this file's kernel instead."""
+    from ddq_b200 import _lib
+    L = _lib.load()
+    assert L.ddq_set_debug(8, 0) == 0
+    yield
+    L.ddq_set_debug(0, 0)
 
 
 def sms():
