@@ -337,26 +337,53 @@ extern "C" int ddq_argmax_f16(const void* logits, int64_t B, int64_t V, int64_t*
 // token tile); chunks reuse one workspace in stream order.
 static const int64_t kLmChunk = 64;
 
+// Workspace layout of the fused lm_head: [0, lmh_area_bytes) the streaming
+// kernel's arrival counter and per-CTA words (kept zero between calls), then
+// the decode kernel's activation planes for calls of more tokens.
 extern "C" size_t ddq_lm_head_argmax_workspace_size(int64_t M, int64_t N, int64_t K) {
   if (M <= 0 || N <= 0 || K <= 0 || K % 16 != 0) return 0;
   const int64_t mc = M < kLmChunk ? M : kLmChunk;
-  if (mc < tc_min_m()) return 0;
   const int dev = current_device();
   const int sms = dev >= 0 ? device_sm_count(dev) : -1;
-  return dec_plan(mc, N, K, sms > 0 ? sms : 148).ws_bytes;
+  const size_t area = lmh_area_bytes(sms);
+  if (mc < tc_min_m()) return area;
+  return area + dec_plan(mc, N, K, sms > 0 ? sms : 148).ws_bytes;
 }
+
+namespace {
+bool lmh_shape(int64_t M, int64_t N, int64_t K) {
+  if ((g_debug_flags & ~2) != 0) return false;
+  const int dev = current_device();
+  return dev >= 0 && lmh_eligible(M, N, K, device_sm_count(dev));
+}
+}  // namespace
 
 extern "C" int ddq_lm_head_argmax(const void* x, const uint8_t* wq, const float* scales, int64_t M,
                                   int64_t N, int64_t K, int64_t vocab_offset, uint64_t* packed,
                                   int64_t* ids, void* workspace, size_t workspace_bytes,
                                   void* stream) {
-  (void)workspace; (void)workspace_bytes;
   if (M < 0 || N < 0 || K < 0 || vocab_offset < 0) return DDQ_ERR_SHAPE;
   if (M == 0) return DDQ_OK;
   if (!x || !packed || (N > 0 && (!wq || !scales))) return DDQ_ERR_INVALID_ARGUMENT;
   if (M > 0x7fffffff || N > 0x7fffffff || vocab_offset + N > 0xFFFFFFFFll) return DDQ_ERR_SHAPE;
   if (!(K > 0 && K % 16 == 0 && K <= 12288 && aligned16(x) && aligned16(wq))) return DDQ_ERR_ALIGNMENT;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int dev = current_device();
+  const int sms = dev >= 0 ? device_sm_count(dev) : -1;
+  const size_t area = lmh_area_bytes(sms);
+  if (N > 0 && lmh_shape(M, N, K)) {
+    // one streaming kernel writes packed and ids (no memset, split or unpack)
+    return launch_lmh(reinterpret_cast<const __half*>(x), wq, scales, (int)M, (int)N, (int)K,
+                      vocab_offset, reinterpret_cast<unsigned long long*>(packed), ids, workspace,
+                      workspace_bytes, g_wait_timeout_ns, g_debug_flags, s);
+  }
+  // the decode-kernel path keeps its planes after the streaming kernel's area
+  void* dws = nullptr;
+  size_t dws_bytes = 0;
+  if (workspace && workspace_bytes > area) {
+    dws = static_cast<uint8_t*>(workspace) + area;
+    dws_bytes = workspace_bytes - area;
+  }
   if (cudaMemsetAsync(packed, 0, (size_t)M * sizeof(uint64_t), s) != cudaSuccess) return DDQ_ERR_LAUNCH;
   if (N > 0) {
     const __half* xh = reinterpret_cast<const __half*>(x);
@@ -366,7 +393,7 @@ extern "C" int ddq_lm_head_argmax(const void* x, const uint8_t* wq, const float*
       int st;
       if (mc >= tc_min_m())
         st = launch_dec(xh + m0 * K, wq, scales, nullptr, DDQ_DTYPE_NONE, nullptr, pk + m0,
-                        vocab_offset, mc, (int)N, (int)K, workspace, workspace_bytes,
+                        vocab_offset, mc, (int)N, (int)K, dws, dws_bytes,
                         g_wait_timeout_ns, g_debug_flags, s);
       else
         st = launch_skinny_argmax(xh + m0 * K, wq, scales, pk + m0, vocab_offset, mc, (int)N,

@@ -59,6 +59,15 @@ bool rs_eligible(int64_t M, int64_t N, int64_t K, int sms);
 int launch_rs(const __half* x, const uint8_t* wq, const float* scales, const void* bias,
               int bias_dtype, __half* y, int M, int N, int K, unsigned long long timeout_ns,
               cudaStream_t s, int debug_flags = 0);
+// Fused lm_head argmax for 1..16 tokens streaming 16-row weight tiles with one
+// bulk copy each (lmh.cu).  Its workspace area (arrival counter + per-CTA
+// words, lmh_area_bytes) leads the lm_head workspace and must be zero before
+// the first call; every call leaves the counter at zero.
+bool lmh_eligible(int64_t M, int64_t N, int64_t K, int sms);
+size_t lmh_area_bytes(int sms);
+int launch_lmh(const __half* x, const uint8_t* wq, const float* scales, int M, int N, int K,
+               int64_t vocab_offset, unsigned long long* packed, int64_t* ids, void* ws,
+               size_t ws_bytes, unsigned long long timeout_ns, int debug_flags, cudaStream_t s);
 // Prefill shapes: exact e4m3 -> fp16 weight expansion into the workspace
 // (N * K * 2 bytes), then the fp16 tensor-core GEMM (tc_prefill.cu).
 size_t pf_workspace_bytes(int64_t N, int64_t K);

@@ -20,7 +20,21 @@ from typing import Optional, Tuple
 import torch
 
 from . import _lib
-from .gemm_fp8 import workspace
+
+_lm_workspaces: dict = {}
+
+
+def lm_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """The lm_head's own zero-filled workspace per (device, current stream),
+    grown on demand.  It is not shared with the other GEMM entry points: its
+    first bytes hold the streaming kernel's arrival counter, which every call
+    leaves at zero for the next one."""
+    key = (device.type, device.index, torch.cuda.current_stream(device).cuda_stream)
+    buf = _lm_workspaces.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
+        _lm_workspaces[key] = buf
+    return buf
 
 
 def shard_range(vocab: int, rank: int, world: int) -> Tuple[int, int]:
@@ -76,7 +90,7 @@ def lm_head_argmax(x: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor,
     L = _lib.load()
     with torch.cuda.device(x.device):
         nws = L.ddq_lm_head_argmax_workspace_size(M, N, K)
-        ws = workspace(x.device, nws) if nws else None
+        ws = lm_workspace(x.device, nws) if nws else None
         st = L.ddq_lm_head_argmax(x2.data_ptr(), wq.contiguous().data_ptr(),
                                   scales.contiguous().data_ptr(), M, N, K, int(vocab_offset),
                                   packed.data_ptr(), ids.data_ptr(),

@@ -133,7 +133,10 @@ def main(argv=None):
     packed = torch.empty(M, dtype=torch.int64, device=dev)
     nws = (L.ddq_lm_head_argmax_workspace_size(M, N, K) if a.lm_head
            else L.ddq_w8a16_gemm_workspace_size(M, N, K))
-    ws = gemm_fp8.workspace(dev, nws) if nws else None
+    if a.lm_head:
+        ws = lm_head.lm_workspace(dev, nws) if nws else None
+    else:
+        ws = gemm_fp8.workspace(dev, nws) if nws else None
     stream = torch.cuda.current_stream(dev)
 
     ids = torch.empty(M, dtype=torch.int64, device=dev)

@@ -278,7 +278,13 @@ int ddq_argmax_f16(const void* logits, int64_t B, int64_t V, int64_t* out,
                    void* stream);
 
 /*
- * Bytes of workspace ddq_lm_head_argmax needs (per-tile partial maxima).
+ * Bytes of workspace ddq_lm_head_argmax needs.  It starts with an arrival
+ * counter and one word per CTA and token (1..16 tokens: one streaming kernel
+ * whose last CTA combines them), followed by the activation planes of the
+ * decode-kernel path used for more tokens.  Zero-fill it once before its
+ * first use; every call leaves the counter at zero.  Keep it for
+ * ddq_lm_head_argmax calls only (other entry points would overwrite the
+ * counter), one workspace per stream.
  */
 size_t ddq_lm_head_argmax_workspace_size(int64_t M, int64_t N, int64_t K);
 
@@ -291,7 +297,10 @@ size_t ddq_lm_head_argmax_workspace_size(int64_t M, int64_t N, int64_t K);
  * that a MAX over packed values of several shards (an NCCL all-gather or
  * all-reduce MAX) yields the global greedy token.  ids[m] (may be NULL)
  * receives the decoded global index of this shard's best logit.
- * The logits are never written to memory.
+ * The logits are never written to memory.  1..16 tokens with K % 64 == 0
+ * (K <= 4096) run one kernel that streams 16-row weight tiles and writes
+ * packed[] and ids[] itself; other shapes run the activation split, the
+ * decode kernel with an argmax epilogue and an unpack kernel.
  * Replaces: engine.py:338 (lm_head via gemm_d) + engine.py:345/351
  * (sampler_d.forward on the last position), sampler_d.cu:10-49.
  */
