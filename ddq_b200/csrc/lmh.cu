@@ -188,40 +188,54 @@ __global__ void __launch_bounds__(LM_THREADS, 1) w8a16_lmh_kernel(const LmArgs a
       }
       const uint32_t wlo = sbase + (uint32_t)s * tile_bytes + (uint32_t)(g * K + t * 16);
       const uint32_t whi = wlo + (uint32_t)(8 * K);
-      float acc[2][NB][4];
+      // Two K blocks per step, each MMA j into set (block parity, j parity):
+      // consecutive MMAs never feed each other (mma.sync issues in order), so
+      // four independent accumulator chains per token block.
+      float acc[4][NB][4];
 #pragma unroll
-      for (int h = 0; h < 2; ++h)
+      for (int h = 0; h < 4; ++h)
 #pragma unroll
         for (int nb = 0; nb < NB; ++nb) acc[h][nb][0] = acc[h][nb][1] = acc[h][nb][2] = acc[h][nb][3] = 0.f;
-#pragma unroll 2
-      for (int kb = 0; kb < KB; ++kb) {
-        const int h = kb & 1;  // two accumulator sets: half-length MMA chains
-        const uint4 lo = lm_lds128(wlo + (uint32_t)(kb * 64));
-        const uint4 hi = lm_lds128(whi + (uint32_t)(kb * 64));
-        uint4 x0[NB], x1[NB];
+      for (int kb = 0; kb < KB; kb += 2) {
+        const int nk = kb + 1 < KB ? 2 : 1;
+        uint32_t lw[2][4], hw[2][4], xs[2][NB][8];
 #pragma unroll
-        for (int nb = 0; nb < NB; ++nb) {
-          x0[nb] = make_uint4(0u, 0u, 0u, 0u);
-          x1[nb] = x0[nb];
-          if (xok[nb]) {
-            x0[nb] = lm_lds128(xrow[nb] + (uint32_t)(kb * 128));
-            x1[nb] = lm_lds128(xrow[nb] + (uint32_t)(kb * 128 + 16));
+        for (int h = 0; h < 2; ++h) {
+          if (h < nk) {
+            const uint4 lo = lm_lds128(wlo + (uint32_t)((kb + h) * 64));
+            const uint4 hi = lm_lds128(whi + (uint32_t)((kb + h) * 64));
+            lw[h][0] = lo.x; lw[h][1] = lo.y; lw[h][2] = lo.z; lw[h][3] = lo.w;
+            hw[h][0] = hi.x; hw[h][1] = hi.y; hw[h][2] = hi.z; hw[h][3] = hi.w;
+#pragma unroll
+            for (int nb = 0; nb < NB; ++nb) {
+              uint4 x0 = make_uint4(0u, 0u, 0u, 0u), x1 = x0;
+              if (xok[nb]) {
+                x0 = lm_lds128(xrow[nb] + (uint32_t)((kb + h) * 128));
+                x1 = lm_lds128(xrow[nb] + (uint32_t)((kb + h) * 128 + 16));
+              }
+              xs[h][nb][0] = x0.x; xs[h][nb][1] = x0.y; xs[h][nb][2] = x0.z; xs[h][nb][3] = x0.w;
+              xs[h][nb][4] = x1.x; xs[h][nb][5] = x1.y; xs[h][nb][6] = x1.z; xs[h][nb][7] = x1.w;
+            }
+          } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) lw[h][q] = hw[h][q] = 0u;
+#pragma unroll
+            for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+              for (int q = 0; q < 8; ++q) xs[h][nb][q] = 0u;
           }
         }
-        const uint32_t lw[4] = {lo.x, lo.y, lo.z, lo.w};
-        const uint32_t hw[4] = {hi.x, hi.y, hi.z, hi.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const uint32_t a0 = e4m3x2_to_half2_bits_x2m8(lw[j], 0x4140u);
-          const uint32_t a2 = e4m3x2_to_half2_bits_x2m8(lw[j], 0x4342u);
-          const uint32_t a1 = e4m3x2_to_half2_bits_x2m8(hw[j], 0x4140u);
-          const uint32_t a3 = e4m3x2_to_half2_bits_x2m8(hw[j], 0x4342u);
 #pragma unroll
-          for (int nb = 0; nb < NB; ++nb) {
-            const uint32_t xs[8] = {x0[nb].x, x0[nb].y, x0[nb].z, x0[nb].w,
-                                    x1[nb].x, x1[nb].y, x1[nb].z, x1[nb].w};
-            if (h == 0) lm_mma(acc[0][nb], a0, a1, a2, a3, xs[2 * j], xs[2 * j + 1]);
-            else lm_mma(acc[1][nb], a0, a1, a2, a3, xs[2 * j], xs[2 * j + 1]);
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t a0 = e4m3x2_to_half2_bits_x2m8(lw[h][j], 0x4140u);
+            const uint32_t a2 = e4m3x2_to_half2_bits_x2m8(lw[h][j], 0x4342u);
+            const uint32_t a1 = e4m3x2_to_half2_bits_x2m8(hw[h][j], 0x4140u);
+            const uint32_t a3 = e4m3x2_to_half2_bits_x2m8(hw[h][j], 0x4342u);
+#pragma unroll
+            for (int nb = 0; nb < NB; ++nb)
+              lm_mma(acc[2 * h + (j & 1)][nb], a0, a1, a2, a3, xs[h][nb][2 * j], xs[h][nb][2 * j + 1]);
           }
         }
       }
@@ -235,8 +249,11 @@ __global__ void __launch_bounds__(LM_THREADS, 1) w8a16_lmh_kernel(const LmArgs a
       for (int nb = 0; nb < NB; ++nb) {
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
-          const __half vlo = __float2half_rn((acc[0][nb][c] + acc[1][nb][c]) * slo);
-          const __half vhi = __float2half_rn((acc[0][nb][2 + c] + acc[1][nb][2 + c]) * shi);
+          const float slo_acc = (acc[0][nb][c] + acc[1][nb][c]) + (acc[2][nb][c] + acc[3][nb][c]);
+          const float shi_acc = (acc[0][nb][2 + c] + acc[1][nb][2 + c]) +
+                                (acc[2][nb][2 + c] + acc[3][nb][2 + c]);
+          const __half vlo = __float2half_rn(slo_acc * slo);
+          const __half vhi = __float2half_rn(shi_acc * shi);
           unsigned long long cand = 0ull;
           if (nlo < N && __half2float(vlo) > -FLT_MAX)
             cand = ((unsigned long long)f16_order_key(vlo) << 32) | ilo;

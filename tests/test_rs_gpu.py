@@ -1,9 +1,8 @@
-"""GPU parity tests of the resident-slice GEMM kernels (``rs.cu``, 1..16
-tokens, each CTA's weight slice in shared memory, weights on the MMA rows):
-the e4m3 variant (three activation planes, M * K <= 16384) and the fp16
-variant (the other shapes, and every shape in a subprocess with DDQ_RS8=0),
+"""GPU parity tests of the resident-slice GEMM kernel (``rs.cu``, 1..16
+tokens, each CTA's weight slice in shared memory, weights on the MMA rows)
 against the CPU oracle: every token count, ragged row counts and K values, every
-per-CTA tile count up to the limit of 8 sixteen-row tiles, every e4m3 code,
+per-CTA tile count up to the limit (6 sixteen-row tiles at 1..8 tokens, 5 at
+9..16), every e4m3 code,
 the three bias types, a non-finite activation, chains of dependent calls
 issued back to back (the kernel lets the next one start at its own entry),
 graph replay, bitwise reproducibility and the dispatch boundaries."""
@@ -72,7 +71,7 @@ def test_ragged_shapes(g, lib, M, N, K):
     check(g, M, N, K, seed=M * 7 + N)
 
 
-@pytest.mark.parametrize("per_cta", range(1, 9))
+@pytest.mark.parametrize("per_cta", range(1, 7))
 def test_every_tile_count_per_cta(g, lib, per_cta):
     """N chosen so the busiest CTA holds per_cta tiles of 16 rows (one row
     past a multiple of 16: the last tile is partial and its rows past N read
@@ -83,10 +82,14 @@ def test_every_tile_count_per_cta(g, lib, per_cta):
     check(g, M, N, K, seed=per_cta)
 
 
-def test_tile_limit_per_cta(lib):
+def test_tile_limit_per_cta(g, lib):
+    """6 tiles per CTA at up to 8 tokens, 5 at 9..16; one tile more goes to
+    another kernel (both give the oracle's result)."""
     K = 512
-    assert lib.ddq_w8a16_gemm_kernel_count(4, 8 * 16 * sms(), K) == 1
-    assert lib.ddq_w8a16_gemm_kernel_count(4, 8 * 16 * sms() + 1, K) == 2
+    assert lib.ddq_w8a16_gemm_kernel_count(4, 6 * 16 * sms(), K) == 1
+    assert lib.ddq_w8a16_gemm_kernel_count(4, 6 * 16 * sms() + 1, K) == 2
+    check(g, 12, 5 * 16 * sms(), K, seed=61)
+    check(g, 12, 5 * 16 * sms() + 1, K, seed=62)
 
 
 def test_dispatch_boundaries(lib):
@@ -195,31 +198,3 @@ def test_deterministic_bitwise(g, M):
     for _ in range(3):
         assert torch.equal(g.f8_forward(xd, wqd, sd), a)
 
-
-def test_fp16_variant_in_a_subprocess(cuda_device):
-    """DDQ_RS8=0 (read once per process) sends every shape to the fp16 variant
-    (integer e4m3 -> fp16 conversion, mma.sync m16n8k16); its results on the
-    shapes the e4m3 variant normally takes must match the oracle too."""
-    import os
-    import subprocess
-    import sys
-    code = (
-        "import numpy as np, torch, sys\n"
-        "sys.path.insert(0, %r)\n"
-        "from ddq_b200 import gemm_fp8, _lib\n"
-        "from oracle import w8a16 as o\n"
-        "L = _lib.load()\n"
-        "for M, N, K in [(1, 9728, 896), (8, 1152, 896), (16, 4864, 896), (3, 896, 4864), (13, 17, 1024)]:\n"
-        "    assert L.ddq_w8a16_gemm_kernel_count(M, N, K) == 1\n"
-        "    rng = np.random.default_rng(M + N)\n"
-        "    x = rng.normal(0, 1, (M, K)).astype(np.float16)\n"
-        "    wq, s = o.quantize(rng.normal(0, 0.02, (N, K)).astype(np.float32))\n"
-        "    y = gemm_fp8.f8_forward(torch.from_numpy(x).cuda(), torch.from_numpy(wq).cuda(),\n"
-        "                            torch.from_numpy(s).cuda())\n"
-        "    err = o.normwise_rel_err(y.cpu().numpy(), o.f8_forward(x, wq, s))\n"
-        "    assert err <= 3e-3, (M, N, K, err)\n"
-        "print('ok')\n") % os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    env = dict(os.environ, DDQ_RS8="0")
-    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
-                       timeout=600)
-    assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
