@@ -15,8 +15,8 @@
 // 148 SMs, so the last CTAs finish within 1.5 % of the others.  A tile's
 // 16 x K bytes are one contiguous range: one bulk copy (TMA engine) per tile,
 // issued by a producer warp into a ring of stages, many tiles in flight per
-// SM.  Each of the 8 consumer warps takes whole tiles (tile i goes to warp
-// i mod 8), so no partial sums cross warps; a thread keeps the best packed
+// SM.  Each consumer warp takes whole tiles (tile i goes to warp i mod the
+// consumer count), so no partial sums cross warps; a thread keeps the best packed
 // word of the rows it sees per token.  At the end the CTA reduces them and
 // writes one word per token to a per-CTA slot of the workspace; the last CTA
 // to finish (an arrival counter in the workspace) combines the slots in CTA
@@ -33,8 +33,11 @@
 namespace ddq {
 namespace {
 
-constexpr int LM_CONSUMERS = 8;                  // consumer warps
-constexpr int LM_THREADS = (LM_CONSUMERS + 1) * 32;
+// Consumer warps: every warp computes one tile at a time and is bound by
+// its own instruction latencies, so the tiles in flight per SM set the rate;
+// 16 consumers (plus the producer warp) by default, DDQ_LMH_WARPS=8 for
+// measurements.
+constexpr int LM_MAX_CONSUMERS = 16;
 constexpr int LM_TILE = 16;
 constexpr int LM_MAX_STAGES = 16;
 constexpr int LM_SMEM_MAX = 232448;
@@ -79,8 +82,9 @@ __device__ __forceinline__ void lm_mma(float* d, uint32_t a0, uint32_t a1, uint3
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
+template <int NC>
 __device__ __forceinline__ void lm_consumer_bar() {
-  asm volatile("bar.sync 1, %0;" ::"r"(LM_CONSUMERS * 32) : "memory");
+  asm volatile("bar.sync 1, %0;" ::"r"(NC * 32) : "memory");
 }
 __device__ __forceinline__ unsigned long long lm_max(unsigned long long a, unsigned long long b) {
   return a > b ? a : b;
@@ -89,9 +93,9 @@ __device__ __forceinline__ unsigned long long lm_max(unsigned long long a, unsig
 // Shared memory: [0, stages * 16 * K) the ring of weight tiles; off_x the
 // activations [M][K] fp16; off_bar full[stages], empty[stages], the x
 // barrier, the abort, drain and last-CTA flags, then (at + 32) the per-warp
-// best words [8][16 tokens] (u64).
-template <int NB>
-__global__ void __launch_bounds__(LM_THREADS, 1) w8a16_lmh_kernel(const LmArgs a) {
+// best words [NC][16 tokens] (u64).
+template <int NB, int NC>
+__global__ void __launch_bounds__((NC + 1) * 32, 1) w8a16_lmh_kernel(const LmArgs a) {
   extern __shared__ __align__(128) uint8_t lm_smem[];
   const uint32_t sbase = ptx::smem_u32(lm_smem);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -124,7 +128,7 @@ __global__ void __launch_bounds__(LM_THREADS, 1) w8a16_lmh_kernel(const LmArgs a
   __syncthreads();
   ptx::pdl_launch_dependents();
 
-  if (warp == LM_CONSUMERS) {
+  if (warp == NC) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       auto issue = [&](int i) {
@@ -175,7 +179,7 @@ __global__ void __launch_bounds__(LM_THREADS, 1) w8a16_lmh_kernel(const LmArgs a
     for (int nb = 0; nb < NB; ++nb) best[nb][0] = best[nb][1] = 0ull;
     bool ok = ptx::mbar_wait(bar_x, 0u, a.timeout_ns, abort_flag);
     if (ok && warp == 0 && lane == 0) trace_stamp(tr, 5);
-    for (int i = warp; ok && i < ntl; i += LM_CONSUMERS) {
+    for (int i = warp; ok && i < ntl; i += NC) {
       const int s = i % S;
       const int row0 = (tile0 + i) * LM_TILE;
       // the two rows this thread scores, and their scales (issued early)
@@ -280,15 +284,15 @@ __global__ void __launch_bounds__(LM_THREADS, 1) w8a16_lmh_kernel(const LmArgs a
         wbest[warp * 16 + nb * 8 + 2 * t + 1] = best[nb][1];
       }
     }
-    lm_consumer_bar();
+    lm_consumer_bar<NC>();
     if (tid < M) {
       unsigned long long v = 0ull;
 #pragma unroll
-      for (int w = 0; w < LM_CONSUMERS; ++w) v = lm_max(v, wbest[w * 16 + tid]);
+      for (int w = 0; w < NC; ++w) v = lm_max(v, wbest[w * 16 + tid]);
       a.part[(size_t)b * M + tid] = v;
       __threadfence();  // this word is visible device-wide before the arrival below
     }
-    lm_consumer_bar();
+    lm_consumer_bar<NC>();
     if (warp == 0 && lane == 0) trace_stamp(tr, 6);
     // the last CTA to arrive combines every CTA's words (in CTA order: the
     // maximum does not depend on it) and clears the counter
@@ -297,7 +301,7 @@ __global__ void __launch_bounds__(LM_THREADS, 1) w8a16_lmh_kernel(const LmArgs a
       const unsigned int prev = atomicAdd(a.counter, 1u);
       *last_flag = prev == (unsigned int)(G - 1) ? 1 : 0;
     }
-    lm_consumer_bar();
+    lm_consumer_bar<NC>();
     if (*last_flag) {
       __threadfence();
       if (tid < M) {
@@ -340,7 +344,7 @@ LmPlan lmh_plan(int64_t M, int64_t N, int64_t K, int sms) {
   const int64_t tile_bytes = LM_TILE * K;
   const int64_t x_bytes = M * K * 2;
   const int64_t off_x_max = LM_SMEM_MAX - ((x_bytes + 15) & ~15ll) - (16 * LM_MAX_STAGES + 32) -
-                            8 * LM_CONSUMERS * 16 - 16;
+                            8 * LM_MAX_CONSUMERS * 16 - 16;
   int64_t stages = off_x_max / tile_bytes;
   const int64_t per_cta = (tiles + grid - 1) / grid;
   if (stages > LM_MAX_STAGES) stages = LM_MAX_STAGES;
@@ -349,7 +353,7 @@ LmPlan lmh_plan(int64_t M, int64_t N, int64_t K, int sms) {
   if (stages < 1) return p;
   const int64_t off_x = stages * tile_bytes;
   const int64_t off_bar = off_x + ((x_bytes + 15) & ~15ll);
-  const int64_t total = off_bar + 16 * stages + 32 + 8 * LM_CONSUMERS * 16;
+  const int64_t total = off_bar + 16 * stages + 32 + 8 * LM_MAX_CONSUMERS * 16;
   if (total > LM_SMEM_MAX) return p;
   p.ok = true;
   p.grid = (int)grid;
@@ -360,14 +364,22 @@ LmPlan lmh_plan(int64_t M, int64_t N, int64_t K, int sms) {
   return p;
 }
 
-template <int NB>
+int lmh_consumers() {
+  static const int v = [] {
+    const char* e = std::getenv("DDQ_LMH_WARPS");
+    return (e && std::atoi(e) == 8) ? 8 : 16;
+  }();
+  return v;
+}
+
+template <int NB, int NC>
 int launch_lmh_t(const LmPlan& p, const LmArgs& a, cudaStream_t s) {
   static SmemAttrOnce attr;
-  const int ast = ensure_smem_attr(attr, current_device(), w8a16_lmh_kernel<NB>, LM_SMEM_MAX);
+  const int ast = ensure_smem_attr(attr, current_device(), w8a16_lmh_kernel<NB, NC>, LM_SMEM_MAX);
   if (ast) return ast;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)p.grid);
-  cfg.blockDim = dim3(LM_THREADS);
+  cfg.blockDim = dim3((NC + 1) * 32);
   cfg.dynamicSmemBytes = (size_t)p.smem;
   cfg.stream = s;
   cudaLaunchAttribute at;
@@ -375,7 +387,7 @@ int launch_lmh_t(const LmPlan& p, const LmArgs& a, cudaStream_t s) {
   at.val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = &at;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, w8a16_lmh_kernel<NB>, a);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, w8a16_lmh_kernel<NB, NC>, a);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return DDQ_ERR_LAUNCH;
@@ -422,7 +434,10 @@ int launch_lmh(const __half* x, const uint8_t* wq, const float* scales, int M, i
   a.off_bar = p.off_bar;
   a.timeout_ns = timeout_ns;
   a.trace = (debug_flags & 2) != 0;
-  return M <= 8 ? launch_lmh_t<1>(p, a, s) : launch_lmh_t<2>(p, a, s);
+  // 9..16 tokens: 8 consumers (16 would exceed the registers a thread may
+  // hold at 544 threads per CTA)
+  if (M > 8) return launch_lmh_t<2, 8>(p, a, s);
+  return lmh_consumers() == 8 ? launch_lmh_t<1, 8>(p, a, s) : launch_lmh_t<1, 16>(p, a, s);
 }
 
 bool lmh_eligible(int64_t M, int64_t N, int64_t K, int sms) { return lmh_plan(M, N, K, sms).ok; }

@@ -19,9 +19,9 @@
 //     where shared memory leaves room, stream their own slices meanwhile;
 //   * after the dependency: one bulk copy of all of x (M x K fp16,
 //     contiguous), then warp w runs the 64-wide K blocks kb = w, w + 8, ...
-//     of all its tiles, ordered so that consecutive MMAs never depend on
-//     each other, then a warp-ordered sum of the 8 partials per output,
-//     scale * 256, bias, fp16.
+//     of all its tiles (tile by tile; ordering the MMAs so that consecutive
+//     ones never share an accumulator measured slower), then a
+//     warp-ordered sum of the 8 partials per output, scale * 256, bias, fp16.
 // Weights on the A operand: one MMA covers 16 weight rows x 8 tokens, so at
 // up to 8 tokens it takes half the MMAs (and the same e4m3 conversions) of
 // tokens-on-rows; 9..16 tokens use two 8-token blocks per A fragment.
@@ -184,66 +184,45 @@ __global__ void __launch_bounds__(RS_THREADS, 2) w8a16_rs_kernel(const RsArgs a)
     xok[nb] = tok < M;
     xrow[nb] = sbase + (uint32_t)a.off_x + (uint32_t)((xok[nb] ? tok : 0) * K * 2 + t * 32);
   }
-  // Consecutive MMAs must not feed each other (mma.sync issues in order and
-  // a dependent one waits for its predecessor's result), so the loop runs
-  // j (the 4 MMAs of a 64-wide K block) outside the tiles and token blocks,
-  // and with fewer than 4 (tile, token block) pairs the j's accumulate into
-  // JS separate sets: every run of 4 consecutive MMAs is independent.
-  constexpr int JS = NT * NB >= 4 ? 1 : NT * NB >= 2 ? 2 : 4;
-  float acc[NT][NB][JS][4];
+  float acc[NT][NB][4];
 #pragma unroll
   for (int i = 0; i < NT; ++i)
 #pragma unroll
-    for (int nb = 0; nb < NB; ++nb)
-#pragma unroll
-      for (int js = 0; js < JS; ++js)
-        acc[i][nb][js][0] = acc[i][nb][js][1] = acc[i][nb][js][2] = acc[i][nb][js][3] = 0.f;
+    for (int nb = 0; nb < NB; ++nb) acc[i][nb][0] = acc[i][nb][1] = acc[i][nb][2] = acc[i][nb][3] = 0.f;
   for (int kb = warp; kb < KB; kb += RS_WARPS) {
-    uint32_t xs[NB][8];
+    uint4 x0[NB], x1[NB];
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb) {
-      uint4 x0 = make_uint4(0u, 0u, 0u, 0u), x1 = x0;
+      x0[nb] = make_uint4(0u, 0u, 0u, 0u);
+      x1[nb] = x0[nb];
       if (xok[nb]) {
-        x0 = rs_lds128(xrow[nb] + (uint32_t)(kb * 128));
-        x1 = rs_lds128(xrow[nb] + (uint32_t)(kb * 128 + 16));
+        x0[nb] = rs_lds128(xrow[nb] + (uint32_t)(kb * 128));
+        x1[nb] = rs_lds128(xrow[nb] + (uint32_t)(kb * 128 + 16));
       }
-      xs[nb][0] = x0.x; xs[nb][1] = x0.y; xs[nb][2] = x0.z; xs[nb][3] = x0.w;
-      xs[nb][4] = x1.x; xs[nb][5] = x1.y; xs[nb][6] = x1.z; xs[nb][7] = x1.w;
     }
-    uint32_t lw[NT][4], hw[NT][4];  // this K block's raw e4m3 weight words, every tile
 #pragma unroll
     for (int tl = 0; tl < NT; ++tl) {
       if (tl < ntl) {
         const uint4 lo = rs_lds128(wlo + (uint32_t)tl * tstride + (uint32_t)(kb * 64));
         const uint4 hi = rs_lds128(whi + (uint32_t)tl * tstride + (uint32_t)(kb * 64));
-        lw[tl][0] = lo.x; lw[tl][1] = lo.y; lw[tl][2] = lo.z; lw[tl][3] = lo.w;
-        hw[tl][0] = hi.x; hw[tl][1] = hi.y; hw[tl][2] = hi.z; hw[tl][3] = hi.w;
-      }
-    }
+        const uint32_t lw[4] = {lo.x, lo.y, lo.z, lo.w};
+        const uint32_t hw[4] = {hi.x, hi.y, hi.z, hi.w};
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t a0 = e4m3x2_to_half2_bits_x2m8(lw[j], 0x4140u);
+          const uint32_t a2 = e4m3x2_to_half2_bits_x2m8(lw[j], 0x4342u);
+          const uint32_t a1 = e4m3x2_to_half2_bits_x2m8(hw[j], 0x4140u);
+          const uint32_t a3 = e4m3x2_to_half2_bits_x2m8(hw[j], 0x4342u);
 #pragma unroll
-      for (int tl = 0; tl < NT; ++tl) {
-        if (tl < ntl) {
-          const uint32_t a0 = e4m3x2_to_half2_bits_x2m8(lw[tl][j], 0x4140u);
-          const uint32_t a2 = e4m3x2_to_half2_bits_x2m8(lw[tl][j], 0x4342u);
-          const uint32_t a1 = e4m3x2_to_half2_bits_x2m8(hw[tl][j], 0x4140u);
-          const uint32_t a3 = e4m3x2_to_half2_bits_x2m8(hw[tl][j], 0x4342u);
-#pragma unroll
-          for (int nb = 0; nb < NB; ++nb)
-            rs_mma(acc[tl][nb][j % JS], a0, a1, a2, a3, xs[nb][2 * j], xs[nb][2 * j + 1]);
+          for (int nb = 0; nb < NB; ++nb) {
+            const uint32_t xs[8] = {x0[nb].x, x0[nb].y, x0[nb].z, x0[nb].w,
+                                    x1[nb].x, x1[nb].y, x1[nb].z, x1[nb].w};
+            rs_mma(acc[tl][nb], a0, a1, a2, a3, xs[2 * j], xs[2 * j + 1]);
+          }
         }
       }
     }
   }
-#pragma unroll
-  for (int i = 0; i < NT; ++i)
-#pragma unroll
-    for (int nb = 0; nb < NB; ++nb)
-#pragma unroll
-      for (int js = 1; js < JS; ++js)
-#pragma unroll
-        for (int q = 0; q < 4; ++q) acc[i][nb][0][q] += acc[i][nb][js][q];
   __syncthreads();  // the weight slice is dead: the partial sums reuse it
   if (tid == 0) trace_stamp(tr, 4);
 
@@ -258,10 +237,10 @@ __global__ void __launch_bounds__(RS_THREADS, 2) w8a16_rs_kernel(const RsArgs a)
 #pragma unroll
       for (int nb = 0; nb < NB; ++nb) {
         float* p = red + ((size_t)warp * TOK + nb * 8 + 2 * t) * rows + tl * RS_TILE + g;
-        p[0] = acc[tl][nb][0][0];
-        p[rows] = acc[tl][nb][0][1];
-        p[8] = acc[tl][nb][0][2];
-        p[rows + 8] = acc[tl][nb][0][3];
+        p[0] = acc[tl][nb][0];
+        p[rows] = acc[tl][nb][1];
+        p[8] = acc[tl][nb][2];
+        p[rows + 8] = acc[tl][nb][3];
       }
     }
   }
@@ -311,6 +290,9 @@ RsPlan rs_plan(int64_t M, int64_t N, int64_t K, int sms) {
   const int64_t ntl = (tiles + grid - 1) / grid;  // largest per-CTA tile count
   const int64_t nb = M <= 8 ? 1 : 2;
   if (ntl > (nb == 1 ? RS_MAX_TILES : RS_MAX_TILES - 1)) return p;
+  // one tile per CTA with a long K (the Qwen2.5 down projection, 56 CTAs):
+  // the thin kernel's 8-row tiles on twice the SMs measured faster
+  if (ntl == 1 && K >= 2048) return p;
   const int64_t w_bytes = ntl * RS_TILE * K;
   const int64_t red_bytes = (int64_t)RS_WARPS * ntl * RS_TILE * nb * 8 * 4;
   if (red_bytes > w_bytes) return p;  // the partial sums reuse the weight slice
