@@ -14,8 +14,7 @@
 // contiguous run of tiles - 151,936 rows are 9,496 tiles, 64 or 65 per CTA on
 // 148 SMs, so the last CTAs finish within 1.5 % of the others.  A tile's
 // 16 x K bytes are one contiguous range: one bulk copy (TMA engine) per tile,
-// issued by a producer warp into a ring of stages, many tiles in flight per
-// SM.  Each consumer warp takes whole tiles (tile i goes to warp i mod the
+// issued by a producer warp into a ring of two stages per consumer warp.  Each consumer warp takes whole tiles (tile i goes to warp i mod the
 // consumer count), so no partial sums cross warps; a thread keeps the best packed
 // word of the rows it sees per token.  At the end the CTA reduces them and
 // writes one word per token to a per-CTA slot of the workspace; the last CTA
@@ -33,13 +32,16 @@
 namespace ddq {
 namespace {
 
-// Consumer warps: every warp computes one tile at a time and is bound by
-// its own instruction latencies, so the tiles in flight per SM set the rate;
-// 16 consumers (plus the producer warp) by default, DDQ_LMH_WARPS=8 for
-// measurements.
-constexpr int LM_MAX_CONSUMERS = 16;
+// Consumer warps and ring stages: tile i goes to warp i mod NC and to stage
+// i mod 2 NC, so every stage belongs to one warp, which consumes its uses in
+// order - a warp never waits on a phase two ahead of the last one completed
+// (a parity wait cannot tell those apart) - and each warp's next tile loads
+// while it computes the current one.  NC = 7: 14 stages of a 16 x 896-byte
+// tile plus 16 tokens of activations fit in shared memory.
+constexpr int LM_NC = 7;
+constexpr int LM_MAX_CONSUMERS = LM_NC;
 constexpr int LM_TILE = 16;
-constexpr int LM_MAX_STAGES = 16;
+constexpr int LM_MAX_STAGES = 2 * 7;
 constexpr int LM_SMEM_MAX = 232448;
 
 struct LmArgs {
@@ -345,12 +347,8 @@ LmPlan lmh_plan(int64_t M, int64_t N, int64_t K, int sms) {
   const int64_t x_bytes = M * K * 2;
   const int64_t off_x_max = LM_SMEM_MAX - ((x_bytes + 15) & ~15ll) - (16 * LM_MAX_STAGES + 32) -
                             8 * LM_MAX_CONSUMERS * 16 - 16;
-  int64_t stages = off_x_max / tile_bytes;
-  const int64_t per_cta = (tiles + grid - 1) / grid;
-  if (stages > LM_MAX_STAGES) stages = LM_MAX_STAGES;
-  if (stages > per_cta) stages = per_cta;
-  if (stages < 2 && per_cta > 1) return p;
-  if (stages < 1) return p;
+  const int64_t stages = 2 * LM_NC;  // the ownership rule above needs exactly this many
+  if (stages * tile_bytes > off_x_max) return p;
   const int64_t off_x = stages * tile_bytes;
   const int64_t off_bar = off_x + ((x_bytes + 15) & ~15ll);
   const int64_t total = off_bar + 16 * stages + 32 + 8 * LM_MAX_CONSUMERS * 16;
@@ -362,14 +360,6 @@ LmPlan lmh_plan(int64_t M, int64_t N, int64_t K, int sms) {
   p.off_x = (int)off_x;
   p.off_bar = (int)off_bar;
   return p;
-}
-
-int lmh_consumers() {
-  static const int v = [] {
-    const char* e = std::getenv("DDQ_LMH_WARPS");
-    return (e && std::atoi(e) == 8) ? 8 : 16;
-  }();
-  return v;
 }
 
 template <int NB, int NC>
@@ -434,10 +424,7 @@ int launch_lmh(const __half* x, const uint8_t* wq, const float* scales, int M, i
   a.off_bar = p.off_bar;
   a.timeout_ns = timeout_ns;
   a.trace = (debug_flags & 2) != 0;
-  // 9..16 tokens: 8 consumers (16 would exceed the registers a thread may
-  // hold at 544 threads per CTA)
-  if (M > 8) return launch_lmh_t<2, 8>(p, a, s);
-  return lmh_consumers() == 8 ? launch_lmh_t<1, 8>(p, a, s) : launch_lmh_t<1, 16>(p, a, s);
+  return M <= 8 ? launch_lmh_t<1, LM_NC>(p, a, s) : launch_lmh_t<2, LM_NC>(p, a, s);
 }
 
 bool lmh_eligible(int64_t M, int64_t N, int64_t K, int sms) { return lmh_plan(M, N, K, sms).ok; }
