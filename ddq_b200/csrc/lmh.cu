@@ -14,9 +14,10 @@
 // contiguous run of tiles - 151,936 rows are 9,496 tiles, 64 or 65 per CTA on
 // 148 SMs, so the last CTAs finish within 1.5 % of the others.  A tile's
 // 16 x K bytes are one contiguous range: one bulk copy (TMA engine) per tile,
-// issued by a producer warp into a ring of two stages per consumer warp.  Each consumer warp takes whole tiles (tile i goes to warp i mod the
-// consumer count), so no partial sums cross warps; a thread keeps the best packed
-// word of the rows it sees per token.  At the end the CTA reduces them and
+// issued by a producer warp into a ring of two stages per consumer warp.
+// Each consumer warp takes whole tiles (tile i goes to warp i mod the
+// consumer count), so no partial sums cross warps; a thread keeps the best
+// packed word of the rows it sees per token.  At the end the CTA reduces them and
 // writes one word per token to a per-CTA slot of the workspace; the last CTA
 // to finish (an arrival counter in the workspace) combines the slots in CTA
 // order into packed[] and ids[] and clears the counter for the next call.
