@@ -46,6 +46,26 @@ __device__ __forceinline__ uint32_t e4m3x2_to_half2_bits_x2m8(uint32_t v, uint32
   return (t + (t & 0x00800080u)) << 7;
 }
 
+// The four e4m3fn bytes of w -> two fp16x2 words (bytes 0,1 -> lo; 2,3 -> hi).
+// HW: the hardware converter (cvt.rn.f16x2.e4m3x2, exact: every e4m3fn value
+// is an fp16 value), one instruction per pair; otherwise the integer-ALU form
+// above, four instructions per pair, whose results are the values times 2^-8.
+// kE4m3ToF16Scale<HW> is the factor that restores the value (1 or 256).
+template <bool HW>
+__device__ __forceinline__ void e4m3x4_to_half2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  if constexpr (HW) {
+    asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\t"
+        "cvt.rn.f16x2.e4m3x2 %0, l;\n\tcvt.rn.f16x2.e4m3x2 %1, h;\n\t}"
+        : "=r"(lo), "=r"(hi)
+        : "r"(w));
+  } else {
+    lo = e4m3x2_to_half2_bits_x2m8(w, 0x4140u);
+    hi = e4m3x2_to_half2_bits_x2m8(w, 0x4342u);
+  }
+}
+template <bool HW>
+constexpr float kE4m3ToF16Scale = HW ? 1.f : 256.f;
+
 // Two fp32 values -> two e4m3fn bytes (a -> low byte), round to nearest even,
 // saturating to +-448.  For |v| <= 464 this equals torch's float8_e4m3fn cast.
 __device__ __forceinline__ uint16_t float2_to_e4m3x2(float a, float b) {

@@ -97,7 +97,7 @@ __device__ __forceinline__ unsigned long long lm_max(unsigned long long a, unsig
 // activations [M][K] fp16; off_bar full[stages], empty[stages], the x
 // barrier, the abort, drain and last-CTA flags, then (at + 32) the per-warp
 // best words [NC][16 tokens] (u64).
-template <int NB, int NC>
+template <int NB, int NC, bool HW>
 __global__ void __launch_bounds__((NC + 1) * 32, 1) w8a16_lmh_kernel(const LmArgs a) {
   extern __shared__ __align__(128) uint8_t lm_smem[];
   const uint32_t sbase = ptx::smem_u32(lm_smem);
@@ -187,8 +187,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) w8a16_lmh_kernel(const LmArg
       const int row0 = (tile0 + i) * LM_TILE;
       // the two rows this thread scores, and their scales (issued early)
       const int nlo = row0 + g, nhi = row0 + g + 8;
-      const float slo = nlo < N ? a.scales[nlo] * 256.f : 0.f;
-      const float shi = nhi < N ? a.scales[nhi] * 256.f : 0.f;
+      const float slo = nlo < N ? a.scales[nlo] * kE4m3ToF16Scale<HW> : 0.f;
+      const float shi = nhi < N ? a.scales[nhi] * kE4m3ToF16Scale<HW> : 0.f;
       if (!ptx::mbar_wait(bar_full + 8 * s, (uint32_t)((i / S) & 1), a.timeout_ns, abort_flag)) {
         ok = false;
         break;
@@ -236,10 +236,9 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) w8a16_lmh_kernel(const LmArg
         for (int j = 0; j < 4; ++j) {
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            const uint32_t a0 = e4m3x2_to_half2_bits_x2m8(lw[h][j], 0x4140u);
-            const uint32_t a2 = e4m3x2_to_half2_bits_x2m8(lw[h][j], 0x4342u);
-            const uint32_t a1 = e4m3x2_to_half2_bits_x2m8(hw[h][j], 0x4140u);
-            const uint32_t a3 = e4m3x2_to_half2_bits_x2m8(hw[h][j], 0x4342u);
+            uint32_t a0, a1, a2, a3;
+            e4m3x4_to_half2x2<HW>(lw[h][j], a0, a2);
+            e4m3x4_to_half2x2<HW>(hw[h][j], a1, a3);
 #pragma unroll
             for (int nb = 0; nb < NB; ++nb)
               lm_mma(acc[2 * h + (j & 1)][nb], a0, a1, a2, a3, xs[h][nb][2 * j], xs[h][nb][2 * j + 1]);
@@ -363,10 +362,18 @@ LmPlan lmh_plan(int64_t M, int64_t N, int64_t K, int sms) {
   return p;
 }
 
-template <int NB, int NC>
+bool lmh_hw_cvt() {
+  static const bool v = [] {
+    const char* e = std::getenv("DDQ_E4M3_CVT");
+    return !(e && e[0] == 'i');
+  }();
+  return v;
+}
+
+template <int NB, int NC, bool HW>
 int launch_lmh_t(const LmPlan& p, const LmArgs& a, cudaStream_t s) {
   static SmemAttrOnce attr;
-  const int ast = ensure_smem_attr(attr, current_device(), w8a16_lmh_kernel<NB, NC>, LM_SMEM_MAX);
+  const int ast = ensure_smem_attr(attr, current_device(), w8a16_lmh_kernel<NB, NC, HW>, LM_SMEM_MAX);
   if (ast) return ast;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)p.grid);
@@ -378,7 +385,7 @@ int launch_lmh_t(const LmPlan& p, const LmArgs& a, cudaStream_t s) {
   at.val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = &at;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, w8a16_lmh_kernel<NB, NC>, a);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, w8a16_lmh_kernel<NB, NC, HW>, a);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return DDQ_ERR_LAUNCH;
@@ -425,7 +432,9 @@ int launch_lmh(const __half* x, const uint8_t* wq, const float* scales, int M, i
   a.off_bar = p.off_bar;
   a.timeout_ns = timeout_ns;
   a.trace = (debug_flags & 2) != 0;
-  return M <= 8 ? launch_lmh_t<1, LM_NC>(p, a, s) : launch_lmh_t<2, LM_NC>(p, a, s);
+  if (lmh_hw_cvt())
+    return M <= 8 ? launch_lmh_t<1, LM_NC, true>(p, a, s) : launch_lmh_t<2, LM_NC, true>(p, a, s);
+  return M <= 8 ? launch_lmh_t<1, LM_NC, false>(p, a, s) : launch_lmh_t<2, LM_NC, false>(p, a, s);
 }
 
 bool lmh_eligible(int64_t M, int64_t N, int64_t K, int sms) { return lmh_plan(M, N, K, sms).ok; }

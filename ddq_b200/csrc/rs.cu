@@ -97,7 +97,7 @@ __device__ __forceinline__ void rs_mma(float* d, uint32_t a0, uint32_t a1, uint3
 //   off_x           x, row-major fp16 [M][K] (one bulk copy)
 //   off_sc, off_bi  per-row scale * 256 and bias (fp32)
 //   off_bar         weight barrier, activation barrier, abort and drain flags
-template <int NT, int NB>
+template <int NT, int NB, bool HW>
 __global__ void __launch_bounds__(RS_THREADS, 2) w8a16_rs_kernel(const RsArgs a) {
   extern __shared__ __align__(128) uint8_t rs_smem[];
   const uint32_t sbase = ptx::smem_u32(rs_smem);
@@ -141,7 +141,7 @@ __global__ void __launch_bounds__(RS_THREADS, 2) w8a16_rs_kernel(const RsArgs a)
     const int n = row0 + tid;
     float s = 0.f, bv = 0.f;
     if (n < N) {
-      s = a.scales[n] * 256.f;
+      s = a.scales[n] * kE4m3ToF16Scale<HW>;
       if (a.bias_dtype == DDQ_DTYPE_F16) bv = __half2float(reinterpret_cast<const __half*>(a.bias)[n]);
       else if (a.bias_dtype == DDQ_DTYPE_F32) bv = reinterpret_cast<const float*>(a.bias)[n];
     }
@@ -209,10 +209,9 @@ __global__ void __launch_bounds__(RS_THREADS, 2) w8a16_rs_kernel(const RsArgs a)
         const uint32_t hw[4] = {hi.x, hi.y, hi.z, hi.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const uint32_t a0 = e4m3x2_to_half2_bits_x2m8(lw[j], 0x4140u);
-          const uint32_t a2 = e4m3x2_to_half2_bits_x2m8(lw[j], 0x4342u);
-          const uint32_t a1 = e4m3x2_to_half2_bits_x2m8(hw[j], 0x4140u);
-          const uint32_t a3 = e4m3x2_to_half2_bits_x2m8(hw[j], 0x4342u);
+          uint32_t a0, a1, a2, a3;
+          e4m3x4_to_half2x2<HW>(lw[j], a0, a2);
+          e4m3x4_to_half2x2<HW>(hw[j], a1, a3);
 #pragma unroll
           for (int nb = 0; nb < NB; ++nb) {
             const uint32_t xs[8] = {x0[nb].x, x0[nb].y, x0[nb].z, x0[nb].w,
@@ -316,11 +315,21 @@ RsPlan rs_plan(int64_t M, int64_t N, int64_t K, int sms) {
   return p;
 }
 
-template <int NT, int NB>
+// DDQ_E4M3_CVT=int selects the integer-ALU weight conversion, hw (default)
+// the hardware converter (for measurements).
+bool hw_cvt() {
+  static const bool v = [] {
+    const char* e = std::getenv("DDQ_E4M3_CVT");
+    return !(e && e[0] == 'i');
+  }();
+  return v;
+}
+
+template <int NT, int NB, bool HW>
 int launch_rs_t(const RsPlan& p, const RsArgs& a, cudaStream_t s) {
   // the launch's own size still sets the occupancy
   static SmemAttrOnce attr;
-  const int ast = ensure_smem_attr(attr, current_device(), w8a16_rs_kernel<NT, NB>, RS_SMEM_MAX);
+  const int ast = ensure_smem_attr(attr, current_device(), w8a16_rs_kernel<NT, NB, HW>, RS_SMEM_MAX);
   if (ast) return ast;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)p.grid);
@@ -332,7 +341,7 @@ int launch_rs_t(const RsPlan& p, const RsArgs& a, cudaStream_t s) {
   at.val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = &at;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, w8a16_rs_kernel<NT, NB>, a);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, w8a16_rs_kernel<NT, NB, HW>, a);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return DDQ_ERR_LAUNCH;
@@ -340,16 +349,16 @@ int launch_rs_t(const RsPlan& p, const RsArgs& a, cudaStream_t s) {
   return check_launch();
 }
 
-template <int NB>
+template <int NB, bool HW>
 int launch_rs_nb(const RsPlan& p, const RsArgs& a, cudaStream_t s) {
   switch (p.nt) {
-    case 1: return launch_rs_t<1, NB>(p, a, s);
-    case 2: return launch_rs_t<2, NB>(p, a, s);
-    case 3: return launch_rs_t<3, NB>(p, a, s);
-    case 4: return launch_rs_t<4, NB>(p, a, s);
-    case 5: return launch_rs_t<5, NB>(p, a, s);
+    case 1: return launch_rs_t<1, NB, HW>(p, a, s);
+    case 2: return launch_rs_t<2, NB, HW>(p, a, s);
+    case 3: return launch_rs_t<3, NB, HW>(p, a, s);
+    case 4: return launch_rs_t<4, NB, HW>(p, a, s);
+    case 5: return launch_rs_t<5, NB, HW>(p, a, s);
     default:
-      if constexpr (NB == 1) return launch_rs_t<6, NB>(p, a, s);
+      if constexpr (NB == 1) return launch_rs_t<6, NB, HW>(p, a, s);
       else return DDQ_ERR_SHAPE;  // 9..16 tokens take at most 5 tiles per CTA
   }
 }
@@ -383,7 +392,8 @@ int launch_rs(const __half* x, const uint8_t* wq, const float* scales, const voi
   a.off_bar = p.off_bar;
   a.timeout_ns = timeout_ns;
   a.trace = (debug_flags & 2) != 0;
-  return p.nb == 1 ? launch_rs_nb<1>(p, a, s) : launch_rs_nb<2>(p, a, s);
+  if (hw_cvt()) return p.nb == 1 ? launch_rs_nb<1, true>(p, a, s) : launch_rs_nb<2, true>(p, a, s);
+  return p.nb == 1 ? launch_rs_nb<1, false>(p, a, s) : launch_rs_nb<2, false>(p, a, s);
 }
 
 }  // namespace ddq
