@@ -1,4 +1,4 @@
-// lmh.cu - fused lm_head GEMM + greedy argmax for 1..16 tokens, streaming the
+// lmh.cu - fused lm_head GEMM + greedy argmax for 1..8 tokens, streaming the
 // weight through shared memory with large contiguous bulk copies.
 //
 // Semantics (engine.py:338 + sampler_d.cu:10-70 on the last position): for
@@ -305,10 +305,21 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) w8a16_lmh_kernel(const LmArg
     }
     lm_consumer_bar<NC>();
     if (*last_flag) {
+      // every consumer thread loads a share of the G x M words at once (one
+      // L2 round trip), folds them per token into shared memory, then the
+      // token maxima are written
       __threadfence();
+      unsigned long long* tok_best = wbest;  // reused: [M] words
+      if (tid < M) tok_best[tid] = 0ull;
+      lm_consumer_bar<NC>();
+      const int total = G * M;
+      for (int i = tid; i < total; i += NC * 32) {
+        const unsigned long long v = __ldcg(a.part + i);
+        if (v) atomicMax(tok_best + (i % M), v);
+      }
+      lm_consumer_bar<NC>();
       if (tid < M) {
-        unsigned long long v = 0ull;
-        for (int c = 0; c < G; ++c) v = lm_max(v, __ldcg(a.part + (size_t)c * M + tid));
+        const unsigned long long v = tok_best[tid];
         a.packed[tid] = v;
         if (a.ids) a.ids[tid] = v ? (long long)(0xFFFFFFFFull - (v & 0xFFFFFFFFull)) : 0ll;
       }
@@ -330,14 +341,16 @@ struct LmPlan {
 int64_t lmh_max_m() {
   static const int64_t v = [] {
     const char* e = std::getenv("DDQ_LMH_MAX_M");
-    return e ? (int64_t)std::atoll(e) : (int64_t)16;
+    return e ? (int64_t)std::atoll(e) : (int64_t)8;
   }();
   return v;
 }
 
 LmPlan lmh_plan(int64_t M, int64_t N, int64_t K, int sms) {
   LmPlan p{};
-  if (M < 1 || M > 16 || M > lmh_max_m() || N < 1 || K < 64 || K % 64 != 0 || K > 4096 ||
+  // 1..8 tokens (at 9..16 the consumers' MMAs, not the weight stream, bound
+  // it and the decode kernel's lm_head path measured faster)
+  if (M < 1 || M > 8 || M > lmh_max_m() || N < 1 || K < 64 || K % 64 != 0 || K > 4096 ||
       sms <= 0)
     return p;
   if (N > 0x7fffffff - LM_TILE) return p;

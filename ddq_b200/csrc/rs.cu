@@ -21,7 +21,7 @@
 //     contiguous), then warp w runs the 64-wide K blocks kb = w, w + 8, ...
 //     of all its tiles (tile by tile; ordering the MMAs so that consecutive
 //     ones never share an accumulator measured slower), then a
-//     warp-ordered sum of the 8 partials per output, scale * 256, bias, fp16.
+//     warp-ordered sum of the 8 partials per output, scale, bias, fp16.
 // Weights on the A operand: one MMA covers 16 weight rows x 8 tokens, so at
 // up to 8 tokens it takes half the MMAs (and the same e4m3 conversions) of
 // tokens-on-rows; 9..16 tokens use two 8-token blocks per A fragment.
@@ -31,9 +31,11 @@
 // activations (B); MMA j takes k 16t+4j .. 16t+4j+3 as the fragment's logical
 // k {2t, 2t+1, 2t+8, 2t+9}.  A and B follow the same map, so each MMA adds
 // the same products as in natural order, and one 16-byte weight load per
-// row feeds four MMAs.  The e4m3 -> fp16 conversion is integer-only and
-// exact (value * 2^-8, subnormals included); the factor 256 is folded into
-// the row scale.  Results are bitwise reproducible (fixed warp-ordered sum).
+// row feeds four MMAs.  The e4m3 -> fp16 conversion is the hardware
+// converter (one instruction per pair, exact, subnormals included; it
+// measured faster than the integer-ALU form, which DDQ_E4M3_CVT=int selects
+// and whose factor 2^-8 the row scale then undoes).  Results are bitwise
+// reproducible (fixed warp-ordered sum).
 #include <cstdlib>
 
 #include "common.cuh"
@@ -95,7 +97,8 @@ __device__ __forceinline__ void rs_mma(float* d, uint32_t a0, uint32_t a1, uint3
 //                   after the MMAs, the partial sums [warp][NB * 8][rows]
 //                   fp32 reuse it
 //   off_x           x, row-major fp16 [M][K] (one bulk copy)
-//   off_sc, off_bi  per-row scale * 256 and bias (fp32)
+//   off_sc, off_bi  per-row scale (times 256 with the integer conversion) and
+//                   bias (fp32)
 //   off_bar         weight barrier, activation barrier, abort and drain flags
 template <int NT, int NB, bool HW>
 __global__ void __launch_bounds__(RS_THREADS, 2) w8a16_rs_kernel(const RsArgs a) {

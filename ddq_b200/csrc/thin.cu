@@ -22,7 +22,7 @@
 //     starts its own copy while this one computes;
 //   * after the wait: the M x K fp16 activations (L2), one bulk copy per
 //     token row, then per (tile, 64-wide K block) one 16-byte weight load,
-//     16 exact e4m3 -> fp16 conversions and 4 MMAs, tokens on the MMA rows
+//     8 exact e4m3 -> fp16x2 conversions and 4 MMAs, tokens on the MMA rows
 //     (zero rows past M), the tile's 8 weight rows on the MMA columns;
 //   * no activation split pre-pass (fp16 activations are used as they are),
 //     no workspace; both mbarrier waits are bounded (DDQ_ERR_TIMEOUT in the
@@ -35,9 +35,9 @@
 // same map, so each MMA adds the same products as in natural order, and one
 // 16-byte load per operand feeds four MMAs.
 //
-// Conversion: e4m3x2_to_half2_bits_x2m8 (integer ALU ops) gives each weight
-// times 2^-8 exactly, subnormals included; the factor 256 is folded into the
-// row scale (exact).  The eight warps split the (tile, K block) units
+// Conversion: the hardware converter (cvt.rn.f16x2.e4m3x2, one instruction per
+// pair of weights; exact, subnormals included - it measured faster than the
+// four-instruction integer form in the resident-slice kernel).  The eight warps split the (tile, K block) units
 // round-robin, write their partial sums to shared memory and the epilogue
 // adds them in warp order, so results are bitwise reproducible.
 #include <cstdlib>
@@ -111,7 +111,7 @@ __device__ __forceinline__ void th_mma(float* d, uint32_t a0, uint32_t a1, uint3
 //              == 0, so that rows g and g + 1 fall on different banks)
 //   off_x      activations, row-major fp16, row stride sx = 2K + 16 (rows
 //              g and g + 1 on different banks)
-//   off_sc     per-row scale * 256 (fp32), off_bi per-row bias (fp32)
+//   off_sc     per-row scale (fp32), off_bi per-row bias (fp32)
 //   off_red    partial sums [warp][m][tile][8 rows] (fp32); aliases the
 //              weight and activation area, which is dead by then, when it fits
 //   off_bar    weight barrier, activation barrier, abort flag
@@ -164,7 +164,7 @@ __global__ void __launch_bounds__(TH_THREADS) w8a16_thin_kernel(const ThinArgs a
     const int n = row0 + tid;
     float s = 0.f, bv = 0.f;
     if (n < N) {
-      s = a.scales[n] * 256.f;
+      s = a.scales[n] * kE4m3ToF16Scale<true>;
       if (a.bias_dtype == DDQ_DTYPE_F16) bv = __half2float(reinterpret_cast<const __half*>(a.bias)[n]);
       else if (a.bias_dtype == DDQ_DTYPE_F32) bv = reinterpret_cast<const float*>(a.bias)[n];
     }
@@ -211,14 +211,15 @@ __global__ void __launch_bounds__(TH_THREADS) w8a16_thin_kernel(const ThinArgs a
           h0 = lds128(xhi + (uint32_t)(kb * 128));
           h1 = lds128(xhi + (uint32_t)(kb * 128 + 16));
         }
-        th_mma(acc[tl], l0.x, h0.x, l0.y, h0.y, e4m3x2_to_half2_bits_x2m8(wv.x, 0x4140u),
-               e4m3x2_to_half2_bits_x2m8(wv.x, 0x4342u));
-        th_mma(acc[tl], l0.z, h0.z, l0.w, h0.w, e4m3x2_to_half2_bits_x2m8(wv.y, 0x4140u),
-               e4m3x2_to_half2_bits_x2m8(wv.y, 0x4342u));
-        th_mma(acc[tl], l1.x, h1.x, l1.y, h1.y, e4m3x2_to_half2_bits_x2m8(wv.z, 0x4140u),
-               e4m3x2_to_half2_bits_x2m8(wv.z, 0x4342u));
-        th_mma(acc[tl], l1.z, h1.z, l1.w, h1.w, e4m3x2_to_half2_bits_x2m8(wv.w, 0x4140u),
-               e4m3x2_to_half2_bits_x2m8(wv.w, 0x4342u));
+        uint32_t b[8];
+        e4m3x4_to_half2x2<true>(wv.x, b[0], b[1]);
+        e4m3x4_to_half2x2<true>(wv.y, b[2], b[3]);
+        e4m3x4_to_half2x2<true>(wv.z, b[4], b[5]);
+        e4m3x4_to_half2x2<true>(wv.w, b[6], b[7]);
+        th_mma(acc[tl], l0.x, h0.x, l0.y, h0.y, b[0], b[1]);
+        th_mma(acc[tl], l0.z, h0.z, l0.w, h0.w, b[2], b[3]);
+        th_mma(acc[tl], l1.x, h1.x, l1.y, h1.y, b[4], b[5]);
+        th_mma(acc[tl], l1.z, h1.z, l1.w, h1.w, b[6], b[7]);
       }
     }
   }
