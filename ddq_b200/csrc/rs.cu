@@ -267,6 +267,151 @@ __global__ void __launch_bounds__(RS_THREADS, 2) w8a16_rs_kernel(const RsArgs a)
   }
 }
 
+// ----------------------------------------------------------------------------
+// 17..64 tokens: warps over token blocks
+// ----------------------------------------------------------------------------
+// Same resident weight slice and bulk-copied activations, but the 8 warps
+// form a grid of NBW token blocks of 8 tokens x KSW = 8 / NBW K slices:
+// warp w takes token block w mod NBW and the 64-wide K blocks kb = w / NBW
+// (mod KSW) of every tile.  Each warp then owns its tokens' outputs (no
+// cross-warp sum at all at 64 tokens, a sum of two slices at 17..32), at the
+// price of converting every weight once per token block - cheap with the
+// hardware converter - instead of holding 8 token blocks of accumulators.
+template <int NT, int NBW, bool HW>
+__global__ void __launch_bounds__(RS_THREADS, 1) w8a16_rsw_kernel(const RsArgs a) {
+  constexpr int KSW = RS_WARPS / NBW;
+  extern __shared__ __align__(128) uint8_t rs_smem[];
+  const uint32_t sbase = ptx::smem_u32(rs_smem);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int G = gridDim.x, b = blockIdx.x;
+  const int tile0 = (int)(((int64_t)b * a.tiles) / G);
+  const int ntl = (int)(((int64_t)(b + 1) * a.tiles) / G) - tile0;  // 1..NT
+  const int row0 = tile0 * RS_TILE, rows = ntl * RS_TILE;
+  const int M = a.M, N = a.N, K = a.K, KB = K >> 6;
+  const int valid = min(rows, N - row0);
+  const uint32_t bar_w = sbase + (uint32_t)a.off_bar, bar_x = bar_w + 8;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(rs_smem + a.off_bar + 16);
+  volatile int* drain_flag = reinterpret_cast<volatile int*>(rs_smem + a.off_bar + 20);
+  const bool tr = a.trace != 0;
+  if (tid == 0) {
+    trace_stamp(tr, 0);
+    ptx::mbar_init(bar_w, 1);
+    ptx::mbar_init(bar_x, 1);
+    *abort_flag = 0;
+    *drain_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  __syncthreads();
+  if (tid == 0) {
+    ptx::mbar_arrive_expect_tx(bar_w, (uint32_t)(valid * K));
+    rs_bulk_g2s(sbase, a.wq + (size_t)row0 * K, (uint32_t)(valid * K), bar_w);
+    trace_stamp(tr, 2);
+  }
+  ptx::pdl_launch_dependents();
+  for (int i = valid * K / 16 + tid; i < rows * K / 16; i += RS_THREADS)
+    reinterpret_cast<uint4*>(rs_smem)[i] = make_uint4(0u, 0u, 0u, 0u);
+  float* sc = reinterpret_cast<float*>(rs_smem + a.off_sc);
+  float* bi = reinterpret_cast<float*>(rs_smem + a.off_bi);
+  if (tid < rows) {
+    const int n = row0 + tid;
+    float s = 0.f, bv = 0.f;
+    if (n < N) {
+      s = a.scales[n] * kE4m3ToF16Scale<HW>;
+      if (a.bias_dtype == DDQ_DTYPE_F16) bv = __half2float(reinterpret_cast<const __half*>(a.bias)[n]);
+      else if (a.bias_dtype == DDQ_DTYPE_F32) bv = reinterpret_cast<const float*>(a.bias)[n];
+    }
+    sc[tid] = s;
+    bi[tid] = bv;
+  }
+  ptx::pdl_wait();
+  if (tid == 0) {
+    trace_stamp(tr, 3);
+    ptx::mbar_arrive_expect_tx(bar_x, (uint32_t)(M * K * 2));
+    rs_bulk_g2s(sbase + (uint32_t)a.off_x, a.x, (uint32_t)(M * K * 2), bar_x);
+  }
+  if (ptx::mbar_wait(bar_w, 0u, a.timeout_ns, abort_flag))
+    ptx::mbar_wait(bar_x, 0u, a.timeout_ns, abort_flag);
+  __syncthreads();
+  if (*abort_flag) {
+    if (tid == 0) {
+      record_device_error(DDQ_ERR_TIMEOUT);
+      ptx::mbar_wait(bar_w, 0u, a.timeout_ns, drain_flag);
+      ptx::mbar_wait(bar_x, 0u, a.timeout_ns, drain_flag);
+    }
+    return;
+  }
+  if (tid == 0) trace_stamp(tr, 5);
+
+  const int g = lane >> 2, t = lane & 3;
+  const int nb = warp % NBW, ks = warp / NBW;
+  const int tok = nb * 8 + g;
+  const bool xok = tok < M;
+  const uint32_t xrow = sbase + (uint32_t)a.off_x + (uint32_t)((xok ? tok : 0) * K * 2 + t * 32);
+  const uint32_t wlo = sbase + (uint32_t)(g * K + t * 16);
+  const uint32_t whi = wlo + (uint32_t)(8 * K);
+  const uint32_t tstride = (uint32_t)(RS_TILE * K);
+  float acc[NT][4];
+#pragma unroll
+  for (int i = 0; i < NT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  for (int kb = ks; kb < KB; kb += KSW) {
+    uint4 x0 = make_uint4(0u, 0u, 0u, 0u), x1 = x0;
+    if (xok) {
+      x0 = rs_lds128(xrow + (uint32_t)(kb * 128));
+      x1 = rs_lds128(xrow + (uint32_t)(kb * 128 + 16));
+    }
+    const uint32_t xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+    for (int tl = 0; tl < NT; ++tl) {
+      if (tl < ntl) {
+        const uint4 lo = rs_lds128(wlo + (uint32_t)tl * tstride + (uint32_t)(kb * 64));
+        const uint4 hi = rs_lds128(whi + (uint32_t)tl * tstride + (uint32_t)(kb * 64));
+        const uint32_t lw[4] = {lo.x, lo.y, lo.z, lo.w};
+        const uint32_t hw[4] = {hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t a0, a1, a2, a3;
+          e4m3x4_to_half2x2<HW>(lw[j], a0, a2);
+          e4m3x4_to_half2x2<HW>(hw[j], a1, a3);
+          rs_mma(acc[tl], a0, a1, a2, a3, xs[2 * j], xs[2 * j + 1]);
+        }
+      }
+    }
+  }
+  __syncthreads();  // the weight slice is dead: the K slices' partials reuse it
+  if (tid == 0) trace_stamp(tr, 4);
+  // partials [K slice][token][row] (row-contiguous), then the slice-ordered sum
+  const int mpad = NBW * 8;
+  float* red = reinterpret_cast<float*>(rs_smem);
+#pragma unroll
+  for (int tl = 0; tl < NT; ++tl) {
+    if (tl < ntl) {
+      float* p = red + ((size_t)ks * mpad + nb * 8 + 2 * t) * rows + tl * RS_TILE + g;
+      p[0] = acc[tl][0];
+      p[rows] = acc[tl][1];
+      p[8] = acc[tl][2];
+      p[rows + 8] = acc[tl][3];
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < rows * M; i += RS_THREADS) {
+    const int m = i / rows, rl = i - m * rows;  // consecutive threads: consecutive rows
+    const int n = row0 + rl;
+    if (n < N) {
+      float s = 0.f;
+#pragma unroll
+      for (int k2 = 0; k2 < KSW; ++k2) s += red[((size_t)k2 * mpad + m) * rows + rl];
+      a.y[(size_t)m * N + n] = __float2half_rn(fmaf(s, sc[rl], bi[rl]));
+    }
+  }
+  if (tr) {
+    __syncthreads();
+    if (tid == 0) {
+      trace_stamp(tr, 6);
+      trace_stamp(tr, 7);
+    }
+  }
+}
+
 // DDQ_RS_MAX_M overrides the largest token count the kernel takes (0
 // switches it off) for measurements.
 int64_t rs_max_m() {
@@ -366,9 +511,90 @@ int launch_rs_nb(const RsPlan& p, const RsArgs& a, cudaStream_t s) {
   }
 }
 
+// 17..64 tokens (warps over token blocks).  DDQ_RSW_MAX_M overrides the
+// largest token count it takes (0 switches it off) for measurements.
+int64_t rsw_max_m() {
+  static const int64_t v = [] {
+    const char* e = std::getenv("DDQ_RSW_MAX_M");
+    return e ? (int64_t)std::atoll(e) : (int64_t)64;
+  }();
+  return v;
+}
+
+RsPlan rsw_plan(int64_t M, int64_t N, int64_t K, int sms) {
+  RsPlan p{};
+  if (M <= 16 || M > 64 || M > rsw_max_m() || N < 1 || K < 64 || K % 64 != 0 || sms <= 0)
+    return p;
+  if (N > 0x7fffffff - RS_TILE || K > (1 << 20)) return p;
+  const int64_t tiles = (N + RS_TILE - 1) / RS_TILE;
+  const int64_t grid = tiles < sms ? tiles : sms;
+  const int64_t ntl = (tiles + grid - 1) / grid;
+  if (ntl > RS_MAX_TILES) return p;
+  const int64_t nbw = M <= 32 ? 4 : 8;
+  const int64_t w_bytes = ntl * RS_TILE * K;
+  const int64_t red_bytes = (int64_t)(RS_WARPS / nbw) * nbw * 8 * ntl * RS_TILE * 4;
+  if (red_bytes > w_bytes) return p;  // the partials reuse the weight slice
+  const int64_t x_bytes = M * K * 2;
+  if (w_bytes > (int64_t)0xFFFFF || x_bytes > (int64_t)0xFFFFF) return p;
+  const int64_t off_x = w_bytes;
+  const int64_t off_sc = off_x + ((x_bytes + 15) & ~15ll);
+  const int64_t off_bi = off_sc + ntl * RS_TILE * 4;
+  const int64_t off_bar = off_bi + ntl * RS_TILE * 4;
+  const int64_t total = off_bar + 32;
+  if (total > RS_SMEM_MAX) return p;
+  p.ok = true;
+  p.grid = (int)grid;
+  p.nt = (int)ntl;
+  p.nb = (int)nbw;
+  p.smem = (int)total;
+  p.off_x = (int)off_x;
+  p.off_sc = (int)off_sc;
+  p.off_bi = (int)off_bi;
+  p.off_bar = (int)off_bar;
+  return p;
+}
+
+template <int NT, int NBW, bool HW>
+int launch_rsw_t(const RsPlan& p, const RsArgs& a, cudaStream_t s) {
+  static SmemAttrOnce attr;
+  const int ast =
+      ensure_smem_attr(attr, current_device(), w8a16_rsw_kernel<NT, NBW, HW>, RS_SMEM_MAX);
+  if (ast) return ast;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)p.grid);
+  cfg.blockDim = dim3(RS_THREADS);
+  cfg.dynamicSmemBytes = (size_t)p.smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at;
+  at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at.val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = &at;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, w8a16_rsw_kernel<NT, NBW, HW>, a);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return DDQ_ERR_LAUNCH;
+  }
+  return check_launch();
+}
+
+template <int NBW>
+int launch_rsw_nb(const RsPlan& p, const RsArgs& a, cudaStream_t s) {
+  switch (p.nt) {
+    case 1: return launch_rsw_t<1, NBW, true>(p, a, s);
+    case 2: return launch_rsw_t<2, NBW, true>(p, a, s);
+    case 3: return launch_rsw_t<3, NBW, true>(p, a, s);
+    case 4: return launch_rsw_t<4, NBW, true>(p, a, s);
+    case 5: return launch_rsw_t<5, NBW, true>(p, a, s);
+    default: return launch_rsw_t<6, NBW, true>(p, a, s);
+  }
+}
+
 }  // namespace
 
-bool rs_eligible(int64_t M, int64_t N, int64_t K, int sms) { return rs_plan(M, N, K, sms).ok; }
+bool rs_eligible(int64_t M, int64_t N, int64_t K, int sms) {
+  return rs_plan(M, N, K, sms).ok || rsw_plan(M, N, K, sms).ok;
+}
 
 int launch_rs(const __half* x, const uint8_t* wq, const float* scales, const void* bias,
               int bias_dtype, __half* y, int M, int N, int K, unsigned long long timeout_ns,
@@ -376,7 +602,8 @@ int launch_rs(const __half* x, const uint8_t* wq, const float* scales, const voi
   const int sms = device_sm_count(current_device());
   if (sms <= 0) return DDQ_ERR_DEVICE;
   if (!aligned16(x) || !aligned16(wq)) return DDQ_ERR_ALIGNMENT;
-  const RsPlan p = rs_plan(M, N, K, sms);
+  const RsPlan pw = rsw_plan(M, N, K, sms);
+  const RsPlan p = pw.ok ? pw : rs_plan(M, N, K, sms);
   if (!p.ok) return DDQ_ERR_SHAPE;
   RsArgs a{};
   a.x = x;
@@ -395,6 +622,7 @@ int launch_rs(const __half* x, const uint8_t* wq, const float* scales, const voi
   a.off_bar = p.off_bar;
   a.timeout_ns = timeout_ns;
   a.trace = (debug_flags & 2) != 0;
+  if (pw.ok) return p.nb == 4 ? launch_rsw_nb<4>(p, a, s) : launch_rsw_nb<8>(p, a, s);
   if (hw_cvt()) return p.nb == 1 ? launch_rs_nb<1, true>(p, a, s) : launch_rs_nb<2, true>(p, a, s);
   return p.nb == 1 ? launch_rs_nb<1, false>(p, a, s) : launch_rs_nb<2, false>(p, a, s);
 }

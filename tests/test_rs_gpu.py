@@ -1,6 +1,7 @@
-"""GPU parity tests of the resident-slice GEMM kernel (``rs.cu``, 1..16
-tokens, each CTA's weight slice in shared memory, weights on the MMA rows)
-against the CPU oracle: every token count, ragged row counts and K values, every
+"""GPU parity tests of the resident-slice GEMM kernels (``rs.cu``: each CTA's
+weight slice in shared memory, weights on the MMA rows; 1..16 tokens with
+the warps over K blocks, 17..64 with the warps over 8-token blocks) against
+the CPU oracle: every token count, ragged row counts and K values, every
 per-CTA tile count up to the limit (6 sixteen-row tiles at 1..8 tokens, 5 at
 9..16), every e4m3 code,
 the three bias types, a non-finite activation, chains of dependent calls
@@ -95,7 +96,9 @@ def test_tile_limit_per_cta(g, lib):
 def test_dispatch_boundaries(lib):
     assert lib.ddq_w8a16_gemm_kernel_count(3, 9728, 896) == 1     # gate/up, 3 tokens
     assert lib.ddq_w8a16_gemm_kernel_count(16, 9728, 896) == 1    # gate/up, 16 tokens
-    assert lib.ddq_w8a16_gemm_kernel_count(17, 9728, 896) == 2    # more than 16 tokens
+    assert lib.ddq_w8a16_gemm_kernel_count(17, 9728, 896) == 1    # 17..64 tokens: warps over tokens
+    assert lib.ddq_w8a16_gemm_kernel_count(64, 1152, 896) == 1
+    assert lib.ddq_w8a16_gemm_kernel_count(17, 896, 4864) == 2    # x exceeds shared memory
     assert lib.ddq_w8a16_gemm_kernel_count(4, 1152, 912) == 2     # K % 64 != 0
     assert lib.ddq_w8a16_gemm_kernel_count(16, 896, 8192) == 2    # x + slice exceed shared memory
 
@@ -198,3 +201,70 @@ def test_deterministic_bitwise(g, M):
     for _ in range(3):
         assert torch.equal(g.f8_forward(xd, wqd, sd), a)
 
+
+
+@pytest.mark.parametrize("M", [17, 24, 31, 32, 33, 40, 48, 57, 63, 64])
+@pytest.mark.parametrize("N,K", [(1152, 896), (9728, 896), (896, 896), (4864, 896)])
+def test_warps_over_tokens(g, lib, M, N, K):
+    """17..64 tokens: every warp owns an 8-token block (and, up to 32 tokens,
+    half of the K blocks; the two halves are summed in order)."""
+    assert lib.ddq_w8a16_gemm_kernel_count(M, N, K) == 1
+    check(g, M, N, K, seed=400 + M + N)
+
+
+@pytest.mark.parametrize("M,N,K", [(20, 7, 256), (37, 1000, 512), (64, 17, 1024), (50, 2049, 640),
+                                   (33, 896, 2048)])
+def test_warps_over_tokens_ragged(g, lib, M, N, K):
+    assert lib.ddq_w8a16_gemm_kernel_count(M, N, K) == 1
+    check(g, M, N, K, seed=M * 11 + N)
+
+
+def test_warps_over_tokens_chained_and_replayed(g):
+    """Chained calls of 24 and 64 tokens issued back to back equal the same
+    chain with synchronisations, and a replayed graph equals the eager call."""
+    torch.manual_seed(9)
+    shapes = [(896, 896), (1152, 896), (9728, 1152), (896, 9728)]
+    for M in (24, 64):
+        ws = [g.quantize((torch.randn(N, K, device="cuda") * 0.02).half()) for N, K in shapes]
+        x = torch.randn(M, 896, device="cuda").half()
+        ys = [x]
+        for rep in range(2):
+            for wq, s in ws:
+                ys.append(g.f8_forward(ys[-1], wq, s))
+        torch.cuda.synchronize()
+        ref = [x]
+        for rep in range(2):
+            for wq, s in ws:
+                ref.append(g.f8_forward(ref[-1], wq, s))
+                torch.cuda.synchronize()
+        for i, (a, r) in enumerate(zip(ys[1:], ref[1:])):
+            assert torch.equal(a, r), (M, i)
+    M, N, K = 48, 9728, 896
+    x, w, b = gen(M, N, K, seed=71)
+    wq, s = o.quantize(w)
+    xd, wqd, sd, bd = dev(x), dev(wq), dev(s), dev(b)
+    eager = g.f8_forward(xd, wqd, sd, bd)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = g.f8_forward(xd, wqd, sd, bd)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, eager)
+
+
+def test_warps_over_tokens_nonfinite_and_bias(g):
+    M, N, K = 40, 1152, 896
+    x, w, b = gen(M, N, K, seed=73)
+    wq, s = o.quantize(w)
+    for bb in (b.astype(np.float16), b):
+        y = g.f8_forward(dev(x), dev(wq), dev(s), dev(bb))
+        assert o.normwise_rel_err(y.cpu().numpy(), o.f8_forward(x, wq, s, bb)) <= TIGHT
+    ref = g.f8_forward(dev(x), dev(wq), dev(s), dev(b))
+    x2 = x.copy()
+    x2[35, 10] = np.inf
+    y = g.f8_forward(dev(x2), dev(wq), dev(s), dev(b))
+    assert not torch.isfinite(y[35]).all()
+    keep = [i for i in range(M) if i != 35]
+    assert torch.equal(y[keep], ref[keep])
