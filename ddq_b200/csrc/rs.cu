@@ -531,6 +531,12 @@ RsPlan rsw_plan(int64_t M, int64_t N, int64_t K, int sms) {
   const int64_t ntl = (tiles + grid - 1) / grid;
   if (ntl > RS_MAX_TILES) return p;
   const int64_t nbw = M <= 32 ? 4 : 8;
+  // The legacy mma.sync path runs at about one m16n8k16 per 8 SM cycles on
+  // B200 (gate/up 9728 x 896 at 64 tokens: 272K MMAs took 7.7 us on 148 SMs),
+  // so beyond ~768 MMAs per CTA (~3 us) the tcgen05 decode kernel is faster
+  // (measured: q/k/v and o at 32-64 tokens 4.3-5.1 us here against 6.1-7.9;
+  // gate/up at 32 tokens 7.7 against 6.9).
+  if (ntl * (K / 16) * ((M + 7) / 8) > 768) return p;
   const int64_t w_bytes = ntl * RS_TILE * K;
   const int64_t red_bytes = (int64_t)(RS_WARPS / nbw) * nbw * 8 * ntl * RS_TILE * 4;
   if (red_bytes > w_bytes) return p;  // the partials reuse the weight slice

@@ -96,7 +96,7 @@ def test_tile_limit_per_cta(g, lib):
 def test_dispatch_boundaries(lib):
     assert lib.ddq_w8a16_gemm_kernel_count(3, 9728, 896) == 1     # gate/up, 3 tokens
     assert lib.ddq_w8a16_gemm_kernel_count(16, 9728, 896) == 1    # gate/up, 16 tokens
-    assert lib.ddq_w8a16_gemm_kernel_count(17, 9728, 896) == 1    # 17..64 tokens: warps over tokens
+    assert lib.ddq_w8a16_gemm_kernel_count(24, 4864, 896) == 1    # 17..64 tokens: warps over tokens
     assert lib.ddq_w8a16_gemm_kernel_count(64, 1152, 896) == 1
     assert lib.ddq_w8a16_gemm_kernel_count(17, 896, 4864) == 2    # x exceeds shared memory
     assert lib.ddq_w8a16_gemm_kernel_count(4, 1152, 912) == 2     # K % 64 != 0
@@ -204,12 +204,19 @@ def test_deterministic_bitwise(g, M):
 
 
 @pytest.mark.parametrize("M", [17, 24, 31, 32, 33, 40, 48, 57, 63, 64])
-@pytest.mark.parametrize("N,K", [(1152, 896), (9728, 896), (896, 896), (4864, 896)])
+@pytest.mark.parametrize("N,K", [(1152, 896), (896, 896), (2048, 896)])
 def test_warps_over_tokens(g, lib, M, N, K):
     """17..64 tokens: every warp owns an 8-token block (and, up to 32 tokens,
     half of the K blocks; the two halves are summed in order)."""
     assert lib.ddq_w8a16_gemm_kernel_count(M, N, K) == 1
     check(g, M, N, K, seed=400 + M + N)
+
+
+@pytest.mark.parametrize("M,N,K", [(32, 9728, 896), (64, 9728, 896), (64, 4864, 896)])
+def test_big_shapes_above_16_tokens_go_to_the_tensor_core_kernel(g, lib, M, N, K):
+    """More than ~768 legacy MMAs per CTA: the split + tcgen05 decode kernel."""
+    assert lib.ddq_w8a16_gemm_kernel_count(M, N, K) == 2
+    check(g, M, N, K, seed=500 + M)
 
 
 @pytest.mark.parametrize("M,N,K", [(20, 7, 256), (37, 1000, 512), (64, 17, 1024), (50, 2049, 640),
@@ -239,7 +246,7 @@ def test_warps_over_tokens_chained_and_replayed(g):
                 torch.cuda.synchronize()
         for i, (a, r) in enumerate(zip(ys[1:], ref[1:])):
             assert torch.equal(a, r), (M, i)
-    M, N, K = 48, 9728, 896
+    M, N, K = 48, 2048, 896
     x, w, b = gen(M, N, K, seed=71)
     wq, s = o.quantize(w)
     xd, wqd, sd, bd = dev(x), dev(wq), dev(s), dev(b)
