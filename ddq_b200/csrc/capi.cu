@@ -89,18 +89,28 @@ int g_debug_flags = 0;
 // shapes it would take run the decode kernel; the trace flag (bit 1) alone
 // keeps it (it writes phase stamps too).
 bool thin_shape(int64_t M, int64_t N, int64_t K) {
-  if (M > thin_max_m() || (g_debug_flags & ~(2 | 8)) != 0) return false;
+  if (M > thin_max_m() || (g_debug_flags & ~(2 | 8 | 32)) != 0) return false;
   const int dev = current_device();
   return dev >= 0 && thin_eligible(M, N, K, device_sm_count(dev));
 }
 
 // The resident-slice kernel (rs.cu) takes the shapes it fits first, under
 // the same debug-flag rule as the thin kernel; bit 3 sends its shapes to the
-// thin kernel (which then takes the ones it fits).
+// thin kernel (which then takes the ones it fits); bit 5 (skip the
+// tensor-core resident-slice kernel) leaves both of them in place.
 bool rs_shape(int64_t M, int64_t N, int64_t K) {
-  if ((g_debug_flags & ~2) != 0) return false;
+  if ((g_debug_flags & ~(2 | 32)) != 0) return false;
   const int dev = current_device();
   return dev >= 0 && rs_eligible(M, N, K, device_sm_count(dev));
+}
+
+// The tensor-core resident-slice kernel (rt.cu) takes 17..64-token shapes
+// before every other path; any debug bit but the trace (bit 1) and its own
+// timeout hook (bit 4) sends them to the older paths.
+bool rt_shape(int64_t M, int64_t N, int64_t K, bool swiglu) {
+  if ((g_debug_flags & ~(2 | 16)) != 0) return false;
+  const int dev = current_device();
+  return dev >= 0 && rt_eligible(M, N, K, device_sm_count(dev), swiglu);
 }
 
 bool tc_eligible(const void* x, const void* wq, int64_t K) {
@@ -155,6 +165,9 @@ extern "C" int ddq_w8a16_gemm(const void* x, const uint8_t* wq, const float* sca
   const __half* xh = reinterpret_cast<const __half*>(x);
   __half* yh = reinterpret_cast<__half*>(y);
   if (tc_eligible(x, wq, K) && M >= tc_min_m()) {
+    if (rt_shape(M, N, K, false))
+      return launch_rt(xh, wq, scales, bias, bias_dtype, yh, (int)M, (int)N, (int)K, false,
+                       g_wait_timeout_ns, s, g_debug_flags);
     if (rs_shape(M, N, K))
       return launch_rs(xh, wq, scales, bias, bias_dtype, yh, (int)M, (int)N, (int)K,
                        g_wait_timeout_ns, s, g_debug_flags);
@@ -179,7 +192,7 @@ extern "C" int ddq_w8a16_gemm(const void* x, const uint8_t* wq, const float* sca
 extern "C" int ddq_w8a16_gemm_kernel_count(int64_t M, int64_t N, int64_t K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   if (K % 16 != 0 || M < tc_min_m()) return 1;
-  if (rs_shape(M, N, K) || thin_shape(M, N, K)) return 1;
+  if (rt_shape(M, N, K, false) || rs_shape(M, N, K) || thin_shape(M, N, K)) return 1;
   if (M <= kDecodeMaxM || pf_shape(M, N)) return 2;  // split + GEMM / expansion + GEMM
   return 1;
 }
@@ -209,6 +222,9 @@ extern "C" int ddq_w8a16_gemm_swiglu(const void* x, const uint8_t* wq_gu, const 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const __half* xh = reinterpret_cast<const __half*>(x);
   __half* zh = reinterpret_cast<__half*>(z);
+  if (M >= tc_min_m() && rt_shape(M, 2 * I, K, true))
+    return launch_rt(xh, wq_gu, scales_gu, bias, bias_dtype, zh, (int)M, (int)(2 * I), (int)K,
+                     true, g_wait_timeout_ns, s, g_debug_flags);
   if (M <= kDecodeMaxM)
     return launch_dec(xh, wq_gu, scales_gu, bias, bias_dtype, zh, nullptr, 0, (int)M, (int)(2 * I),
                       (int)K, workspace, workspace_bytes, g_wait_timeout_ns, g_debug_flags, s,

@@ -55,6 +55,14 @@ int launch_thin(const __half* x, const uint8_t* wq, const float* scales, const v
 // 1..16 tokens, K % 64 == 0: each CTA's contiguous weight slice resident in
 // shared memory (one bulk copy) before the grid dependency, weights on the
 // mma.sync A operand, dependents triggered at entry (rs.cu).  No workspace.
+// 17..64 tokens on the tcgen05 tensor cores with resident weight slices
+// converted to fp16 before the grid dependency (rt.cu); optional SwiGLU
+// epilogue over the 16-row gate/up interleave.  No workspace.
+bool rt_eligible(int64_t M, int64_t N, int64_t K, int sms, bool swiglu);
+int launch_rt(const __half* x, const uint8_t* wq, const float* scales, const void* bias,
+              int bias_dtype, __half* y, int M, int N, int K, bool swiglu,
+              unsigned long long timeout_ns, cudaStream_t s, int debug_flags);
+
 bool rs_eligible(int64_t M, int64_t N, int64_t K, int sms);
 int launch_rs(const __half* x, const uint8_t* wq, const float* scales, const void* bias,
               int bias_dtype, __half* y, int M, int N, int K, unsigned long long timeout_ns,
