@@ -96,7 +96,7 @@ struct RtArgs {
   int ncols;      // TMEM columns allocated (power of two >= 32)
   int off_b, off_x, off_sb, off_red, off_bar;  // shared-memory offsets (bytes)
   unsigned long long timeout_ns;
-  int debug_flags;  // bit 4: skip the accumulator-ready signal (timeout test)
+  int debug_flags;  // bit 1: phase stamps; bit 4: skip the accumulator-ready signal
 };
 
 __device__ __forceinline__ void rt_bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
@@ -152,8 +152,10 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
   volatile int* drain_flag = abort_flag + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + a.off_bar + RT_NBAR * 8 + 8);
   const uint32_t bstage = (uint32_t)a.rmax * 128u;
+  const bool tr = (a.debug_flags & 2) != 0;  // phase stamps (ddq_read_trace)
 
   if (tid == 0) {
+    trace_stamp(tr, 0);
     ptx::mbar_init(bar(RT_BAR_W), 1);
     for (int i = 0; i < RT_XS; ++i) {
       ptx::mbar_init(bar(RT_BAR_XF + i), 1);
@@ -192,6 +194,7 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
                     bar(RT_BAR_W));
     }
     ptx::prefetch_tmap(&tm_x);
+    trace_stamp(tr, 2);
     ptx::pdl_launch_dependents();
   }
 
@@ -202,6 +205,7 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
     // ---------------------------------------------------- activation producer
     if (lane == 0) {
       ptx::pdl_wait();  // x comes from the previous kernel
+      trace_stamp(tr, 3);
       int issued = 0;
       for (int i = 0; i < nat; ++i) {
         const int s = i % RT_XS;
@@ -232,6 +236,7 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
           break;
         }
         ptx::tc_fence_after();
+        if (i == 0) trace_stamp(tr, 5);  // first atom of x and of fp16 weights ready
         const uint32_t xa = sbase + (uint32_t)(a.off_x + sx * RT_XSTAGE);
         const uint32_t ba = sbase + (uint32_t)a.off_b + (uint32_t)sb * bstage;
 #pragma unroll
@@ -241,6 +246,7 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
         ptx::mma_commit(bar(RT_BAR_BE + sb));
         ptx::mma_commit(bar(RT_BAR_XE + sx));
       }
+      trace_stamp(tr, 4);  // last MMA issued
       if (ok && !(a.debug_flags & 16)) ptx::mma_commit(bar(RT_BAR_ACC));
       // this thread's MMAs are complete before TMEM or shared memory is reused
       ptx::mma_commit(bar(RT_BAR_DRAIN));
@@ -398,6 +404,10 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
 
   ptx::tc_fence_before();
   __syncthreads();
+  if (tid == 0) {
+    trace_stamp(tr, 6);
+    trace_stamp(tr, 7);
+  }
   if (warp == 1) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem_d, (uint32_t)a.ncols);

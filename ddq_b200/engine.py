@@ -140,6 +140,10 @@ class Engine:
         # on their own streams (the step is latency-bound; the slices overlap;
         # measured: 64 = 2 x 32 beats 1 x 64 and 4 x 16, 1 x 32 beats 2 x 16)
         self.decode_chains = 2
+        # decode steps of <= 64 sequences: the norms and the attention emit the
+        # e4m3 planes of the split-plane decode GEMM (True), or fp16 operands
+        # for the resident-slice GEMMs (False)
+        self.decode_planes = True
         self._chain_streams: List[torch.cuda.Stream] = []
         self._graphs = {}
 
@@ -269,7 +273,8 @@ class Engine:
         B, S, H = x.shape
         hd, nh, nkv = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads
         scale = hd ** -0.5
-        if pos is not None and S == 1 and self.linear_kind == "fp8" and B <= 64:
+        if (pos is not None and S == 1 and self.linear_kind == "fp8" and B <= 64
+                and self.decode_planes):
             return self._decode_layer(li, x, delta, cache, b0, cos, sin, pos)
         x, h = self.add_rmsnorm(x, L["in_norm"], delta)
         qkv = self.linear(h, L["qkv"])

@@ -199,7 +199,8 @@ def test_dispatch(lib):
         for M in (17, 32, 64):
             assert lib.ddq_w8a16_gemm_kernel_count(M, N, K) == 1
     assert lib.ddq_w8a16_gemm_kernel_count(32, 1152, 912) == 2     # K % 64 != 0
-    assert lib.ddq_w8a16_gemm_kernel_count(65, 1152, 896) == 2     # prefill kernels
+    assert lib.ddq_w8a16_gemm_kernel_count(65, 1152, 896) == 1     # 64 < M < 128: tc_gemm
+    assert lib.ddq_w8a16_gemm_kernel_count(200, 1152, 896) == 2    # expansion + prefill GEMM
     # lm_head rows: more than 256 rows per CTA, the decode kernel
     assert lib.ddq_w8a16_gemm_kernel_count(32, 151936, 896) == 2
     # debug bit 5 leaves 17..64 tokens to the older kernels
