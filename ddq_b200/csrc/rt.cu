@@ -26,7 +26,9 @@
 //       swizzled K-major layout (cvt.rn.f16x2.e4m3x2: exact);
 //   after it
 //     warp 0      TMA loads of the activation atoms (64 tokens x 64 K, 8 KB)
-//                 through a 3-stage ring
+//                 through a ring of 3..16 stages (as many as the shared-memory
+//                 budget leaves: the fetch from L2 is latency-bound, so its
+//                 rate grows with the atoms in flight)
 //     warp 1      one thread issues 4 MMAs (K = 16) per atom into one
 //                 64 x R fp32 accumulator
 //     warps 2-7   converters, two fp16 weight atoms ahead of the MMAs
@@ -57,7 +59,7 @@ namespace ddq {
 namespace {
 
 constexpr int RT_THREADS = 256;
-constexpr int RT_XS = 3;                // activation ring stages
+constexpr int RT_XS_MAX = 16;           // activation ring stages (the plan picks 3..16)
 constexpr int RT_BS = 2;                // fp16 weight ring stages
 constexpr int RT_XSTAGE = 64 * 128;     // 64 tokens x 64 fp16 (one swizzle atom)
 constexpr int RT_CONV_THREADS = 192;    // warps 2-7
@@ -69,9 +71,9 @@ constexpr int kSmemReservedPerCta = 1024;
 
 // barrier slots (8 bytes each) from off_bar
 constexpr int RT_BAR_W = 0;                      // weight slice landed
-constexpr int RT_BAR_XF = 1;                     // [RT_XS] activation atom landed
-constexpr int RT_BAR_XE = RT_BAR_XF + RT_XS;     // [RT_XS] activation stage free
-constexpr int RT_BAR_BF = RT_BAR_XE + RT_XS;     // [RT_BS] fp16 weight atom ready
+constexpr int RT_BAR_XF = 1;                     // [xs] activation atom landed
+constexpr int RT_BAR_XE = RT_BAR_XF + RT_XS_MAX; // [xs] activation stage free
+constexpr int RT_BAR_BF = RT_BAR_XE + RT_XS_MAX; // [RT_BS] fp16 weight atom ready
 constexpr int RT_BAR_BE = RT_BAR_BF + RT_BS;     // [RT_BS] fp16 weight stage free
 constexpr int RT_BAR_ACC = RT_BAR_BE + RT_BS;    // accumulator complete
 constexpr int RT_BAR_DRAIN = RT_BAR_ACC + 1;     // MMA drain on exit
@@ -92,6 +94,7 @@ struct RtArgs {
   int splits;     // K splits = cluster size (gridDim.x)
   int atoms;      // K / 64
   int rmax;       // most rows any CTA takes
+  int xs;         // activation ring stages
   int vec_y;      // y rows 16-byte aligned: vector stores
   int ncols;      // TMEM columns allocated (power of two >= 32)
   int off_b, off_x, off_sb, off_red, off_bar;  // shared-memory offsets (bytes)
@@ -124,7 +127,7 @@ __device__ __forceinline__ uint32_t rt_pack(float a, float b) {
 //            the MMAs, the fp32 partials [64][rmax] of a K split reuse it
 //            unless off_red places them apart
 //   off_b    RT_BS fp16 weight atoms, rmax rows x 128 B each, swizzled
-//   off_x    RT_XS activation atoms, 64 rows x 128 B each, swizzled (TMA)
+//   off_x    xs activation atoms, 64 rows x 128 B each, swizzled (TMA)
 //   off_sb   scale[rmax], bias[rmax] fp32
 //   off_bar  barriers, abort and drain flags, TMEM address
 template <bool SWIGLU>
@@ -157,7 +160,7 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
   if (tid == 0) {
     trace_stamp(tr, 0);
     ptx::mbar_init(bar(RT_BAR_W), 1);
-    for (int i = 0; i < RT_XS; ++i) {
+    for (int i = 0; i < a.xs; ++i) {
       ptx::mbar_init(bar(RT_BAR_XF + i), 1);
       ptx::mbar_init(bar(RT_BAR_XE + i), 1);
     }
@@ -207,10 +210,11 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
       ptx::pdl_wait();  // x comes from the previous kernel
       trace_stamp(tr, 3);
       int issued = 0;
+      const int xs = a.xs;
       for (int i = 0; i < nat; ++i) {
-        const int s = i % RT_XS;
-        if (i >= RT_XS &&
-            !ptx::mbar_wait(bar(RT_BAR_XE + s), (uint32_t)((i / RT_XS) - 1) & 1u, tmo, abort_flag))
+        const int s = i % xs;
+        if (i >= xs &&
+            !ptx::mbar_wait(bar(RT_BAR_XE + s), (uint32_t)((i / xs) - 1) & 1u, tmo, abort_flag))
           break;
         ptx::mbar_arrive_expect_tx(bar(RT_BAR_XF + s), (uint32_t)RT_XSTAGE);
         ptx::tma_load_2d(sbase + (uint32_t)(a.off_x + s * RT_XSTAGE), &tm_x, k0 + i * 64, 0,
@@ -218,8 +222,8 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
         ++issued;
       }
       // every copy this CTA started has landed before it may exit
-      for (int i = issued > RT_XS ? issued - RT_XS : 0; i < issued; ++i)
-        ptx::mbar_wait(bar(RT_BAR_XF + i % RT_XS), (uint32_t)(i / RT_XS) & 1u, tmo, drain_flag);
+      for (int i = issued > xs ? issued - xs : 0; i < issued; ++i)
+        ptx::mbar_wait(bar(RT_BAR_XF + i % xs), (uint32_t)(i / xs) & 1u, tmo, drain_flag);
       ptx::mbar_wait(bar(RT_BAR_W), 0u, tmo, drain_flag);
     }
     __syncwarp();
@@ -229,9 +233,9 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
       ptx::pdl_wait();  // every wait below depends on the activations
       const uint32_t idesc = ptx::idesc_f16_f32(64, R);
       for (int i = 0; i < nat; ++i) {
-        const int sb = i % RT_BS, sx = i % RT_XS;
+        const int sb = i % RT_BS, sx = i % a.xs;
         if (!ptx::mbar_wait(bar(RT_BAR_BF + sb), (uint32_t)(i / RT_BS) & 1u, tmo, abort_flag) ||
-            !ptx::mbar_wait(bar(RT_BAR_XF + sx), (uint32_t)(i / RT_XS) & 1u, tmo, abort_flag)) {
+            !ptx::mbar_wait(bar(RT_BAR_XF + sx), (uint32_t)(i / a.xs) & 1u, tmo, abort_flag)) {
           ok = false;
           break;
         }
@@ -425,6 +429,7 @@ namespace {
 struct RtPlan {
   bool ok = false;
   int unit_rows = 8, units = 0, row_ctas = 0, splits = 1, atoms = 0, rmax = 0, ncols = 0;
+  int xs = 3;
   int off_b = 0, off_x = 0, off_sb = 0, off_red = 0, off_bar = 0, smem = 0;
 };
 
@@ -447,7 +452,7 @@ int rt_max_m() {
 RtPlan rt_layout(RtPlan p, int64_t kcmax) {
   const int64_t w_bytes = ((int64_t)p.rmax * kcmax + 1023) & ~1023ll;
   const int64_t b_bytes = (int64_t)RT_BS * p.rmax * 128;
-  const int64_t x_bytes = (int64_t)RT_XS * RT_XSTAGE;
+  const int64_t x_bytes = (int64_t)p.xs * RT_XSTAGE;
   const int64_t sb_bytes = (int64_t)2 * p.rmax * 4;
   const int64_t red_bytes = p.splits > 1 ? (int64_t)64 * p.rmax * 4 : 0;
   int64_t off = w_bytes;
@@ -492,13 +497,42 @@ RtPlan rt_plan(int64_t M, int64_t N, int64_t K, int sms, bool swiglu) {
   int64_t g = sms / p.splits;
   if (g < 1) g = 1;
   if (g > units) g = units;
-  for (;; ++g) {
-    if (g > units || g * p.splits > 2 * sms) return p;
-    p.row_ctas = (int)g;
-    p.rmax = (int)((units + g - 1) / g) * p.unit_rows;
-    if (p.rmax > RT_MAX_N) continue;
-    p = rt_layout(p, kcmax);
-    if (p.smem <= RT_SMEM_PAIR) break;
+  // activation ring: the fetch of x from L2 is latency-bound (about 1 us from
+  // issue to landing), so its rate is the atoms in flight: all of the CTA's
+  // K range where the budget allows, at least 3.  Budget: half an SM (the
+  // next GEMM's CTA can be resident meanwhile) where that still leaves
+  // min(atoms, 8) stages, else the whole 227 KB.  DDQ_RT_XS caps the ring,
+  // DDQ_RT_PAIR=0 / 2 force the whole / the half-SM budget (measurements).
+  const int nat_max = (p.atoms + p.splits - 1) / p.splits;
+  int xs_cap = nat_max < RT_XS_MAX ? nat_max : RT_XS_MAX;
+  static const int env_xs = env_int("DDQ_RT_XS", 0);
+  if (env_xs > 0 && env_xs < xs_cap) xs_cap = env_xs;
+  const int xs_min = xs_cap < 3 ? xs_cap : 3;
+  const int xs_pair_min = xs_cap < 8 ? xs_cap : 8;
+  static const int pair_mode = env_int("DDQ_RT_PAIR", 1);
+  const int64_t g0 = g;
+  for (int pass = 0; pass < 2; ++pass) {
+    // pass 0: the half-SM budget with a deep enough ring; pass 1: the rest
+    const bool pair = pass == 0 ? pair_mode != 0 : pair_mode == 2;
+    const int budget = pair ? RT_SMEM_PAIR : RT_SMEM_MAX;
+    const int lo = pass == 0 && pair_mode == 1 ? xs_pair_min : xs_min;
+    // the half-SM budget keeps to one CTA of this kernel per SM
+    const int64_t gmax = pair ? sms / p.splits : 2 * sms / p.splits;
+    bool fits = false;
+    for (g = g0; !fits; ++g) {
+      if (g > units || g > gmax) break;
+      p.row_ctas = (int)g;
+      p.rmax = (int)((units + g - 1) / g) * p.unit_rows;
+      if (p.rmax > RT_MAX_N) continue;
+      for (int xs = xs_cap; xs >= lo && !fits; --xs) {
+        p.xs = xs;
+        p = rt_layout(p, kcmax);
+        fits = p.smem <= budget;
+      }
+      if (fits) break;
+    }
+    if (fits) break;
+    if (pass == 1) return p;
   }
   p.ncols = 32;
   while (p.ncols < p.rmax) p.ncols *= 2;
@@ -607,6 +641,7 @@ int launch_rt(const __half* x, const uint8_t* wq, const float* scales, const voi
   a.splits = p.splits;
   a.atoms = p.atoms;
   a.rmax = p.rmax;
+  a.xs = p.xs;
   a.vec_y = (a.out_n % 8 == 0) && aligned16(y);
   a.ncols = p.ncols;
   a.off_b = p.off_b;
