@@ -86,8 +86,9 @@ int g_debug_flags = 0;
 
 // The thin kernel has no fault-injection hook, so while a test sets the
 // injection flag (bit 0) or asks for the split + decode kernels (bit 2), the
-// shapes it would take run the decode kernel; the trace flag (bit 1) alone
-// keeps it (it writes phase stamps too).
+// shapes it would take run the decode kernel; the trace flag (bit 1), the
+// thin-kernel test flag (bit 3) and the skip-the-tensor-core-resident-slice
+// flag (bit 5) keep it (it writes phase stamps too).
 bool thin_shape(int64_t M, int64_t N, int64_t K) {
   if (M > thin_max_m() || (g_debug_flags & ~(2 | 8 | 32)) != 0) return false;
   const int dev = current_device();

@@ -31,7 +31,9 @@
 //                 rate grows with the atoms in flight)
 //     warp 1      one thread issues 4 MMAs (K = 16) per atom into one
 //                 64 x R fp32 accumulator
-//     warps 2-7   converters, two fp16 weight atoms ahead of the MMAs
+//     warps 2-7   converters, a ring of fp16 weight atoms ahead of the MMAs
+//                 (every atom where shared memory allows: each refill waits
+//                 for an MMA to complete)
 //     warps 4-7   then the epilogue: token m sits in TMEM lane
 //                 (m mod 16) + 32 (m / 16) (the M = 64 data-path layout),
 //                 weight row j in column j; scale, bias, fp16, stores.
@@ -60,7 +62,7 @@ namespace {
 
 constexpr int RT_THREADS = 256;
 constexpr int RT_XS_MAX = 16;           // activation ring stages (the plan picks 3..16)
-constexpr int RT_BS = 2;                // fp16 weight ring stages
+constexpr int RT_BS_MAX = 20;           // fp16 weight ring stages (up to every atom of a CTA)
 constexpr int RT_XSTAGE = 64 * 128;     // 64 tokens x 64 fp16 (one swizzle atom)
 constexpr int RT_CONV_THREADS = 192;    // warps 2-7
 constexpr int RT_SMEM_MAX = 232448;     // 227 KB opt-in limit per CTA
@@ -73,9 +75,9 @@ constexpr int kSmemReservedPerCta = 1024;
 constexpr int RT_BAR_W = 0;                      // weight slice landed
 constexpr int RT_BAR_XF = 1;                     // [xs] activation atom landed
 constexpr int RT_BAR_XE = RT_BAR_XF + RT_XS_MAX; // [xs] activation stage free
-constexpr int RT_BAR_BF = RT_BAR_XE + RT_XS_MAX; // [RT_BS] fp16 weight atom ready
-constexpr int RT_BAR_BE = RT_BAR_BF + RT_BS;     // [RT_BS] fp16 weight stage free
-constexpr int RT_BAR_ACC = RT_BAR_BE + RT_BS;    // accumulator complete
+constexpr int RT_BAR_BF = RT_BAR_XE + RT_XS_MAX; // [bs] fp16 weight atom ready
+constexpr int RT_BAR_BE = RT_BAR_BF + RT_BS_MAX; // [bs] fp16 weight stage free
+constexpr int RT_BAR_ACC = RT_BAR_BE + RT_BS_MAX; // accumulator complete
 constexpr int RT_BAR_DRAIN = RT_BAR_ACC + 1;     // MMA drain on exit
 constexpr int RT_NBAR = RT_BAR_DRAIN + 1;
 constexpr int RT_BAR_BYTES = RT_NBAR * 8 + 16;   // + abort, drain flag, TMEM holder
@@ -95,6 +97,7 @@ struct RtArgs {
   int atoms;      // K / 64
   int rmax;       // most rows any CTA takes
   int xs;         // activation ring stages
+  int bs;         // fp16 weight ring stages
   int vec_y;      // y rows 16-byte aligned: vector stores
   int ncols;      // TMEM columns allocated (power of two >= 32)
   int off_b, off_x, off_sb, off_red, off_bar;  // shared-memory offsets (bytes)
@@ -126,7 +129,7 @@ __device__ __forceinline__ uint32_t rt_pack(float a, float b) {
 //   0        the e4m3 weight slice [rows][kc] (kc = this CTA's K range); after
 //            the MMAs, the fp32 partials [64][rmax] of a K split reuse it
 //            unless off_red places them apart
-//   off_b    RT_BS fp16 weight atoms, rmax rows x 128 B each, swizzled
+//   off_b    bs fp16 weight atoms, rmax rows x 128 B each, swizzled
 //   off_x    xs activation atoms, 64 rows x 128 B each, swizzled (TMA)
 //   off_sb   scale[rmax], bias[rmax] fp32
 //   off_bar  barriers, abort and drain flags, TMEM address
@@ -164,7 +167,7 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
       ptx::mbar_init(bar(RT_BAR_XF + i), 1);
       ptx::mbar_init(bar(RT_BAR_XE + i), 1);
     }
-    for (int i = 0; i < RT_BS; ++i) {
+    for (int i = 0; i < a.bs; ++i) {
       ptx::mbar_init(bar(RT_BAR_BF + i), RT_CONV_THREADS / 32);
       ptx::mbar_init(bar(RT_BAR_BE + i), 1);
     }
@@ -233,8 +236,8 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
       ptx::pdl_wait();  // every wait below depends on the activations
       const uint32_t idesc = ptx::idesc_f16_f32(64, R);
       for (int i = 0; i < nat; ++i) {
-        const int sb = i % RT_BS, sx = i % a.xs;
-        if (!ptx::mbar_wait(bar(RT_BAR_BF + sb), (uint32_t)(i / RT_BS) & 1u, tmo, abort_flag) ||
+        const int sb = i % a.bs, sx = i % a.xs;
+        if (!ptx::mbar_wait(bar(RT_BAR_BF + sb), (uint32_t)(i / a.bs) & 1u, tmo, abort_flag) ||
             !ptx::mbar_wait(bar(RT_BAR_XF + sx), (uint32_t)(i / a.xs) & 1u, tmo, abort_flag)) {
           ok = false;
           break;
@@ -268,10 +271,10 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
     asm volatile("bar.sync 1, %0;" ::"n"(RT_CONV_THREADS) : "memory");
     ok = ptx::mbar_wait(bar(RT_BAR_W), 0u, tmo, abort_flag);
     for (int i = 0; i < nat && ok; ++i) {
-      const int sb = i % RT_BS;
-      if (i == RT_BS) ptx::pdl_wait();  // later stages wait on MMAs, i.e. on x
-      if (i >= RT_BS &&
-          !ptx::mbar_wait(bar(RT_BAR_BE + sb), (uint32_t)((i / RT_BS) - 1) & 1u, tmo, abort_flag)) {
+      const int sb = i % a.bs;
+      if (i == a.bs) ptx::pdl_wait();  // later stages wait on MMAs, i.e. on x
+      if (i >= a.bs &&
+          !ptx::mbar_wait(bar(RT_BAR_BE + sb), (uint32_t)((i / a.bs) - 1) & 1u, tmo, abort_flag)) {
         ok = false;
         break;
       }
@@ -391,16 +394,42 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
     for (int s = 0; s < S; ++s) any_abort |= ptx::ld_dsmem_u32(ptx::mapa_shared(abort_addr, s)) != 0;
     if (!any_abort) {
       ptx::pdl_wait();
-      const int E = a.M * R;
+      // groups of 4 columns; every split's 16 bytes in flight, then the sum
+      // in split order
+      const int R4 = R >> 2, E = a.M * R4;
       const int e0 = (int)((int64_t)split * E / S), e1 = (int)((int64_t)(split + 1) * E / S);
       const uint32_t red0 = sbase + (uint32_t)a.off_red;
       for (int e = e0 + tid; e < e1; e += RT_THREADS) {
-        const int m = e / R, j = e - m * R;
-        if (r0 + j >= a.N) continue;
+        const int m = e / R4, j = (e - m * R4) * 4;
+        const int n = r0 + j;
+        if (n >= a.N) continue;
         const uint32_t off = red0 + (uint32_t)((m * a.rmax + j) * 4);
-        float acc = 0.f;
-        for (int s = 0; s < S; ++s) acc += ptx::ld_dsmem_f32(ptx::mapa_shared(off, s));
-        a.y[(size_t)m * a.N + r0 + j] = __float2half_rn(fmaf(acc, sc[j], bi[j]));
+        float4 v[8];
+#pragma unroll
+        for (int s = 0; s < 8; ++s)
+          if (s < S) v[s] = ptx::ld_dsmem_f4(ptx::mapa_shared(off, (uint32_t)s));
+        float4 acc = v[0];
+#pragma unroll
+        for (int s = 1; s < 8; ++s) {
+          if (s < S) {
+            acc.x += v[s].x;
+            acc.y += v[s].y;
+            acc.z += v[s].z;
+            acc.w += v[s].w;
+          }
+        }
+        const uint32_t lo = rt_pack(fmaf(acc.x, sc[j], bi[j]), fmaf(acc.y, sc[j + 1], bi[j + 1]));
+        const uint32_t hi =
+            rt_pack(fmaf(acc.z, sc[j + 2], bi[j + 2]), fmaf(acc.w, sc[j + 3], bi[j + 3]));
+        __half* yr = a.y + (size_t)m * a.N + n;
+        if (a.vec_y && n + 4 <= a.N) {
+          *reinterpret_cast<uint2*>(yr) = make_uint2(lo, hi);
+        } else {
+          const uint32_t w[2] = {lo, hi};
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            if (n + i < a.N) yr[i] = __ushort_as_half((unsigned short)(w[i >> 1] >> (16 * (i & 1))));
+        }
       }
     }
     ptx::cluster_sync();  // no CTA leaves while another still reads its partials
@@ -429,7 +458,7 @@ namespace {
 struct RtPlan {
   bool ok = false;
   int unit_rows = 8, units = 0, row_ctas = 0, splits = 1, atoms = 0, rmax = 0, ncols = 0;
-  int xs = 3;
+  int xs = 3, bs = 2;
   int off_b = 0, off_x = 0, off_sb = 0, off_red = 0, off_bar = 0, smem = 0;
 };
 
@@ -451,7 +480,7 @@ int rt_max_m() {
 
 RtPlan rt_layout(RtPlan p, int64_t kcmax) {
   const int64_t w_bytes = ((int64_t)p.rmax * kcmax + 1023) & ~1023ll;
-  const int64_t b_bytes = (int64_t)RT_BS * p.rmax * 128;
+  const int64_t b_bytes = (int64_t)p.bs * p.rmax * 128;
   const int64_t x_bytes = (int64_t)p.xs * RT_XSTAGE;
   const int64_t sb_bytes = (int64_t)2 * p.rmax * 4;
   const int64_t red_bytes = p.splits > 1 ? (int64_t)64 * p.rmax * 4 : 0;
@@ -497,43 +526,40 @@ RtPlan rt_plan(int64_t M, int64_t N, int64_t K, int sms, bool swiglu) {
   int64_t g = sms / p.splits;
   if (g < 1) g = 1;
   if (g > units) g = units;
-  // activation ring: the fetch of x from L2 is latency-bound (about 1 us from
-  // issue to landing), so its rate is the atoms in flight: all of the CTA's
-  // K range where the budget allows, at least 3.  Budget: half an SM (the
-  // next GEMM's CTA can be resident meanwhile) where that still leaves
-  // min(atoms, 8) stages, else the whole 227 KB.  DDQ_RT_XS caps the ring,
-  // DDQ_RT_PAIR=0 / 2 force the whole / the half-SM budget (measurements).
+  // Rings.  Refilling a stage of either ring waits for an MMA to complete;
+  // an activation stage then waits for an L2 fetch as well (about 1 us from
+  // issue to landing), a weight stage only for its conversion.  So the
+  // activation ring gets its stages first - every atom of the CTA's K range
+  // where the budget allows, at most 16 - and the weight ring what is left,
+  // at most every atom; at least min(atoms, 8) and min(atoms, 4) stages.
+  // Budget: half an SM where both rings fit in it (the next GEMM's CTA can
+  // then be resident and fetch its slice meanwhile), else the whole 227 KB;
+  // one CTA of this kernel per SM and split either way.  DDQ_RT_XS caps the
+  // activation ring; DDQ_RT_PAIR=0 / 2 force the whole / the half-SM budget.
+  if (g > sms / p.splits || (int64_t)((units + g - 1) / g) * p.unit_rows > RT_MAX_N) return p;
+  p.row_ctas = (int)g;
+  p.rmax = (int)((units + g - 1) / g) * p.unit_rows;
   const int nat_max = (p.atoms + p.splits - 1) / p.splits;
   int xs_cap = nat_max < RT_XS_MAX ? nat_max : RT_XS_MAX;
   static const int env_xs = env_int("DDQ_RT_XS", 0);
   if (env_xs > 0 && env_xs < xs_cap) xs_cap = env_xs;
-  const int xs_min = xs_cap < 3 ? xs_cap : 3;
-  const int xs_pair_min = xs_cap < 8 ? xs_cap : 8;
+  const int bs_cap = nat_max < RT_BS_MAX ? nat_max : RT_BS_MAX;
+  const int xs_lo = xs_cap < 8 ? xs_cap : 8, bs_lo = bs_cap < 4 ? bs_cap : 4;
   static const int pair_mode = env_int("DDQ_RT_PAIR", 1);
-  const int64_t g0 = g;
-  for (int pass = 0; pass < 2; ++pass) {
-    // pass 0: the half-SM budget with a deep enough ring; pass 1: the rest
+  bool fits = false;
+  for (int pass = 0; pass < 2 && !fits; ++pass) {
     const bool pair = pass == 0 ? pair_mode != 0 : pair_mode == 2;
     const int budget = pair ? RT_SMEM_PAIR : RT_SMEM_MAX;
-    const int lo = pass == 0 && pair_mode == 1 ? xs_pair_min : xs_min;
-    // the half-SM budget keeps to one CTA of this kernel per SM
-    const int64_t gmax = pair ? sms / p.splits : 2 * sms / p.splits;
-    bool fits = false;
-    for (g = g0; !fits; ++g) {
-      if (g > units || g > gmax) break;
-      p.row_ctas = (int)g;
-      p.rmax = (int)((units + g - 1) / g) * p.unit_rows;
-      if (p.rmax > RT_MAX_N) continue;
-      for (int xs = xs_cap; xs >= lo && !fits; --xs) {
+    for (int xs = xs_cap; xs >= xs_lo && !fits; --xs) {
+      for (int bs = bs_cap; bs >= bs_lo && !fits; --bs) {
         p.xs = xs;
+        p.bs = bs;
         p = rt_layout(p, kcmax);
         fits = p.smem <= budget;
       }
-      if (fits) break;
     }
-    if (fits) break;
-    if (pass == 1) return p;
   }
+  if (!fits) return p;
   p.ncols = 32;
   while (p.ncols < p.rmax) p.ncols *= 2;
   // CTAs of this kernel that share an SM must never ask for more than the
@@ -642,6 +668,7 @@ int launch_rt(const __half* x, const uint8_t* wq, const float* scales, const voi
   a.atoms = p.atoms;
   a.rmax = p.rmax;
   a.xs = p.xs;
+  a.bs = p.bs;
   a.vec_y = (a.out_n % 8 == 0) && aligned16(y);
   a.ncols = p.ncols;
   a.off_b = p.off_b;

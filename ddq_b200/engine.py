@@ -34,6 +34,9 @@ versions of RMSNorm, RoPE and SwiGLU below serve the oracle engine.
 semantics in fp32 (dequantised weight, fp32 matmul, fp16 output) and the
 lm_head for fp32 logits rounded to fp16 + lowest-index argmax: the same graph
 with the reference arithmetic, used by the tests to judge the greedy tokens.
+``linear="oracle64"`` is the same with fp64 accumulation (one rounding to
+fp16): another valid summation of the reference semantics, which measures how
+far fp32 summation order alone moves the fp16 logits.
 """
 from __future__ import annotations
 
@@ -219,9 +222,10 @@ class Engine:
         """The projection dispatch point (reference ``_linear``, ``engine.py:85-86``)."""
         if self.linear_kind == "fp8":
             return gemm_fp8.f8_forward(x, p.wq, p.scales, p.bias)
-        y = x.reshape(-1, x.shape[-1]).float() @ p.dequantized().T
+        acc = torch.float64 if self.linear_kind == "oracle64" else torch.float32
+        y = x.reshape(-1, x.shape[-1]).to(acc) @ p.dequantized().to(acc).T
         if p.bias is not None:
-            y = y + p.bias
+            y = y + p.bias.to(acc)
         return y.half().reshape(*x.shape[:-1], -1)
 
     def rmsnorm(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
@@ -402,13 +406,13 @@ class Engine:
         if self.linear_kind == "fp8":
             ids, _ = lmh.lm_head_argmax(h, self.lm_head.wq, self.lm_head.scales)
             return ids
-        logits = (h.float() @ self.lm_head.dequantized().T).half().float()
-        return logits.argmax(dim=-1)
+        return self.logits(h).float().argmax(dim=-1)
 
     def logits(self, h: torch.Tensor) -> torch.Tensor:
         if self.linear_kind == "fp8":
             return gemm_fp8.f8_forward(h, self.lm_head.wq, self.lm_head.scales)
-        return (h.float() @ self.lm_head.dequantized().T).half()
+        acc = torch.float64 if self.linear_kind == "oracle64" else torch.float32
+        return (h.to(acc) @ self.lm_head.dequantized().to(acc).T).half()
 
     # ------------------------------------------------------------------ reference-style API
     def forward(self, input_ids: torch.Tensor, cache: Optional[KVCache] = None, start: int = 0):

@@ -24,14 +24,16 @@ from __future__ import annotations
 
 from typing import Dict, List, Optional
 
-import numpy as np
 import torch
 
 
 def _fp16_ulp(v: torch.Tensor) -> torch.Tensor:
-    """Spacing of fp16 at |v| (v already fp16-representable), as fp32."""
-    a = v.abs().cpu().numpy().astype(np.float16)
-    return torch.from_numpy(np.spacing(a).astype(np.float32)).to(v.device)
+    """Spacing of fp16 at |v| (v fp16-representable, finite), as fp32, on v's
+    device: 2^(e - 10) for |v| in [2^e, 2^(e+1)), e >= -14; 2^-24 below."""
+    a = v.float().abs()
+    _, ex = torch.frexp(a)                      # |v| = m * 2^ex, m in [0.5, 1)
+    e = torch.where(a > 0, torch.clamp(ex - 1, min=-14), torch.full_like(ex, -14))
+    return torch.ldexp(torch.ones_like(v, dtype=torch.float32), e - 10)
 
 
 @torch.no_grad()
@@ -48,7 +50,7 @@ def oracle_logits_at(oracle, prompts: torch.Tensor, tokens: torch.Tensor,
         part = seq[b0:b0 + chunk]
         cache = oracle.new_cache(part.shape[0], part.shape[1])
         h = oracle.hidden(part, cache, 0, 0)[:, S - 1:S - 1 + T, :]
-        lg = (h.reshape(-1, h.shape[-1]).float() @ oracle.lm_head.dequantized().T).half()
+        lg = oracle.logits(h.reshape(-1, h.shape[-1]))
         outs.append(lg.float().reshape(part.shape[0], T, -1))
         del cache, h, lg
     return torch.cat(outs)
@@ -110,3 +112,44 @@ def free_run_report(oracle, prompts: torch.Tensor, tokens: torch.Tensor,
         first.append(int((~same[b]).nonzero()[0]))
     return {"sequences": int(tokens.shape[0]), "identical": int(identical.sum()),
             "first_difference_step": sorted(first)}
+
+
+@torch.no_grad()
+def oracle_noise_report(oracle, other, prompts: torch.Tensor, tokens: torch.Tensor) -> Dict:
+    """Two valid summations of the reference semantics (``oracle``: fp32
+    accumulation; ``other``: e.g. fp64) on the same teacher-forced contexts:
+    how often their greedy picks differ and by what margin (in fp16 ulps of
+    ``oracle``'s logits, as ``teacher_forced_report`` measures this engine),
+    and how far their fp16 logits lie apart (max and 99.99th percentile over
+    every vocabulary entry of every generated position, in ulps).  The
+    margins of the picks where two equally valid summations disagree are the
+    floor below which a differing pick is an fp16-level tie."""
+    B, T = tokens.shape
+    hist = {"0": 0, "1": 0, "2": 0, ">2": 0}
+    differ = 0
+    worst = 0.0
+    dmax = 0.0
+    qs = []
+    chunk = 8
+    for b0 in range(0, B, chunk):
+        la = oracle_logits_at(oracle, prompts[b0:b0 + chunk], tokens[b0:b0 + chunk], chunk)
+        lb = oracle_logits_at(other, prompts[b0:b0 + chunk], tokens[b0:b0 + chunk], chunk)
+        ulp = _fp16_ulp(la.reshape(-1)).reshape(la.shape)
+        d = ((lb - la).abs() / ulp)
+        dmax = max(dmax, float(d.max()))
+        qs.append(float(torch.quantile(d.reshape(-1)[::97].float(), 0.9999)))
+        del d, ulp
+        pa = la.argmax(dim=-1)
+        pb = lb.argmax(dim=-1)
+        best = la.max(dim=-1).values
+        chosen = la.gather(-1, pb[..., None]).squeeze(-1)
+        margin = (best - chosen) / _fp16_ulp(best)
+        for b, t in (pa != pb).nonzero().tolist():
+            m = float(margin[b, t])
+            differ += 1
+            worst = max(worst, m)
+            hist["0" if m == 0 else "1" if m <= 1 else "2" if m <= 2 else ">2"] += 1
+        del la, lb
+    return {"steps": B * T, "differ": differ, "differ_by_margin_ulps": hist,
+            "max_margin_ulps": round(worst, 3), "max_logit_diff_ulps": round(dmax, 3),
+            "p9999_logit_diff_ulps": round(max(qs), 3)}
