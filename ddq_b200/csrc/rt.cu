@@ -224,6 +224,7 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
                          bar(RT_BAR_XF + s));
         ++issued;
       }
+      trace_stamp(tr, 11);  // last activation load issued
       // every copy this CTA started has landed before it may exit
       for (int i = issued > xs ? issued - xs : 0; i < issued; ++i)
         ptx::mbar_wait(bar(RT_BAR_XF + i % xs), (uint32_t)(i / xs) & 1u, tmo, drain_flag);
@@ -244,6 +245,8 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
         }
         ptx::tc_fence_after();
         if (i == 0) trace_stamp(tr, 5);  // first atom of x and of fp16 weights ready
+        if (i == nat / 2) trace_stamp(tr, 8);
+        if (i == nat - 1) trace_stamp(tr, 9);
         const uint32_t xa = sbase + (uint32_t)(a.off_x + sx * RT_XSTAGE);
         const uint32_t ba = sbase + (uint32_t)a.off_b + (uint32_t)sb * bstage;
 #pragma unroll
@@ -301,12 +304,14 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar(RT_BAR_BF + sb));
     }
+    if (tid == 64) trace_stamp(tr, 10);  // this converter warp's last atom
 
     if (warp >= 4) {
       // ---------------------------------------------------- epilogue
       const int q = warp & 3;  // TMEM lane quarter this warp may read
       const int m = 16 * q + lane;
       const bool got = ok && ptx::mbar_wait(bar(RT_BAR_ACC), 0u, tmo, abort_flag);
+      if (tid == 128) trace_stamp(tr, 12);  // accumulator complete
       ptx::tc_fence_after();
       ptx::pdl_wait();  // y may be a buffer the previous kernel reads
       if (got) {

@@ -207,7 +207,11 @@ def main(argv=None):
             t0 = used[:, 0].min()
             rel = (used - t0) / 1e3
             names = ["entry", "setup", "w_issued", "w_landed", "mma_done", "acc_ready",
-                     "epi_done", "exit"]
+                     "epi_done", "exit",
+                     # kernels with more phases (rt.cu): half-way and last
+                     # activation atom ready, converters done, last activation
+                     # load issued, accumulator complete
+                     "x_half", "x_last", "conv_done", "x_issued_last", "acc_full"]
             trace = {"ctas": int(len(used)), "span_us": round(float(rel[:, 7].max()), 3)}
             for j, nm in enumerate(names):
                 col = rel[:, j][used[:, j] > 0]
