@@ -582,15 +582,19 @@ def generation_parity(eng, prompts, toks):
          "lm_head": eng.lm_head}
     oracle = Engine(eng.cfg, w, eng.device, linear="oracle")
     tf = parity.teacher_forced_report(oracle, prompts, toks, max_listed=32)
+    # the reference semantics' own floor: fp64 accumulation on the same contexts
+    floor = parity.oracle_noise_report(oracle, Engine(eng.cfg, w, eng.device, linear="oracle64"),
+                                       prompts, toks)
     free = parity.free_run_report(oracle, prompts, toks)
     for layer in eng.layers:    # drop the oracle's fp32 weight copies
         for p in layer.values():
             if hasattr(p, "_wdeq"):
                 p._wdeq = None
     eng.lm_head._wdeq = None
-    return {"teacher_forced": tf, "free_run": free,
+    return {"teacher_forced": tf, "reference_floor": floor, "free_run": free,
             "judge": "same graph with fp32 projections of the dequantised weights, fp16 logits, "
-                     "lowest-index argmax; margin = oracle fp16 logit of its pick minus of ours"}
+                     "lowest-index argmax; margin = oracle fp16 logit of its pick minus of ours; "
+                     "reference_floor = the same oracle with fp64 accumulation against it"}
 
 
 def launches_per_step(calls):

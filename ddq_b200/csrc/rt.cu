@@ -150,6 +150,12 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
   const int valid = min(R, a.N - r0);
   const int at0 = split * a.atoms / S, at1 = (split + 1) * a.atoms / S;
   const int nat = at1 - at0, kc = nat * 64, k0 = at0 * 64;
+  // Step i takes atom (i + rot) mod nat of the CTA's K range: every CTA reads
+  // the same activations, and CTAs walking them in lockstep would all ask
+  // the same few L2 lines at once (measured: atoms landing ~0.5 us apart);
+  // rotated starts spread the requests over the whole activation block.  The
+  // order is fixed per CTA, so results stay bitwise reproducible.
+  const int rot = rc % nat;
   const int K = a.K;
   const uint64_t tmo = a.timeout_ns;
   const uint32_t bar0 = sbase + (uint32_t)a.off_bar;
@@ -220,7 +226,8 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
             !ptx::mbar_wait(bar(RT_BAR_XE + s), (uint32_t)((i / xs) - 1) & 1u, tmo, abort_flag))
           break;
         ptx::mbar_arrive_expect_tx(bar(RT_BAR_XF + s), (uint32_t)RT_XSTAGE);
-        ptx::tma_load_2d(sbase + (uint32_t)(a.off_x + s * RT_XSTAGE), &tm_x, k0 + i * 64, 0,
+        const int at = i + rot < nat ? i + rot : i + rot - nat;
+        ptx::tma_load_2d(sbase + (uint32_t)(a.off_x + s * RT_XSTAGE), &tm_x, k0 + at * 64, 0,
                          bar(RT_BAR_XF + s));
         ++issued;
       }
@@ -286,7 +293,7 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
       // 128 bytes (chunk c lands at c ^ (row mod 8)).  Rows >= valid convert
       // whatever the slice buffer holds: they only reach accumulator
       // columns that are never stored.
-      const uint8_t* src = smem + i * 64;
+      const uint8_t* src = smem + (i + rot < nat ? i + rot : i + rot - nat) * 64;
       uint8_t* dst = smem + a.off_b + sb * bstage;
       for (int u = ct; u < R * 4; u += RT_CONV_THREADS) {
         const int r = u >> 2, c = u & 3, sw = r & 7;
