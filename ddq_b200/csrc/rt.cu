@@ -64,7 +64,8 @@ constexpr int RT_THREADS = 256;
 constexpr int RT_XS_MAX = 16;           // activation ring stages (the plan picks 3..16)
 constexpr int RT_BS_MAX = 20;           // fp16 weight ring stages (up to every atom of a CTA)
 constexpr int RT_XSTAGE = 64 * 128;     // 64 tokens x 64 fp16 (one swizzle atom)
-constexpr int RT_CONV_THREADS = 192;    // warps 2-7
+constexpr int RT_ISSUERS = 3;           // MMA issuers: lane 0 of warps 1-3
+constexpr int RT_CONV_THREADS = 128;    // warps 4-7
 constexpr int RT_SMEM_MAX = 232448;     // 227 KB opt-in limit per CTA
 constexpr int RT_SMEM_PAIR = 113 * 1024;  // two CTAs per SM
 constexpr int RT_MAX_N = 256;           // MMA N limit (weight rows per CTA)
@@ -78,8 +79,8 @@ constexpr int RT_BAR_XE = RT_BAR_XF + RT_XS_MAX; // [xs] activation stage free
 constexpr int RT_BAR_BF = RT_BAR_XE + RT_XS_MAX; // [bs] fp16 weight atom ready
 constexpr int RT_BAR_BE = RT_BAR_BF + RT_BS_MAX; // [bs] fp16 weight stage free
 constexpr int RT_BAR_ACC = RT_BAR_BE + RT_BS_MAX; // accumulator complete
-constexpr int RT_BAR_DRAIN = RT_BAR_ACC + 1;     // MMA drain on exit
-constexpr int RT_NBAR = RT_BAR_DRAIN + 1;
+constexpr int RT_BAR_DRAIN = RT_BAR_ACC + 1;     // [RT_ISSUERS] MMA drain on exit
+constexpr int RT_NBAR = RT_BAR_DRAIN + RT_ISSUERS;
 constexpr int RT_BAR_BYTES = RT_NBAR * 8 + 16;   // + abort, drain flag, TMEM holder
 
 struct RtArgs {
@@ -100,6 +101,7 @@ struct RtArgs {
   int bs;         // fp16 weight ring stages
   int vec_y;      // y rows 16-byte aligned: vector stores
   int ncols;      // TMEM columns allocated (power of two >= 32)
+  int acc_stride; // TMEM columns between the issuers' accumulators
   int off_b, off_x, off_sb, off_red, off_bar;  // shared-memory offsets (bytes)
   unsigned long long timeout_ns;
   int debug_flags;  // bit 1: phase stamps; bit 4: skip the accumulator-ready signal
@@ -177,8 +179,8 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
       ptx::mbar_init(bar(RT_BAR_BF + i), RT_CONV_THREADS / 32);
       ptx::mbar_init(bar(RT_BAR_BE + i), 1);
     }
-    ptx::mbar_init(bar(RT_BAR_ACC), 1);
-    ptx::mbar_init(bar(RT_BAR_DRAIN), 1);
+    ptx::mbar_init(bar(RT_BAR_ACC), (uint32_t)(nat < RT_ISSUERS ? nat : RT_ISSUERS));
+    for (int w = 0; w < RT_ISSUERS; ++w) ptx::mbar_init(bar(RT_BAR_DRAIN + w), 1);
     *abort_flag = 0;
     *drain_flag = 0;
     ptx::fence_mbar_init();
@@ -238,12 +240,18 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
       ptx::mbar_wait(bar(RT_BAR_W), 0u, tmo, drain_flag);
     }
     __syncwarp();
-  } else if (warp == 1) {
-    // ---------------------------------------------------- MMA issuer
-    if (lane == 0) {
+  } else if (warp <= RT_ISSUERS) {
+    // ---------------------------------------------------- MMA issuers
+    // Issuing a tcgen05.mma costs its thread ~30 ns at these tile sizes
+    // (measured), well above the tensor pipe's time for it, so three threads
+    // issue: w takes atoms i = w, w + 3, ... into its own accumulator
+    // (columns w * acc_stride), summed in order w = 0, 1, 2 by the epilogue.
+    const int w = warp - 1;
+    if (lane == 0 && w < nat) {
       ptx::pdl_wait();  // every wait below depends on the activations
       const uint32_t idesc = ptx::idesc_f16_f32(64, R);
-      for (int i = 0; i < nat; ++i) {
+      const uint32_t acc = tmem_d + (uint32_t)(w * a.acc_stride);
+      for (int i = w; i < nat; i += RT_ISSUERS) {
         const int sb = i % a.bs, sx = i % a.xs;
         if (!ptx::mbar_wait(bar(RT_BAR_BF + sb), (uint32_t)(i / a.bs) & 1u, tmo, abort_flag) ||
             !ptx::mbar_wait(bar(RT_BAR_XF + sx), (uint32_t)(i / a.xs) & 1u, tmo, abort_flag)) {
@@ -258,21 +266,21 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
         const uint32_t ba = sbase + (uint32_t)a.off_b + (uint32_t)sb * bstage;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          ptx::mma_f16_ss(tmem_d, ptx::smem_desc_sw128(xa + 32u * kk),
-                          ptx::smem_desc_sw128(ba + 32u * kk), idesc, (i | kk) != 0 ? 1u : 0u);
+          ptx::mma_f16_ss(acc, ptx::smem_desc_sw128(xa + 32u * kk),
+                          ptx::smem_desc_sw128(ba + 32u * kk), idesc, (i != w || kk) ? 1u : 0u);
         ptx::mma_commit(bar(RT_BAR_BE + sb));
         ptx::mma_commit(bar(RT_BAR_XE + sx));
       }
-      trace_stamp(tr, 4);  // last MMA issued
+      if (w == 0) trace_stamp(tr, 4);  // issuer 0's last MMA issued
       if (ok && !(a.debug_flags & 16)) ptx::mma_commit(bar(RT_BAR_ACC));
       // this thread's MMAs are complete before TMEM or shared memory is reused
-      ptx::mma_commit(bar(RT_BAR_DRAIN));
-      ptx::mbar_wait(bar(RT_BAR_DRAIN), 0u, tmo, drain_flag);
+      ptx::mma_commit(bar(RT_BAR_DRAIN + w));
+      ptx::mbar_wait(bar(RT_BAR_DRAIN + w), 0u, tmo, drain_flag);
     }
     __syncwarp();
   } else {
     // ---------------------------------------------------- converters
-    const int ct = tid - 64;
+    const int ct = tid - 32 * (RT_ISSUERS + 1);
     for (int r = ct; r < R; r += RT_CONV_THREADS) {
       const int n = r0 + r;
       sc[r] = n < a.N ? a.scales[n] : 0.f;
@@ -311,14 +319,15 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar(RT_BAR_BF + sb));
     }
-    if (tid == 64) trace_stamp(tr, 10);  // this converter warp's last atom
+    if (ct == 0) trace_stamp(tr, 10);  // this converter warp's last atom
 
     if (warp >= 4) {
       // ---------------------------------------------------- epilogue
       const int q = warp & 3;  // TMEM lane quarter this warp may read
       const int m = 16 * q + lane;
+      const int ni = nat < RT_ISSUERS ? nat : RT_ISSUERS;  // accumulators written
       const bool got = ok && ptx::mbar_wait(bar(RT_BAR_ACC), 0u, tmo, abort_flag);
-      if (tid == 128) trace_stamp(tr, 12);  // accumulator complete
+      if (ct == 0) trace_stamp(tr, 12);  // accumulators complete
       ptx::tc_fence_after();
       ptx::pdl_wait();  // y may be a buffer the previous kernel reads
       if (got) {
@@ -331,6 +340,18 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
           for (int j8 = 0; j8 < 4; ++j8)
             if (c0 + 8 * j8 < R) ptx::tmem_ld_32x32b_x8(tl + (uint32_t)(c0 + 8 * j8), v + 8 * j8);
           ptx::tmem_ld_wait();
+          // the other issuers' accumulators, added in issuer order
+          for (int w = 1; w < ni; ++w) {
+            uint32_t u[32];
+#pragma unroll
+            for (int j8 = 0; j8 < 4; ++j8)
+              if (c0 + 8 * j8 < R)
+                ptx::tmem_ld_32x32b_x8(tl + (uint32_t)(w * a.acc_stride + c0 + 8 * j8), u + 8 * j8);
+            ptx::tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(u[j]));
+          }
           if (lane < 16 && S > 1) {
             // fp32 partial of token row m (all 64; rows >= M hold zeros)
 #pragma unroll
@@ -470,7 +491,7 @@ namespace {
 struct RtPlan {
   bool ok = false;
   int unit_rows = 8, units = 0, row_ctas = 0, splits = 1, atoms = 0, rmax = 0, ncols = 0;
-  int xs = 3, bs = 2;
+  int xs = 3, bs = 2, acc_stride = 32;
   int off_b = 0, off_x = 0, off_sb = 0, off_red = 0, off_bar = 0, smem = 0;
 };
 
@@ -572,8 +593,11 @@ RtPlan rt_plan(int64_t M, int64_t N, int64_t K, int sms, bool swiglu) {
     }
   }
   if (!fits) return p;
+  // one accumulator per MMA issuer, 32-column aligned
+  p.acc_stride = (p.rmax + 31) & ~31;
+  const int nacc = nat_max < RT_ISSUERS ? nat_max : RT_ISSUERS;
   p.ncols = 32;
-  while (p.ncols < p.rmax) p.ncols *= 2;
+  while (p.ncols < nacc * p.acc_stride) p.ncols *= 2;
   // CTAs of this kernel that share an SM must never ask for more than the
   // SM's 512 TMEM columns between them (a CTA of a cluster that waited in
   // tcgen05.alloc for its neighbour could hold up the cluster barrier): at
@@ -683,6 +707,7 @@ int launch_rt(const __half* x, const uint8_t* wq, const float* scales, const voi
   a.bs = p.bs;
   a.vec_y = (a.out_n % 8 == 0) && aligned16(y);
   a.ncols = p.ncols;
+  a.acc_stride = p.acc_stride;
   a.off_b = p.off_b;
   a.off_x = p.off_x;
   a.off_sb = p.off_sb;
