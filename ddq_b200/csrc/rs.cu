@@ -17,10 +17,8 @@
 //   * the CTA signals griddepcontrol.launch_dependents at entry, so the next
 //     kernel's CTAs are scheduled as soon as every CTA of this one runs and,
 //     where shared memory leaves room, stream their own slices meanwhile;
-//   * after the dependency: all of x (M x K fp16, contiguous) in 4 KB bulk
-//     copies from a CTA-dependent start (CTAs copying the same bytes in
-//     lockstep queue on the same L2 lines), then warp w runs the 64-wide K
-//     blocks kb = w, w + 8, ...
+//   * after the dependency: one bulk copy of all of x (M x K fp16,
+//     contiguous), then warp w runs the 64-wide K blocks kb = w, w + 8, ...
 //     of all its tiles (tile by tile; ordering the MMAs so that consecutive
 //     ones never share an accumulator measured slower), then a
 //     warp-ordered sum of the 8 partials per output, scale, bias, fp16.
@@ -77,21 +75,6 @@ __device__ __forceinline__ void rs_bulk_g2s(uint32_t dst, const void* src, uint3
       "l"(src), "r"(bytes), "r"(bar)
       : "memory");
 }
-// x (M x K fp16, contiguous) in 4 KB pieces from a piece that depends on the
-// CTA: every CTA reads the same activations right after the dependency, and a
-// single copy per CTA would have all of them ask the same L2 lines at once.
-__device__ __forceinline__ void rs_copy_x(uint32_t dst, const void* src, uint32_t bytes,
-                                          uint32_t bar, int cta) {
-  constexpr uint32_t P = 4096;
-  const uint32_t np = (bytes + P - 1) / P;
-  const uint32_t r = (uint32_t)cta % np;
-  for (uint32_t q = 0; q < np; ++q) {
-    const uint32_t j = q + r < np ? q + r : q + r - np;
-    const uint32_t off = j * P;
-    rs_bulk_g2s(dst + off, static_cast<const uint8_t*>(src) + off, min(P, bytes - off), bar);
-  }
-}
-
 __device__ __forceinline__ uint4 rs_lds128(uint32_t a) {
   uint4 v;
   asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
@@ -174,7 +157,7 @@ __global__ void __launch_bounds__(RS_THREADS, 2) w8a16_rs_kernel(const RsArgs a)
   if (tid == 0) {
     trace_stamp(tr, 3);
     ptx::mbar_arrive_expect_tx(bar_x, (uint32_t)(M * K * 2));
-    rs_copy_x(sbase + (uint32_t)a.off_x, a.x, (uint32_t)(M * K * 2), bar_x, b);
+    rs_bulk_g2s(sbase + (uint32_t)a.off_x, a.x, (uint32_t)(M * K * 2), bar_x);
   }
   // bounded waits: on a timeout the CTA records DDQ_ERR_TIMEOUT, waits once
   // more (bounded) for its copies and leaves without writing y
@@ -344,7 +327,7 @@ __global__ void __launch_bounds__(RS_THREADS, 1) w8a16_rsw_kernel(const RsArgs a
   if (tid == 0) {
     trace_stamp(tr, 3);
     ptx::mbar_arrive_expect_tx(bar_x, (uint32_t)(M * K * 2));
-    rs_copy_x(sbase + (uint32_t)a.off_x, a.x, (uint32_t)(M * K * 2), bar_x, b);
+    rs_bulk_g2s(sbase + (uint32_t)a.off_x, a.x, (uint32_t)(M * K * 2), bar_x);
   }
   if (ptx::mbar_wait(bar_w, 0u, a.timeout_ns, abort_flag))
     ptx::mbar_wait(bar_x, 0u, a.timeout_ns, abort_flag);

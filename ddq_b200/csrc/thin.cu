@@ -20,10 +20,8 @@
 //     engine, no multicast) per row counted on an mbarrier; where the slice
 //     and activations leave room, the next kernel's CTA shares the SM and
 //     starts its own copy while this one computes;
-//   * after the wait: the M x K fp16 activations (L2), each token row in
-//     4 KB bulk copies from a CTA-dependent start (lockstep copies of the
-//     same rows by every CTA queue on the same L2 lines), then per (tile,
-//     64-wide K block) one 16-byte weight load,
+//   * after the wait: the M x K fp16 activations (L2), one bulk copy per
+//     token row, then per (tile, 64-wide K block) one 16-byte weight load,
 //     8 exact e4m3 -> fp16x2 conversions and 4 MMAs, tokens on the MMA rows
 //     (zero rows past M), the tile's 8 weight rows on the MMA columns;
 //   * no activation split pre-pass (fp16 activations are used as they are),
@@ -158,19 +156,8 @@ __global__ void __launch_bounds__(TH_THREADS) w8a16_thin_kernel(const ThinArgs a
   // 2) activations (L2), one bulk copy per token row; row scales and biases
   const uint32_t sx = sbase + (uint32_t)a.off_x;
   if (tid == 0) ptx::mbar_arrive_expect_tx(bar_x, (uint32_t)(M * K * 2));
-  if (tid < M) {
-    // 4 KB pieces from a CTA-dependent start: every CTA copies the same rows
-    // right after the dependency, and copies in lockstep queue on the same
-    // L2 lines
-    const uint32_t bytes = (uint32_t)(K * 2), np = (bytes + 4095u) / 4096u;
-    const uint32_t r = (uint32_t)blockIdx.x % np;
-    for (uint32_t q = 0; q < np; ++q) {
-      const uint32_t off = (q + r < np ? q + r : q + r - np) * 4096u;
-      bulk_g2s(sx + (uint32_t)(tid * a.sx) + off,
-               reinterpret_cast<const uint8_t*>(a.x + (size_t)tid * K) + off,
-               min(4096u, bytes - off), bar_x);
-    }
-  }
+  if (tid < M)
+    bulk_g2s(sx + (uint32_t)(tid * a.sx), a.x + (size_t)tid * K, (uint32_t)(K * 2), bar_x);
   float* sc = reinterpret_cast<float*>(th_smem + a.off_sc);
   float* bi = reinterpret_cast<float*>(th_smem + a.off_bi);
   if (tid < rows) {
