@@ -152,12 +152,6 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
   const int valid = min(R, a.N - r0);
   const int at0 = split * a.atoms / S, at1 = (split + 1) * a.atoms / S;
   const int nat = at1 - at0, kc = nat * 64, k0 = at0 * 64;
-  // Step i takes atom (i + rot) mod nat of the CTA's K range: every CTA reads
-  // the same activations, and CTAs walking them in lockstep would all ask
-  // the same few L2 lines at once (measured: atoms landing ~0.5 us apart);
-  // rotated starts spread the requests over the whole activation block.  The
-  // order is fixed per CTA, so results stay bitwise reproducible.
-  const int rot = rc % nat;
   const int K = a.K;
   const uint64_t tmo = a.timeout_ns;
   const uint32_t bar0 = sbase + (uint32_t)a.off_bar;
@@ -228,8 +222,7 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
             !ptx::mbar_wait(bar(RT_BAR_XE + s), (uint32_t)((i / xs) - 1) & 1u, tmo, abort_flag))
           break;
         ptx::mbar_arrive_expect_tx(bar(RT_BAR_XF + s), (uint32_t)RT_XSTAGE);
-        const int at = i + rot < nat ? i + rot : i + rot - nat;
-        ptx::tma_load_2d(sbase + (uint32_t)(a.off_x + s * RT_XSTAGE), &tm_x, k0 + at * 64, 0,
+        ptx::tma_load_2d(sbase + (uint32_t)(a.off_x + s * RT_XSTAGE), &tm_x, k0 + i * 64, 0,
                          bar(RT_BAR_XF + s));
         ++issued;
       }
@@ -238,6 +231,7 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
       for (int i = issued > xs ? issued - xs : 0; i < issued; ++i)
         ptx::mbar_wait(bar(RT_BAR_XF + i % xs), (uint32_t)(i / xs) & 1u, tmo, drain_flag);
       ptx::mbar_wait(bar(RT_BAR_W), 0u, tmo, drain_flag);
+      trace_stamp(tr, 15);  // producer drained
     }
     __syncwarp();
   } else if (warp <= RT_ISSUERS) {
@@ -301,7 +295,7 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
       // 128 bytes (chunk c lands at c ^ (row mod 8)).  Rows >= valid convert
       // whatever the slice buffer holds: they only reach accumulator
       // columns that are never stored.
-      const uint8_t* src = smem + (i + rot < nat ? i + rot : i + rot - nat) * 64;
+      const uint8_t* src = smem + i * 64;
       uint8_t* dst = smem + a.off_b + sb * bstage;
       for (int u = ct; u < R * 4; u += RT_CONV_THREADS) {
         const int r = u >> 2, c = u & 3, sw = r & 7;
@@ -352,6 +346,7 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
             for (int j = 0; j < 32; ++j)
               v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(u[j]));
           }
+          if (c0 == 0 && ct == 0) trace_stamp(tr, 13);  // first chunk in registers
           if (lane < 16 && S > 1) {
             // fp32 partial of token row m (all 64; rows >= M hold zeros)
 #pragma unroll
@@ -413,6 +408,7 @@ __global__ void __launch_bounds__(RT_THREADS, 2)
         }
       }
     }
+    if (ct == 0) trace_stamp(tr, 14);  // epilogue stores issued
     __syncwarp();
   }
 

@@ -319,15 +319,6 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
     kb = (nsplit > 1 ? (int)blockIdx.z : 0) * args.kps;
     nk = max(0, min(args.kps, KS - kb));
   };
-  // K stage of step i of unit u: every CTA reads the same activation planes,
-  // and CTAs walking K in lockstep would all ask the same L2 lines at once;
-  // each unit starts at its own stage (u mod nk) instead.  All three roles
-  // use this order, fixed per unit (bitwise reproducible).
-  auto kstage = [&](int kb, int nk, int u, int i) {
-    int j = i + u % nk;
-    if (j >= nk) j -= nk;
-    return kb + j;
-  };
 
   // full[s]: both producers arrive (expect_tx) and their TMA bytes land
   const uint32_t bar_full = sbase + L::OFF_BAR;
@@ -412,12 +403,10 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
         int i = 0;
         if (!waited) {
           const int pre = nk < NS ? nk : NS;
-          for (; i < pre; ++i, adv()) issue_w(rs, kstage(kb, nk, u, i), n0);  // fresh: no wait
-          for (int i2 = NS; i2 < nk; ++i2) {
-            const int ks = kstage(kb, nk, u, i2);
-            for (int a = 0; a < stage_atoms(ks); ++a)
-              ptx::tma_prefetch_l2_2d(&tm_w, ks * KB + a * DC_AK, n0);
-          }
+          for (; i < pre; ++i, adv()) issue_w(rs, kb + i, n0);  // fresh stages: no wait
+          for (int i2 = NS; i2 < nk; ++i2)
+            for (int a = 0; a < stage_atoms(kb + i2); ++a)
+              ptx::tma_prefetch_l2_2d(&tm_w, (kb + i2) * KB + a * DC_AK, n0);
           trace_stamp(tr, 2);
           ptx::pdl_wait();
           waited = true;
@@ -427,7 +416,7 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
             ok = false;
             break;
           }
-          issue_w(rs, kstage(kb, nk, u, i), n0);
+          issue_w(rs, kb + i, n0);
         }
       }
       if (!waited) ptx::pdl_wait();
@@ -455,13 +444,12 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
             ok = false;
             break;
           }
-          const int ks = kstage(kb, nk, u, i);
-          const int na = stage_atoms(ks);
+          const int na = stage_atoms(kb + i);
           const uint32_t full = bar_full + 8 * rs;
           ptx::mbar_arrive_expect_tx(full, (uint32_t)(na * L::XA_BYTES));
           const uint32_t dst = sbase + L::OFF_S + rs * L::S_BYTES + L::W_BYTES;
           for (int a = 0; a < na; ++a)
-            ptx::tma_load_3d(dst + a * L::XA_BYTES, &tm_x, ks * KB + a * DC_AK, 0, 0, full);
+            ptx::tma_load_3d(dst + a * L::XA_BYTES, &tm_x, (kb + i) * KB + a * DC_AK, 0, 0, full);
           ++g;
           if (++rs == NS) {
             rs = 0;
@@ -504,7 +492,7 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
           ok = ptx::mbar_wait(bar_full + 8 * s, ph, tmo, abort_flag);
           if (!ok) break;
           ptx::tc_fence_after();
-          const int rem = args.K - kstage(kb, nk, u, i) * KB;
+          const int rem = args.K - (kb + i) * KB;
           const int nkk = rem >= KB ? KB / 32 : (rem + 31) / 32;  // 32-byte K steps with data
           const uint64_t dw = desc0 + (uint64_t)((s * L::S_BYTES) >> 4);
           const uint64_t dx = dw + (uint64_t)(L::W_BYTES >> 4);

@@ -211,7 +211,8 @@ def main(argv=None):
                      # kernels with more phases (rt.cu): half-way and last
                      # activation atom ready, converters done, last activation
                      # load issued, accumulator complete
-                     "x_half", "x_last", "conv_done", "x_issued_last", "acc_full"]
+                     "x_half", "x_last", "conv_done", "x_issued_last", "acc_full",
+                     "epi_chunk0", "epi_stored", "producer_drained"]
             trace = {"ctas": int(len(used)), "span_us": round(float(rel[:, 7].max()), 3)}
             for j, nm in enumerate(names):
                 col = rel[:, j][used[:, j] > 0]
