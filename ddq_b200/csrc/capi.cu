@@ -87,29 +87,33 @@ int g_debug_flags = 0;
 // The thin kernel has no fault-injection hook, so while a test sets the
 // injection flag (bit 0) or asks for the split + decode kernels (bit 2), the
 // shapes it would take run the decode kernel; the trace flag (bit 1), the
-// thin-kernel test flag (bit 3) and the skip-the-tensor-core-resident-slice
-// flag (bit 5) keep it (it writes phase stamps too).
+// thin-kernel test flag (bit 3) and the tensor-core resident-slice flag
+// (bit 6, which takes no 1..16-token shape) keep it (it writes phase stamps
+// too).
 bool thin_shape(int64_t M, int64_t N, int64_t K) {
-  if (M > thin_max_m() || (g_debug_flags & ~(2 | 8 | 32)) != 0) return false;
+  if (M > thin_max_m() || (g_debug_flags & ~(2 | 8 | 64)) != 0) return false;
   const int dev = current_device();
   return dev >= 0 && thin_eligible(M, N, K, device_sm_count(dev));
 }
 
 // The resident-slice kernel (rs.cu) takes the shapes it fits first, under
 // the same debug-flag rule as the thin kernel; bit 3 sends its shapes to the
-// thin kernel (which then takes the ones it fits); bit 5 (skip the
-// tensor-core resident-slice kernel) leaves both of them in place.
+// thin kernel (which then takes the ones it fits); bit 6 (the tensor-core
+// resident-slice kernel for 17..64 tokens) leaves both of them in place.
 bool rs_shape(int64_t M, int64_t N, int64_t K) {
-  if ((g_debug_flags & ~(2 | 32)) != 0) return false;
+  if ((g_debug_flags & ~(2 | 64)) != 0) return false;
   const int dev = current_device();
   return dev >= 0 && rs_eligible(M, N, K, device_sm_count(dev));
 }
 
-// The tensor-core resident-slice kernel (rt.cu) takes 17..64-token shapes
-// before every other path; any debug bit but the trace (bit 1) and its own
-// timeout hook (bit 4) sends them to the older paths.
+// The tensor-core resident-slice kernel (rt.cu) is opt-in (debug bit 6): in
+// a chain of dependent calls it measured slower than the mma.sync resident
+// slice and the split + e4m3 decode kernels at every Qwen2.5 shape (e.g.
+// q/k/v at 64 tokens 7.3 vs 4.9 us, gate/up 11.9 vs 7.8 us).  With the bit
+// it takes 17..64-token shapes before every other path; any further bit but
+// the trace (1) and its timeout hook (4) sends them to the older paths.
 bool rt_shape(int64_t M, int64_t N, int64_t K, bool swiglu) {
-  if ((g_debug_flags & ~(2 | 16)) != 0) return false;
+  if ((g_debug_flags & 64) == 0 || (g_debug_flags & ~(2 | 16 | 64)) != 0) return false;
   const int dev = current_device();
   return dev >= 0 && rt_eligible(M, N, K, device_sm_count(dev), swiglu);
 }

@@ -10,6 +10,17 @@
 // take (rows 32 b + i = gate row 16 b + i, rows 32 b + 16 + i = up row
 // 16 b + i).
 //
+// Status: opt-in (ddq_set_debug bit 6), correct, and slower than the
+// default paths.  In a chain of dependent calls on B200 it measured 7.3 us
+// for q/k/v at 64 tokens (mma.sync resident slice: 4.9), 11.9 us for gate/up
+// (split + e4m3 decode: 7.8) and 22.5 us for down (9.0).  Phase stamps and a
+// standalone probe show where it goes: a tcgen05.mma of M = 64, N <= 72
+// costs its issuing thread ~30 ns (tensor-pipe time ~10 ns), so K = 896 (56
+// MMAs) needs ~1.7 us of issue from one thread, ~1 us from the three used
+// here; the first activation atom lands ~0.5 us after the dependency; the
+// epilogue over three accumulators and the barrier round trips add ~1.5 us.
+// The design notes below are what was built.
+//
 // Why a kernel of its own: at 17..64 tokens the legacy mma.sync path runs out
 // of tensor throughput (one m16n8k16 per about 8 SM cycles: 7.7 us of MMAs
 // alone for the 9728 x 896 gate/up at 64 tokens), and the split-plane e4m3
@@ -29,9 +40,10 @@
 //                 through a ring of 3..16 stages (as many as the shared-memory
 //                 budget leaves: the fetch from L2 is latency-bound, so its
 //                 rate grows with the atoms in flight)
-//     warp 1      one thread issues 4 MMAs (K = 16) per atom into one
-//                 64 x R fp32 accumulator
-//     warps 2-7   converters, a ring of fp16 weight atoms ahead of the MMAs
+//     warps 1-3   three MMA issuers (lane 0), 4 MMAs (K = 16) per atom on
+//                 atoms i = w, w + 3, ... into their own 64 x R fp32
+//                 accumulators, summed in order by the epilogue
+//     warps 4-7   converters, a ring of fp16 weight atoms ahead of the MMAs
 //                 (every atom where shared memory allows: each refill waits
 //                 for an MMA to complete)
 //     warps 4-7   then the epilogue: token m sits in TMEM lane

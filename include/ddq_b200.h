@@ -104,15 +104,15 @@ size_t ddq_w8a16_gemm_workspace_size(int64_t M, int64_t N, int64_t K);
  * Requirements: M >= 0, N >= 1, K >= 1; the fast paths need K % 16 == 0 and
  * 16-byte aligned x / wq (a generic CUDA kernel covers the rest).
  * Kernels by shape (16-byte aligned x and wq, K % 16 == 0):
- *   17..64 tokens, K % 64 == 0, at most 256 weight rows per CTA (every
- *     Qwen2.5-0.5B projection): one tcgen05 kernel, tokens on the MMA's A
- *     operand, each CTA's weight rows converted to fp16 in shared memory
- *     before the grid dependency (K over 1280 split over a cluster);
- *   1..16 tokens (17..64 with few MMAs per CTA while the kernel above is
- *     switched off) where a CTA's weight slice and the activations fit in
- *     shared memory: one mma.sync kernel on a resident weight slice (the
- *     thin kernel takes the 1..16-token shapes that one does not);
- *   other M <= 64: the activation-split pre-pass plus the e4m3 tcgen05 GEMM;
+ *   1..16 tokens, and 17..64 with few MMAs per CTA, where a CTA's weight
+ *     slice and the activations fit in shared memory: one mma.sync kernel
+ *     on a resident weight slice (the thin kernel takes the 1..16-token
+ *     shapes that one does not);
+ *   other M <= 64: the activation-split pre-pass plus the e4m3 tcgen05 GEMM
+ *     (with ddq_set_debug bit 6, 17..64 tokens with K % 64 == 0 run an
+ *     opt-in single tcgen05 kernel instead - tokens on the MMA's A operand,
+ *     each CTA's weight rows converted to fp16 in shared memory before the
+ *     grid dependency - correct, but slower in dependent chains);
  *   larger M: the prefill kernels.
  * The workspace is used by the last two only.  While ddq_set_debug's
  * injection flags are
@@ -168,9 +168,10 @@ int ddq_w8a16_gemm_noalloc(const void* x, const uint8_t* wq, const float* scales
  * wq_gu [2I, K] (and scales_gu, bias [2I]) interleave gate and up in blocks of
  * 16 rows: rows 32 b + i = gate row 16 b + i, rows 32 b + 16 + i = up row
  * 16 b + i (0 <= i < 16).  I % 16 == 0, K % 16 == 0, 16-byte aligned x, wq_gu
- * and z [M, I].  Kernels: 17..64 tokens with K % 64 == 0, the tcgen05
- * resident-slice kernel (no workspace); other M <= 64, the split pre-pass and
- * the e4m3 decode GEMM; larger M, the prefill kernels.  Workspace:
+ * and z [M, I].  Kernels: M <= 64, the split pre-pass and the e4m3 decode
+ * GEMM (with ddq_set_debug bit 6, 17..64 tokens with K % 64 == 0 run the
+ * opt-in tcgen05 resident-slice kernel); larger M, the prefill kernels.
+ * Workspace:
  * ddq_w8a16_gemm_swiglu_workspace_size bytes, used as for ddq_w8a16_gemm.
  */
 size_t ddq_w8a16_gemm_swiglu_workspace_size(int64_t M, int64_t I, int64_t K);
@@ -336,16 +337,16 @@ int ddq_device_error(int* code, void* stream);
  * this process.  flags bit 0 makes the tensor-core kernel skip the
  * accumulator-ready signal, so its epilogue wait runs out and reports
  * DDQ_ERR_TIMEOUT through ddq_device_error() without faulting the GPU;
- * bit 1 turns on the phase trace read by ddq_read_trace(); bit 4 makes the
- * 17..64-token tcgen05 resident-slice kernel skip its accumulator-ready
- * signal the same way; bits 2, 3 and 5 have no effect of their own.  While
- * bit 0 or bit 2 is set, the shapes of the resident-slice and thin kernels
- * run the split + decode kernels instead (bit 2 alone selects exactly that,
- * e.g. to compare a fused producer's planes with the GEMM's own pre-pass);
- * while bit 3 is set, the mma.sync resident-slice kernel's shapes go to the
- * thin kernel where it takes them (to test that kernel); while any bit but
- * 1 and 4 is set, the tcgen05 resident-slice kernel takes no shape (bit 5
- * alone leaves its shapes to the mma.sync kernels where they fit).
+ * bit 1 turns on the phase trace read by ddq_read_trace(); bit 6 switches
+ * on the opt-in 17..64-token tcgen05 resident-slice kernel, and bit 4 makes
+ * that kernel skip its accumulator-ready signal the same way; bits 2 and 3
+ * have no effect of their own.  While bit 0 or bit 2 is set, the shapes of
+ * the resident-slice and thin kernels run the split + decode kernels instead
+ * (bit 2 alone selects exactly that, e.g. to compare a fused producer's
+ * planes with the GEMM's own pre-pass); while bit 3 is set, the mma.sync
+ * resident-slice kernel's shapes go to the thin kernel where it takes them
+ * (to test that kernel); with any bit but 1, 4 and 6 set, the opt-in kernel
+ * takes no shape.
  * A wait that runs out is followed by a second bounded wait for the CTA's own
  * copies in flight; should that one run out too, the CTA exits with copies
  * outstanding and the context's further behaviour is undefined (it has not

@@ -42,14 +42,6 @@ def lib(cuda_device):
     return _lib.load()
 
 
-@pytest.fixture(autouse=True)
-def _without_tensor_core_resident_slices(lib):
-    """17..64-token shapes go to the tensor-core resident-slice kernel
-    (rt.cu, its own tests) first; debug bit 5 keeps them on this file's
-    kernels and on the split + decode kernels."""
-    assert lib.ddq_set_debug(32, 0) == 0
-    yield
-    lib.ddq_set_debug(0, 0)
 
 
 def sms():

@@ -1,4 +1,5 @@
-"""GPU parity tests of the tensor-core resident-slice GEMM (``rt.cu``: 17..64
+"""GPU parity tests of the opt-in tensor-core resident-slice GEMM (``rt.cu``,
+switched on by ddq_set_debug bit 6 for every test here: 17..64
 tokens on the tcgen05 A operand, each CTA's weight rows converted to fp16 in
 shared memory before the grid dependency as the B operand, K split over a
 thread-block cluster when it is long) against the CPU oracle: the Qwen2.5
@@ -44,6 +45,16 @@ def g(cuda_device):
 def lib(cuda_device):
     from ddq_b200 import _lib
     return _lib.load()
+
+
+RT = 64  # ddq_set_debug bit 6: the (opt-in) tensor-core resident-slice kernel
+
+
+@pytest.fixture(autouse=True)
+def _with_tensor_core_resident_slices(lib):
+    assert lib.ddq_set_debug(RT, 0) == 0
+    yield
+    lib.ddq_set_debug(0, 0)
 
 
 def check(g, M, N, K, seed, bias=True):
@@ -203,13 +214,13 @@ def test_dispatch(lib):
     assert lib.ddq_w8a16_gemm_kernel_count(200, 1152, 896) == 2    # expansion + prefill GEMM
     # lm_head rows: more than 256 rows per CTA, the decode kernel
     assert lib.ddq_w8a16_gemm_kernel_count(32, 151936, 896) == 2
-    # debug bit 5 leaves 17..64 tokens to the older kernels
-    assert lib.ddq_set_debug(32, 0) == 0
-    try:
-        assert lib.ddq_w8a16_gemm_kernel_count(64, 9728, 896) == 2
-        assert lib.ddq_w8a16_gemm_kernel_count(64, 1152, 896) == 1  # warps over tokens
-    finally:
-        lib.ddq_set_debug(0, 0)
+    # without bit 6, 17..64 tokens go to the older kernels
+    assert lib.ddq_set_debug(0, 0) == 0
+    assert lib.ddq_w8a16_gemm_kernel_count(64, 9728, 896) == 2      # split + decode
+    assert lib.ddq_w8a16_gemm_kernel_count(64, 1152, 896) == 1      # mma.sync, warps over tokens
+    # bit 6 with an injection bit: the older kernels
+    assert lib.ddq_set_debug(RT | 4, 0) == 0
+    assert lib.ddq_w8a16_gemm_kernel_count(64, 1152, 896) == 2
 
 
 def device_error(lib):
@@ -231,7 +242,7 @@ def test_bounded_wait_reports_timeout_and_context_survives(g, lib, M, N, K):
     assert device_error(lib) == 0
     y0 = torch.zeros(M, N, dtype=torch.float16, device="cuda")
     try:
-        assert lib.ddq_set_debug(16, 20_000_000) == 0
+        assert lib.ddq_set_debug(RT | 16, 20_000_000) == 0
         assert lib.ddq_w8a16_gemm_kernel_count(M, N, K) == 1
         from ddq_b200 import _lib
         st = lib.ddq_w8a16_gemm(xd.data_ptr(), wqd.data_ptr(), sd.data_ptr(), None,
@@ -242,7 +253,7 @@ def test_bounded_wait_reports_timeout_and_context_survives(g, lib, M, N, K):
         assert device_error(lib) == DDQ_ERR_TIMEOUT
         assert not y0.any()  # nothing written
     finally:
-        lib.ddq_set_debug(0, 0)
+        lib.ddq_set_debug(RT, 0)
     y = g.f8_forward(xd, wqd, sd)
     torch.cuda.synchronize()
     assert device_error(lib) == 0
