@@ -32,9 +32,10 @@
 // (one 128-byte swizzle row):
 //   before the grid dependency resolves
 //     * one bulk copy of the CTA's contiguous e4m3 slice (one per row when K
-//       is split), the per-row scale and bias, the TMEM allocation, and the
-//       first two weight atoms converted to fp16 in the canonical 128-byte
-//       swizzled K-major layout (cvt.rn.f16x2.e4m3x2: exact);
+//       is split), the per-row scale and bias, the TMEM allocation, and as
+//       many weight atoms as the fp16 ring holds converted to fp16 in the
+//       canonical 128-byte swizzled K-major layout (cvt.rn.f16x2.e4m3x2:
+//       exact);
 //   after it
 //     warp 0      TMA loads of the activation atoms (64 tokens x 64 K, 8 KB)
 //                 through a ring of 3..16 stages (as many as the shared-memory
@@ -54,8 +55,9 @@
 // and, after a cluster barrier, sums a share of the outputs over the
 // cluster's partials in split order through distributed shared memory:
 // deterministic, no workspace, no atomics.
-// Shared memory stays within half an SM where the shape allows, so the next
-// GEMM's CTA can be resident and fetch its own slice while this one runs.
+// Shared memory stays within half an SM where both rings still fit there
+// (the next GEMM's CTA can then be resident and fetch its own slice while
+// this one runs), else the CTA takes the whole 227 KB.
 // Every mbarrier wait is bounded; on timeout the CTA records
 // DDQ_ERR_TIMEOUT, waits (bounded) for its own copies and MMAs, still takes
 // part in the cluster barriers, writes nothing, frees TMEM and exits.
