@@ -429,8 +429,9 @@ def run_lm_head(args, device, rank, world, peaks):
     per M: the shard kernel per call (a replayed CUDA graph cycling through
     copies of the shard that together exceed twice the L2, so every call reads
     HBM), its HBM fraction, the all-gather per call and the whole sharded pick
-    per call (eager, CUDA events, max over ranks), and on rank 0 the number of
-    token ids that differ from the unsharded pick over the full vocabulary."""
+    per call (eager, CUDA events, max over ranks), the same pick captured as
+    one CUDA graph and replayed, and on rank 0 the number of token ids that
+    differ from the unsharded pick over the full vocabulary."""
     import torch.distributed as dist
     from ddq_b200 import gemm_fp8, lm_head
     V = 151936
@@ -502,9 +503,28 @@ def run_lm_head(args, device, rank, world, peaks):
             torch.cuda.synchronize(device)
             rec["sharded_pick_us"] = round(reduce_max(e0.elapsed_time(e1), world, device)
                                            * 1e3 / n, 2)
+            # the same pick captured once as a CUDA graph (kernel, all-gather,
+            # combine) and replayed: the per-step latency of a serving loop
+            pick = lm_head.ShardedGreedyGraph(x.clone(), wq, sc, lo)
+            for _ in range(3):
+                pick.replay()
+            torch.cuda.synchronize(device)
+            dist.barrier()
+            e0.record()
+            for _ in range(n):
+                gids = pick.replay()
+            e1.record()
+            torch.cuda.synchronize(device)
+            rec["sharded_pick_graph_us"] = round(reduce_max(e0.elapsed_time(e1), world, device)
+                                                 * 1e3 / n, 2)
+            gids = gids.clone()
+            pick.release()
+            del pick
+            torch.cuda.synchronize(device)
             if rank == 0:
                 ref_ids, _ = lm_head.lm_head_argmax(x, *full)
                 rec["mismatch_vs_unsharded"] = int((ids != ref_ids).sum())
+                rec["graph_mismatch_vs_unsharded"] = int((gids != ref_ids).sum())
         out[str(M)] = rec
     if world > 1:
         m = [out[k] for k in ("1", "16", "64")]
@@ -512,7 +532,9 @@ def run_lm_head(args, device, rank, world, peaks):
                  else "shard kernel" if all(r["all_gather_us"] < r["us"] for r in m) else "mixed")
         out["limited_by"] = limit
         out["timing"] = ("shard kernel: replayed CUDA graph; all-gather and sharded pick: eager "
-                         "calls between CUDA events (host launch gaps included); max over ranks")
+                         "calls between CUDA events (host launch gaps included); sharded pick "
+                         "graph: the whole pick captured once (lm_head.ShardedGreedyGraph) and "
+                         "replayed; max over ranks")
     del copies, full
     torch.cuda.empty_cache()
     return out

@@ -106,3 +106,43 @@ def sharded_greedy(x: torch.Tensor, wq_shard: torch.Tensor, scales_shard: torch.
     """Global greedy ids from a vocab-sharded lm_head (one all-gather of M int64/rank)."""
     _, packed = lm_head_argmax(x, wq_shard, scales_shard, vocab_offset)
     return combine_shards(packed, group)
+
+
+class ShardedGreedyGraph:
+    """The vocab-sharded greedy pick (shard kernel, NCCL all-gather, combine)
+    captured once as a CUDA graph and replayed, for serving loops that pick
+    a token every step: no host work between the three parts.
+
+    ``x`` is the static input: copy each step's activations into it, then call
+    ``replay()``, which returns the static int64 ids tensor.  Every rank of
+    ``group`` builds and replays its graph in the same order.  Call
+    ``release()`` on every rank before the process group is destroyed (a
+    graph that still holds an NCCL operation keeps the communicator alive)."""
+
+    def __init__(self, x: torch.Tensor, wq_shard: torch.Tensor, scales_shard: torch.Tensor,
+                 vocab_offset: int, group=None):
+        if not x.is_cuda:
+            raise RuntimeError("ShardedGreedyGraph: CUDA tensors required")
+        self.x = x
+        dev = x.device
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        # warm-up on the capture stream: its lm_head workspace and the
+        # communicator exist before capture
+        with torch.cuda.stream(side):
+            sharded_greedy(x, wq_shard, scales_shard, vocab_offset, group)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=side):
+            self.ids = sharded_greedy(x, wq_shard, scales_shard, vocab_offset, group)
+        torch.cuda.synchronize(dev)
+
+    def replay(self) -> torch.Tensor:
+        if self.graph is None:
+            raise RuntimeError("ShardedGreedyGraph: released")
+        self.graph.replay()
+        return self.ids
+
+    def release(self) -> None:
+        self.graph = None

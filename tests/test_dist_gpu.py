@@ -3,7 +3,8 @@
 Each rank quantizes its contiguous shard of the same seeded 151936 x 896
 weight, runs the fused lm_head argmax on it, and the (max, index) words are
 combined with one NCCL all-gather; every rank must get exactly the token ids
-the unsharded kernel picks on one GPU.  Needs >= 2 GPUs (skipped otherwise)."""
+the unsharded kernel picks on one GPU, eagerly and through the pick captured
+as one CUDA graph (kernel, all-gather, combine) and replayed on new input.  Needs >= 2 GPUs (skipped otherwise)."""
 import os
 import socket
 
@@ -44,6 +45,12 @@ def _rank(rank, world, port, out):
         res = {}
         for M in (1, 16, 64):
             res[M] = lm_head.sharded_greedy(x[:M], wq, s, lo).cpu()
+            # the same pick captured as one CUDA graph, replayed on a new input
+            pick = lm_head.ShardedGreedyGraph(torch.zeros_like(x[:M]), wq, s, lo)
+            pick.x.copy_(x[:M])
+            res[("graph", M)] = pick.replay().clone().cpu()
+            pick.release()
+            torch.cuda.synchronize()
         if rank == 0:
             wq_full, s_full = gemm_fp8.quantize(w)
             for M in (1, 16, 64):
@@ -68,3 +75,4 @@ def test_vocab_sharded_lm_head_over_nccl(world):
         full = out[0][("full", M)]
         for r in range(world):
             assert torch.equal(out[r][M], full), (r, M)
+            assert torch.equal(out[r][("graph", M)], full), (r, M)
