@@ -20,6 +20,7 @@ C ABI of ``libddq_b200.so``; nothing falls back to the CPU.
 """
 from __future__ import annotations
 
+import contextlib
 from typing import List, Optional
 
 import torch
@@ -27,6 +28,19 @@ import torch
 from . import _lib
 
 _workspaces: dict = {}
+_ws_sizes: dict = {}   # (entry, device index, shape) -> workspace bytes
+# the current stream's raw handle without building a Stream object (a few us
+# per call on the eager path); torch's public API where it is missing
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _on_device(device: torch.device):
+    """Make `device` current for the library call (which sizes and launches
+    on the current device), without the two device switches when it already
+    is."""
+    if torch.cuda.current_device() == device.index:
+        return contextlib.nullcontext()
+    return torch.cuda.device(device)
 
 
 def _check(cond: bool, msg: str) -> None:
@@ -35,6 +49,8 @@ def _check(cond: bool, msg: str) -> None:
 
 
 def _stream_ptr(device: torch.device) -> int:
+    if _raw_stream is not None and device.index is not None:
+        return _raw_stream(device.index)
     return torch.cuda.current_stream(device).cuda_stream
 
 
@@ -46,7 +62,7 @@ def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     workspace serves every call ordered on a stream; calls running on
     different streams at the same time get different workspaces.
     """
-    key = (device.type, device.index, torch.cuda.current_stream(device).cuda_stream)
+    key = (device.type, device.index, _stream_ptr(device))
     buf = _workspaces.get(key)
     if buf is None or buf.numel() < nbytes:
         buf = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
@@ -96,13 +112,17 @@ def f8_forward(x: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor,
     wqc = wq.contiguous()
     sc = scales.contiguous()
     L = _lib.load()
-    with torch.cuda.device(x.device):
-        nws = L.ddq_w8a16_gemm_workspace_size(M, N, K)
-        ws = workspace(x.device, nws) if nws else None
+    dev = x.device
+    with _on_device(dev):
+        key = (dev.index, M, N, K)
+        nws = _ws_sizes.get(key)
+        if nws is None:
+            nws = _ws_sizes[key] = L.ddq_w8a16_gemm_workspace_size(M, N, K)
+        ws = workspace(dev, nws) if nws else None
         st = L.ddq_w8a16_gemm(x2.data_ptr(), wqc.data_ptr(), sc.data_ptr(), bptr, bcode,
                               y2.data_ptr(), M, N, K,
                               ws.data_ptr() if ws is not None else None,
-                              ws.numel() if ws is not None else 0, _stream_ptr(x.device))
+                              ws.numel() if ws is not None else 0, _stream_ptr(dev))
     _lib.check(st, "gemm_fp8.f8_forward")
     return y2.reshape(*x.shape[:-1], N)
 
@@ -152,13 +172,17 @@ def f8_forward_swiglu(x: torch.Tensor, wq_il: torch.Tensor, scales_il: torch.Ten
         bcode = _lib.DTYPE_F16 if bias_il.dtype == torch.float16 else _lib.DTYPE_F32
     wqc, sc = wq_il.contiguous(), scales_il.contiguous()
     L = _lib.load()
-    with torch.cuda.device(x.device):
-        nws = L.ddq_w8a16_gemm_swiglu_workspace_size(M, inter, K)
-        ws = workspace(x.device, nws) if nws else None
+    dev = x.device
+    with _on_device(dev):
+        key = ("swiglu", dev.index, M, inter, K)
+        nws = _ws_sizes.get(key)
+        if nws is None:
+            nws = _ws_sizes[key] = L.ddq_w8a16_gemm_swiglu_workspace_size(M, inter, K)
+        ws = workspace(dev, nws) if nws else None
         st = L.ddq_w8a16_gemm_swiglu(x2.data_ptr(), wqc.data_ptr(), sc.data_ptr(), bptr, bcode,
                                      z.data_ptr(), M, inter, K,
                                      ws.data_ptr() if ws is not None else None,
-                                     ws.numel() if ws is not None else 0, _stream_ptr(x.device))
+                                     ws.numel() if ws is not None else 0, _stream_ptr(dev))
     _lib.check(st, "gemm_fp8.f8_forward_swiglu")
     return z.reshape(*x.shape[:-1], inter)
 
