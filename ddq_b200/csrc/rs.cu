@@ -440,6 +440,11 @@ RsPlan rs_plan(int64_t M, int64_t N, int64_t K, int sms) {
   // one tile per CTA with a long K (the Qwen2.5 down projection, 56 CTAs):
   // the thin kernel's 8-row tiles on twice the SMs measured faster
   if (ntl == 1 && K >= 2048) return p;
+  // 9..16 tokens with one tile per CTA (q/k/v, o, up to ~2300 rows): two
+  // 8-token MMAs per weight fragment on at most one SM per 16 rows; the thin
+  // kernel's 8-row tiles with all 16 tokens on the MMA rows measured 0.2-0.55
+  // us faster per chained call (e.g. 1152 x 896 at 16 tokens: 2.91 vs 3.44)
+  if (ntl == 1 && nb == 2 && thin_eligible(M, N, K, sms)) return p;
   const int64_t w_bytes = ntl * RS_TILE * K;
   const int64_t red_bytes = (int64_t)RS_WARPS * ntl * RS_TILE * nb * 8 * 4;
   if (red_bytes > w_bytes) return p;  // the partial sums reuse the weight slice
