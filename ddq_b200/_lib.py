@@ -35,6 +35,10 @@ _SIGNATURES = {
     "ddq_prefill_rope_kv": (ctypes.c_int, [_vp, _c_int64, _vp, _vp, _c_int64, _c_int64, _vp, _vp,
                                            _c_int64, _vp, _vp, _vp, _c_int64, _c_int64, _c_int64,
                                            _c_int64, _c_int64, _vp]),
+    "ddq_w8a16_gemm_qkv_rope_kv": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, _c_int64,
+                                                  _c_int64, _c_int64, _c_int64, _c_int64, _c_int64,
+                                                  _vp, _vp, _c_int64, _c_int64, _vp, _vp, _c_int64,
+                                                  _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "ddq_decode_attention": (ctypes.c_int, [_vp, _c_int64, _vp, _vp, _c_int64, _c_int64, _vp, _vp,
                                             _vp, _vp, _c_int64, _c_int64, _c_int64, _c_int64,
                                             _c_int64, ctypes.c_float, _vp]),
@@ -57,6 +61,7 @@ _SIGNATURES = {
 EXPORTED = tuple(_SIGNATURES)
 
 DTYPE_NONE, DTYPE_F16, DTYPE_F32 = 0, 1, 2
+ERR_SHAPE = 2  # DDQ_ERR_SHAPE: the entry does not take this shape
 
 _lock = threading.Lock()
 _lib = None

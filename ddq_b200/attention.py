@@ -142,3 +142,85 @@ def prefill_rope_kv(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Ten
             torch.cuda.current_stream(qkv.device).cuda_stream)
     _lib.check(st, "prefill_rope_kv")
     return (q, k, v) if kv_out else q
+
+
+def qkv_rope_kv(x: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor,
+                bias: Optional[torch.Tensor], k_cache: torch.Tensor, v_cache: torch.Tensor,
+                cos: torch.Tensor, sin: torch.Tensor, start: int, num_heads: int,
+                num_kv_heads: int, head_dim: int, kv_out: bool = False):
+    """The q/k/v projection of a prefill chunk followed by ``prefill_rope_kv``:
+    x fp16 [B, S, K] (or [B * S, K] with B taken from the caches), wq/scales/bias
+    the fused [(Hq + 2 Hkv) * D, K] projection.  Same results, bit for bit, as
+    ``gemm_fp8.f8_forward`` then ``prefill_rope_kv``.  Where the prefill kernel
+    takes the shape (D == 64, B * S at prefill size) one launch pair (weight
+    expansion + GEMM) does all of it, RoPE and the cache write in the GEMM's
+    epilogue (``ddq_w8a16_gemm_qkv_rope_kv``), and the [B * S, (Hq + 2 Hkv) D]
+    projection is never written; elsewhere the two calls run.  Replaces the
+    reference's q/k/v projections (``engine.py:215-217``), q/k RoPE
+    (``engine.py:219-220``) and cache write (``engine.py:222``)."""
+    from . import gemm_fp8
+
+    def need(cond, msg):
+        if not cond:
+            raise RuntimeError(msg)
+    B = k_cache.shape[0]
+    width = (num_heads + 2 * num_kv_heads) * head_dim
+    need(x.is_cuda and x.dtype == torch.float16, "qkv_rope_kv: x must be fp16 CUDA")
+    need(wq.is_cuda and wq.dtype == torch.uint8 and wq.dim() == 2 and wq.size(0) == width,
+         "qkv_rope_kv: wq must be uint8 [(Hq + 2 Hkv) * D, K]")
+    K = wq.size(1)
+    need(x.size(-1) == K, "qkv_rope_kv: inner dim mismatch")
+    rows = x.contiguous().reshape(-1, K)
+    need(rows.size(0) % B == 0, "qkv_rope_kv: x rows must be B * S")
+    S = rows.size(0) // B
+    st = _lib.ERR_SHAPE
+    if head_dim == 64 and S > 0 and k_cache.data_ptr() % 32 == 0 and \
+            v_cache.data_ptr() % 32 == 0 and k_cache.stride(0) % 16 == 0:
+        for c in (k_cache, v_cache):
+            need(c.is_cuda and c.dtype == torch.float16 and c.dim() == 4 and
+                 tuple(c.shape[:2]) == (B, num_kv_heads) and c.shape[3] == head_dim and
+                 c.stride(3) == 1 and c.stride(2) == head_dim and
+                 c.stride(1) == c.shape[2] * head_dim,
+                 "qkv_rope_kv: caches must be fp16 CUDA [B, Hkv, capacity, D], dense per sequence")
+        need(k_cache.stride(0) == v_cache.stride(0) and k_cache.shape == v_cache.shape,
+             "qkv_rope_kv: k and v caches must have the same shape and strides")
+        need(scales.is_cuda and scales.dtype == torch.float32 and scales.numel() == width,
+             "qkv_rope_kv: scales must be fp32 CUDA [(Hq + 2 Hkv) * D]")
+        cs = cos.reshape(S, head_dim).contiguous()
+        sn = sin.reshape(S, head_dim).contiguous()
+        need(cs.dtype == torch.float32 and sn.dtype == torch.float32,
+             "qkv_rope_kv: fp32 cos/sin [S, D]")
+        if cs.data_ptr() % 32:
+            cs = cs.clone()
+        if sn.data_ptr() % 32:
+            sn = sn.clone()
+        bptr, bcode = None, _lib.DTYPE_NONE
+        if bias is not None and bias.numel() > 0:
+            need(bias.numel() == width and bias.is_cuda and
+                 bias.dtype in (torch.float16, torch.float32), "qkv_rope_kv: bias mismatch")
+            bias = bias.contiguous()
+            bptr = bias.data_ptr()
+            bcode = _lib.DTYPE_F16 if bias.dtype == torch.float16 else _lib.DTYPE_F32
+        q = torch.empty((B, S, num_heads, head_dim), dtype=torch.float16, device=x.device)
+        k = v = None
+        if kv_out:
+            k = torch.empty((B, S, num_kv_heads, head_dim), dtype=torch.float16, device=x.device)
+            v = torch.empty_like(k)
+        wqc, sc = wq.contiguous(), scales.contiguous()
+        L = _lib.load()
+        with torch.cuda.device(x.device):
+            nws = L.ddq_w8a16_gemm_workspace_size(B * S, width, K)
+            ws = gemm_fp8.workspace(x.device, nws) if nws else None
+            st = L.ddq_w8a16_gemm_qkv_rope_kv(
+                rows.data_ptr(), wqc.data_ptr(), sc.data_ptr(), bptr, bcode, B, S, K,
+                num_heads, num_kv_heads, head_dim, k_cache.data_ptr(), v_cache.data_ptr(),
+                k_cache.stride(0), k_cache.shape[2], cs.data_ptr(), sn.data_ptr(), int(start),
+                q.data_ptr(), k.data_ptr() if kv_out else None, v.data_ptr() if kv_out else None,
+                ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+                torch.cuda.current_stream(x.device).cuda_stream)
+        if st != _lib.ERR_SHAPE:
+            _lib.check(st, "qkv_rope_kv")
+            return (q, k, v) if kv_out else q
+    qkv = gemm_fp8.f8_forward(rows, wq, scales, bias)
+    return prefill_rope_kv(qkv, k_cache, v_cache, cos, sin, start, num_heads, num_kv_heads,
+                           head_dim, kv_out=kv_out)

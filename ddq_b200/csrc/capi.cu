@@ -258,6 +258,54 @@ extern "C" int ddq_prefill_rope_kv(const void* qkv, int64_t qkv_stride, void* k_
       reinterpret_cast<cudaStream_t>(stream));
 }
 
+extern "C" int ddq_w8a16_gemm_qkv_rope_kv(const void* x, const uint8_t* wq, const float* scales,
+                                          const void* bias, int bias_dtype, int64_t B, int64_t S,
+                                          int64_t K, int64_t Hq, int64_t Hkv, int64_t D,
+                                          void* k_cache, void* v_cache,
+                                          int64_t cache_batch_stride, int64_t capacity,
+                                          const float* cos, const float* sin, int64_t start,
+                                          void* q_out, void* k_out, void* v_out, void* workspace,
+                                          size_t workspace_bytes, void* stream) {
+  if (B < 0 || S < 0 || K < 0 || Hq < 0 || Hkv < 0 || capacity < 0 || start < 0)
+    return DDQ_ERR_SHAPE;
+  if (bias_dtype != DDQ_DTYPE_NONE && bias_dtype != DDQ_DTYPE_F16 && bias_dtype != DDQ_DTYPE_F32)
+    return DDQ_ERR_INVALID_ARGUMENT;
+  if (bias_dtype != DDQ_DTYPE_NONE && !bias) return DDQ_ERR_INVALID_ARGUMENT;
+  if (B == 0 || S == 0) return DDQ_OK;
+  if (!x || !wq || !scales || !k_cache || !v_cache || !cos || !sin || !q_out)
+    return DDQ_ERR_INVALID_ARGUMENT;
+  const int64_t M = B * S, N = (Hq + 2 * Hkv) * D;
+  // the fused epilogue's shapes only (head_dim 64, a prefill-size chunk);
+  // callers run the GEMM and ddq_prefill_rope_kv for the others
+  if (D != 64 || Hq < 1 || Hkv < 1 || K == 0 || K % 16 != 0 || M > 0x7fffffff ||
+      N > 0x7fffffff || K > 0x7fffffff || capacity > 0x7fffffff || !pf_shape(M, N))
+    return DDQ_ERR_SHAPE;
+  if (start + S > capacity || cache_batch_stride < Hkv * capacity * D) return DDQ_ERR_SHAPE;
+  // the epilogue reads cos/sin and writes q, k, v by whole 32-byte sectors
+  auto a32 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 31u) == 0; };
+  if (!aligned16(x) || !aligned16(wq) || !a32(q_out) || !a32(k_cache) || !a32(v_cache) ||
+      (k_out && !a32(k_out)) || (v_out && !a32(v_out)) || !a32(cos) || !a32(sin) ||
+      cache_batch_stride % 16 != 0)
+    return DDQ_ERR_ALIGNMENT;
+  PfRope r{};
+  r.kc = reinterpret_cast<__half*>(k_cache);
+  r.vc = reinterpret_cast<__half*>(v_cache);
+  r.cache_bstride = cache_batch_stride;
+  r.cap = (int)capacity;
+  r.cos = cos;
+  r.sin = sin;
+  r.start = (int)start;
+  r.q_out = reinterpret_cast<__half*>(q_out);
+  r.k_out = reinterpret_cast<__half*>(k_out);
+  r.v_out = reinterpret_cast<__half*>(v_out);
+  r.S = (int)S;
+  r.Hq = (int)Hq;
+  r.Hkv = (int)Hkv;
+  return launch_pf(reinterpret_cast<const __half*>(x), wq, scales, bias, bias_dtype, nullptr,
+                   (int)M, (int)N, (int)K, workspace, workspace_bytes, g_wait_timeout_ns,
+                   g_debug_flags, reinterpret_cast<cudaStream_t>(stream), false, &r);
+}
+
 extern "C" int ddq_decode_attention(const void* qkv, int64_t qkv_stride, void* k_cache,
                                     void* v_cache, int64_t cache_batch_stride, int64_t capacity,
                                     const float* cos, const float* sin, const int64_t* pos,

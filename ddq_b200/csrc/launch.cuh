@@ -79,10 +79,27 @@ int launch_lmh(const __half* x, const uint8_t* wq, const float* scales, int M, i
 // Prefill shapes: exact e4m3 -> fp16 weight expansion into the workspace
 // (N * K * 2 bytes), then the fp16 tensor-core GEMM (tc_prefill.cu).
 size_t pf_workspace_bytes(int64_t N, int64_t K);
+// QKV epilogue with RoPE and the KV-cache write (head_dim 64): the weight
+// rows are [Hq q heads | Hkv k heads | Hkv v heads] x 64, GEMM token row m is
+// sequence b = m / S, token s = m % S, at cache position start + s.
+struct PfRope {
+  __half* kc;             // [B, Hkv, cap, 64], batch stride cache_bstride
+  __half* vc;
+  int64_t cache_bstride;
+  int cap;
+  const float* cos;       // [S, 64] for positions start .. start + S - 1
+  const float* sin;
+  int start;
+  __half* q_out;          // [B * S, Hq, 64]
+  __half* k_out;          // [B * S, Hkv, 64] or null
+  __half* v_out;
+  int S, Hq, Hkv;
+};
+
 int launch_pf(const __half* x, const uint8_t* wq, const float* scales, const void* bias,
               int bias_dtype, __half* y, int M, int N, int K, void* ws, size_t ws_bytes,
               unsigned long long timeout_ns, int debug_flags, cudaStream_t s,
-              bool swiglu = false);
+              bool swiglu = false, const PfRope* rope = nullptr);
 // A workspace was used by a call other than a double-buffered prefill GEMM
 // (the next prefill call on it must not expand ahead of the previous kernel);
 // a call on a capturing stream also marks it as used in a CUDA graph.

@@ -63,6 +63,8 @@ struct PfLayout {
   static_assert(ALLOC <= 232448, "shared memory budget");
 };
 
+constexpr int PF_EPI_STORE = 0, PF_EPI_SWIGLU = 1, PF_EPI_ROPE = 2;
+
 struct PfArgs {
   const float* scales;
   const void* bias;
@@ -72,6 +74,7 @@ struct PfArgs {
   int tiles_m, tiles_n;
   unsigned long long timeout_ns;
   int debug_flags;
+  PfRope rope;          // PF_EPI_ROPE only
 };
 
 __device__ __forceinline__ float pf_load_bias(const void* bias, int bias_dtype, int n) {
@@ -87,6 +90,27 @@ __device__ __forceinline__ bool pf_wait_drain(uint32_t bar, uint32_t parity, uin
     if (clock64() - t0 > limit) return false;
   }
   return true;
+}
+
+__device__ __forceinline__ void pf_reg_fence8(uint32_t (&r)[8]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7])::"memory");
+}
+
+// 32-byte global accesses (one whole L2 sector; the address must be 32-byte
+// aligned): 8 fp32 read-only loads, 8 words stored
+__device__ __forceinline__ void pf_ld32(const float* p, float* v) {
+  asm volatile("ld.global.nc.v8.f32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]),
+                 "=f"(v[6]), "=f"(v[7])
+               : "l"(p));
+}
+
+__device__ __forceinline__ void pf_st32(__half* p, const uint32_t (&v)[8]) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(v[0]),
+               "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
 }
 
 __device__ __forceinline__ void pf_reg_fence(uint32_t (&r)[32]) {
@@ -139,14 +163,23 @@ __global__ void __launch_bounds__(256) e4m3_to_f16_kernel(const uint8_t* __restr
   if (early) ptx::pdl_wait();
 }
 
-// SWIGLU: the weight is a 16-row interleave of gate and up (rows 32 b + i =
-// gate row 16 b + i, rows 32 b + 16 + i = up row 16 b + i) and the kernel
-// stores silu(gate) * up, N / 2 columns.
-template <bool SWIGLU>
+// PF_EPI_SWIGLU: the weight is a 16-row interleave of gate and up (rows 32 b
+// + i = gate row 16 b + i, rows 32 b + 16 + i = up row 16 b + i) and the
+// kernel stores silu(gate) * up, N / 2 columns.  PF_EPI_ROPE: the QKV
+// projection of a prefill chunk; tiles hold whole 64-row heads (both halves
+// of every rotation pair), each epilogue warp group takes a quarter of every
+// head's dims, rounds the projection to fp16 as the plain store does, then
+// applies RoPE to q and k heads in fp32 with the rounding of the separate
+// kernel (rope.cu) and writes q token-major and k, v into the cache (and
+// token-major copies): bit for bit the result of the GEMM followed by
+// ddq_prefill_rope_kv, without the qkv round trip.
+template <int EPI>
 __global__ void __launch_bounds__(PF_THREADS, 1)
     w8a16_pf_kernel(const __grid_constant__ CUtensorMap tm_x,
                     const __grid_constant__ CUtensorMap tm_w,
                     const __grid_constant__ CUtensorMap tm_y, const PfArgs args) {
+  constexpr bool SWIGLU = EPI == PF_EPI_SWIGLU;
+  constexpr bool ROPE = EPI == PF_EPI_ROPE;
   using L = PfLayout;
   constexpr uint32_t ACC_COLS = PF_BN;
   constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
@@ -284,12 +317,107 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         sb[PF_BN + e] = in ? pf_load_bias(args.bias, args.bias_dtype, n) : 0.f;
       }
       asm volatile("bar.sync 1, 256;" ::: "memory");
+      // RoPE: this thread's token row and its cos/sin values, loaded while
+      // the tile's MMAs run
+      int rm = 0, rb = 0, rs = 0;
+      bool rtok = false;
+      float rc1[16], rs1[16], rc2[16], rs2[16];
+      if constexpr (ROPE) {
+        rm = m0 + q * 32 + lane;
+        rtok = rm < args.M;
+        if (rtok) {
+          rb = rm / args.rope.S;
+          rs = rm - rb * args.rope.S;
+          const float* cr = args.rope.cos + (size_t)rs * 64 + 16 * grp;
+          const float* sr = args.rope.sin + (size_t)rs * 64 + 16 * grp;
+          pf_ld32(cr, rc1);
+          pf_ld32(cr + 8, rc1 + 8);
+          pf_ld32(cr + 32, rc2);
+          pf_ld32(cr + 40, rc2 + 8);
+          pf_ld32(sr, rs1);
+          pf_ld32(sr + 8, rs1 + 8);
+          pf_ld32(sr + 32, rs2);
+          pf_ld32(sr + 40, rs2 + 8);
+        }
+      }
       if (!ptx::mbar_wait(bar_accfull + 8 * b, (uint32_t)(it >> 1) & 1u, tmo, abort_flag)) break;
       if (warp == 4 && lane == 0 && it == 0) trace_stamp(tr, 5);
       ptx::tc_fence_after();
       const uint32_t taddr = tmem_base + (uint32_t)(b * ACC_COLS) + ((uint32_t)(q * 32) << 16);
+      if constexpr (ROPE) {
+        // this thread's token row of the tile; group grp takes dims 16 grp ..
+        // 16 grp + 15 of both halves of every head in the tile (32-byte
+        // stores: whole L2 sectors).  The row's cos/sin values for those dims
+        // were loaded before the accumulator wait and serve all the heads.
+        const PfRope& rp = args.rope;
+        const int heads = min(args.bn, args.N - n0) >> 6;  // N and n0 are multiples of 64
+        const int gh0 = n0 >> 6;                            // q heads, then k, then v heads
+        const int d0 = 16 * grp;
 #pragma unroll 1
-      for (int c = grp; c < args.bn / PF_CH; c += 2) {
+        for (int hh = 0; hh < heads; ++hh) {
+          const int col0 = hh * 64;
+          uint32_t o1[8], o2[8];  // dims d0 .. d0 + 15 and 32 + d0 .. 32 + d0 + 15, fp16 pairs
+          const int gh = gh0 + hh;
+          const bool rot = gh < rp.Hq + rp.Hkv;
+          const float* scl = sb + col0;
+          const float* bia = sb + PF_BN + col0;
+#pragma unroll
+          for (int c8 = 0; c8 < 2; ++c8) {
+            uint32_t r[8], r2[8];  // dims d0 + 8 c8 .. and 32 + d0 + 8 c8 .. of head hh
+            __syncwarp();          // tcgen05.ld is warp-collective
+            ptx::tmem_ld_32x32b_x8(taddr + (uint32_t)(col0 + d0 + 8 * c8), r);
+            ptx::tmem_ld_32x32b_x8(taddr + (uint32_t)(col0 + 32 + d0 + 8 * c8), r2);
+            ptx::tmem_ld_wait();
+            pf_reg_fence8(r);
+            pf_reg_fence8(r2);
+#pragma unroll
+            for (int e2 = 0; e2 < 4; ++e2) {
+              float y1[2], y2[2];
+#pragma unroll
+              for (int t2 = 0; t2 < 2; ++t2) {
+                const int j = 8 * c8 + 2 * e2 + t2, d = d0 + j;
+                // the projection's fp16 output, as the plain store rounds it
+                const float a1 = __half2float(
+                    __float2half_rn(fmaf(__uint_as_float(r[2 * e2 + t2]), scl[d], bia[d])));
+                const float a2 = __half2float(__float2half_rn(
+                    fmaf(__uint_as_float(r2[2 * e2 + t2]), scl[32 + d], bia[32 + d])));
+                if (rot) {
+                  y1[t2] = __fadd_rn(__fmul_rn(a1, rc1[j]), __fmul_rn(-a2, rs1[j]));
+                  y2[t2] = __fadd_rn(__fmul_rn(a2, rc2[j]), __fmul_rn(a1, rs2[j]));
+                } else {
+                  y1[t2] = a1;
+                  y2[t2] = a2;
+                }
+              }
+              const __half2 h1 = __floats2half2_rn(y1[0], y1[1]);
+              const __half2 h2 = __floats2half2_rn(y2[0], y2[1]);
+              o1[4 * c8 + e2] = *reinterpret_cast<const uint32_t*>(&h1);
+              o2[4 * c8 + e2] = *reinterpret_cast<const uint32_t*>(&h2);
+            }
+          }
+          if (!rtok) continue;
+          __half* dst;
+          __half* dst2 = nullptr;
+          if (gh < rp.Hq) {
+            dst = rp.q_out + ((size_t)rm * rp.Hq + gh) * 64;
+          } else {
+            const bool isk = rot;
+            const int g = isk ? gh - rp.Hq : gh - rp.Hq - rp.Hkv;
+            dst = (isk ? rp.kc : rp.vc) + (size_t)rb * rp.cache_bstride +
+                  ((size_t)g * rp.cap + rp.start + rs) * 64;
+            __half* tm_out = isk ? rp.k_out : rp.v_out;
+            if (tm_out) dst2 = tm_out + ((size_t)rm * rp.Hkv + g) * 64;
+          }
+          pf_st32(dst + d0, o1);
+          pf_st32(dst + 32 + d0, o2);
+          if (dst2) {
+            pf_st32(dst2 + d0, o1);
+            pf_st32(dst2 + 32 + d0, o2);
+          }
+        }
+      }
+#pragma unroll 1
+      for (int c = grp; !ROPE && c < args.bn / PF_CH; c += 2) {
         const int col0 = c * PF_CH;
         if (n0 + col0 >= args.N) break;
         uint32_t r[32];
@@ -424,11 +552,11 @@ cudaLaunchAttribute pdl_attr() {
 // Tile width over the weight rows: the MMA time of a tile grows with its
 // width, and the CTAs run ceil(tiles / SMs) tiles each; pick the width that
 // minimises waves x (width + a fixed per-tile cost of ~48 columns).
-int pf_pick_bn(int M, int N, int sms) {
+int pf_pick_bn(int M, int N, int sms, int step = 32) {
   const int tm = (M + PF_BM - 1) / PF_BM;
   int best = PF_BN;
   long best_cost = -1;
-  for (int bn = PF_BN; bn >= 128; bn -= 32) {
+  for (int bn = PF_BN; bn >= 128; bn -= step) {
     const long tiles = (long)tm * ((N + bn - 1) / bn);
     const long waves = (tiles + sms - 1) / sms;
     const long cost = waves * (bn + 48);
@@ -515,16 +643,19 @@ static int pf_take_buffer(const void* ws, cudaStream_t s, bool* early) {
 
 int launch_pf(const __half* x, const uint8_t* wq, const float* scales, const void* bias,
               int bias_dtype, __half* y, int M, int N, int K, void* ws, size_t ws_bytes,
-              unsigned long long timeout_ns, int debug_flags, cudaStream_t s, bool swiglu) {
+              unsigned long long timeout_ns, int debug_flags, cudaStream_t s, bool swiglu,
+              const PfRope* rope) {
   const int dev = current_device();
   const int sms = device_sm_count(dev);
   if (sms <= 0 || dev < 0 || dev >= 64) return DDQ_ERR_DEVICE;
   if (M < 1 || N < 1 || K < 16 || K % 16 != 0) return DDQ_ERR_SHAPE;
   if (!ws || ws_bytes < pf_workspace_bytes(N, K)) return DDQ_ERR_WORKSPACE;
-  if ((reinterpret_cast<uintptr_t>(ws) & 255u) || !aligned16(x) || !aligned16(y) ||
+  if ((reinterpret_cast<uintptr_t>(ws) & 255u) || !aligned16(x) || (!rope && !aligned16(y)) ||
       (N % 8) != 0)
     return DDQ_ERR_ALIGNMENT;
   if (swiglu && N % 32 != 0) return DDQ_ERR_SHAPE;
+  if (rope && (swiglu || N != (rope->Hq + 2 * rope->Hkv) * 64 || rope->S < 1 || M % rope->S != 0))
+    return DDQ_ERR_SHAPE;
   // a workspace of two buffers at fixed offsets (0 and half the workspace,
   // whatever the shape, so that calls of different shapes never overlap):
   // consecutive calls alternate them, so this call's expansion need not wait
@@ -558,17 +689,23 @@ int launch_pf(const __half* x, const uint8_t* wq, const float* scales, const voi
     }
   }
   // 2) the fp16 GEMM
-  auto kern = swiglu ? w8a16_pf_kernel<true> : w8a16_pf_kernel<false>;
-  static SmemAttrOnce attr[2];
-  const int ast = ensure_smem_attr(attr[swiglu ? 1 : 0], dev, kern, PfLayout::ALLOC);
+  const int epi = rope ? PF_EPI_ROPE : swiglu ? PF_EPI_SWIGLU : PF_EPI_STORE;
+  auto kern = epi == PF_EPI_ROPE     ? w8a16_pf_kernel<PF_EPI_ROPE>
+              : epi == PF_EPI_SWIGLU ? w8a16_pf_kernel<PF_EPI_SWIGLU>
+                                     : w8a16_pf_kernel<PF_EPI_STORE>;
+  static SmemAttrOnce attr[3];
+  const int ast = ensure_smem_attr(attr[epi], dev, kern, PfLayout::ALLOC);
   if (ast) return ast;
   CUtensorMap tm_x, tm_w, tm_y;
   int st = pf_tmap(&tm_x, x, (uint64_t)K, (uint64_t)M, PF_BK, PF_BM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st) return st;
-  const int bn = pf_pick_bn(M, N, sms);
+  // the RoPE epilogue takes whole 64-row heads: head-aligned tile widths
+  const int bn = pf_pick_bn(M, N, sms, rope ? 64 : 32);
   st = pf_tmap(&tm_w, w16, (uint64_t)K, (uint64_t)N, PF_BK, (uint32_t)bn, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st) return st;
-  if (swiglu)
+  if (rope)
+    tm_y = tm_x;  // not stored through: the RoPE epilogue writes q, k, v directly
+  else if (swiglu)
     st = pf_tmap(&tm_y, y, (uint64_t)(N / 2), (uint64_t)M, PF_CH / 2, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
   else
     st = pf_tmap(&tm_y, y, (uint64_t)N, (uint64_t)M, PF_CH, 32, CU_TENSOR_MAP_SWIZZLE_64B);
@@ -585,6 +722,7 @@ int launch_pf(const __half* x, const uint8_t* wq, const float* scales, const voi
   a.tiles_n = (N + bn - 1) / bn;
   a.timeout_ns = timeout_ns;
   a.debug_flags = debug_flags;
+  if (rope) a.rope = *rope;
   const int units = a.tiles_m * a.tiles_n;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(units < sms ? units : sms));

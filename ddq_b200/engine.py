@@ -25,7 +25,8 @@ attention -> O -> +residual -> RMSNorm -> gate/up -> SwiGLU -> down ->
 The other operators run on this library's kernels too: residual add +
 RMSNorm (``norm.add_rmsnorm``; on the decode path ``norm.add_rmsnorm_split``,
 which also emits the next GEMM's operand), the prefill RoPE + cache write
-(``attention.prefill_rope_kv``) and the decode attention above.  Prefill
+(``attention.qkv_rope_kv``: in the q/k/v GEMM's epilogue at prefill sizes)
+and the decode attention above.  Prefill
 attention itself is ``scaled_dot_product_attention``.  Their arithmetic
 follows the reference kernels (fp32 math, fp16 storage); the plain-PyTorch
 versions of RMSNorm, RoPE and SwiGLU below serve the oracle engine.
@@ -147,6 +148,10 @@ class Engine:
         # e4m3 planes of the split-plane decode GEMM (True), or fp16 operands
         # for the resident-slice GEMMs (False)
         self.decode_planes = True
+        # prefill chunks: RoPE and the cache write in the q/k/v GEMM's epilogue
+        # (True), or the GEMM and then the separate RoPE + cache kernel (False;
+        # the same bits, one more launch and a round trip of the projection)
+        self.fused_qkv_rope = True
         self._chain_streams: List[torch.cuda.Stream] = []
         self._graphs = {}
 
@@ -281,6 +286,25 @@ class Engine:
                 and self.decode_planes):
             return self._decode_layer(li, x, delta, cache, b0, cos, sin, pos)
         x, h = self.add_rmsnorm(x, L["in_norm"], delta)
+        if pos is None and self.linear_kind == "fp8" and hd in (64, 128):
+            # prefill chunk: the q/k/v projection, RoPE of q and k and the cache
+            # write (one GEMM with them in its epilogue where the prefill kernel
+            # takes the shape, else the GEMM and one RoPE + cache kernel); q, k,
+            # v come back token-major (attention strides independent of the
+            # cache capacity)
+            p = L["qkv"]
+            kc, vc = cache.k[li, b0:b0 + B], cache.v[li, b0:b0 + B]
+            if self.fused_qkv_rope:
+                q, k, v = attention.qkv_rope_kv(h, p.wq, p.scales, p.bias, kc, vc, cos, sin,
+                                                start, nh, nkv, hd, kv_out=True)
+            else:
+                q, k, v = attention.prefill_rope_kv(self.linear(h, p), kc, vc, cos, sin, start,
+                                                    nh, nkv, hd, kv_out=True)
+            o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2),
+                                               v.transpose(1, 2), is_causal=True, scale=scale,
+                                               enable_gqa=True)
+            o = o.transpose(1, 2).reshape(B, S, nh * hd)
+            return self._mlp_block(x, self.linear(o, L["o"]), L)
         qkv = self.linear(h, L["qkv"])
         if pos is not None and S == 1 and self.linear_kind == "fp8":
             # one decode step: RoPE, the cache write and the attention in one kernel
@@ -288,18 +312,6 @@ class Engine:
                                            cache.v[li, b0:b0 + B], cos, sin, pos, nh, nkv, hd,
                                            scale)
             return self._mlp_block(x, self.linear(o.reshape(B, S, nh * hd), L["o"]), L)
-        if pos is None and self.linear_kind == "fp8" and hd in (64, 128):
-            # prefill chunk: RoPE of q and k and the cache write in one kernel;
-            # q, k, v come back token-major (attention strides independent of
-            # the cache capacity)
-            q, k, v = attention.prefill_rope_kv(qkv, cache.k[li, b0:b0 + B],
-                                                cache.v[li, b0:b0 + B], cos, sin, start, nh,
-                                                nkv, hd, kv_out=True)
-            o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2),
-                                               v.transpose(1, 2), is_causal=True, scale=scale,
-                                               enable_gqa=True)
-            o = o.transpose(1, 2).reshape(B, S, nh * hd)
-            return self._mlp_block(x, self.linear(o, L["o"]), L)
         q = qkv[..., : nh * hd].reshape(B, S, nh, hd).transpose(1, 2)
         k = qkv[..., nh * hd: (nh + nkv) * hd].reshape(B, S, nkv, hd).transpose(1, 2)
         v = qkv[..., (nh + nkv) * hd:].reshape(B, S, nkv, hd).transpose(1, 2)

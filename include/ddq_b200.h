@@ -244,6 +244,35 @@ int ddq_prefill_rope_kv(const void* qkv, int64_t qkv_stride, void* k_cache, void
                         int64_t B, int64_t S, int64_t Hq, int64_t Hkv, int64_t D, void* stream);
 
 /*
+ * The q/k/v projection of a prefill chunk with RoPE and the KV-cache write in
+ * its epilogue: bit for bit ddq_w8a16_gemm(x, wq, scales, bias) -> qkv [B * S,
+ * (Hq + 2 Hkv) * D] followed by ddq_prefill_rope_kv(qkv, ...), without writing
+ * or re-reading qkv.  Replaces, for a prefill chunk, the q/k/v projections
+ * (engine.py:215-217; f8_forward + fp8_gemm_kernel, gemm_FP8_d.cu:171-210,
+ * 94-146) with the RoPE kernel on q and k after them (RoPe_d.cu:12-68,
+ * engine.py:219-220) and the cache write (engine.py:126-130, 222).
+ *   x       fp16 [B * S, K] token rows (b major)
+ *   wq, scales, bias, bias_dtype   as ddq_w8a16_gemm with N = (Hq + 2 Hkv) * D
+ *   k_cache, v_cache, cache_batch_stride, capacity, cos, sin, start, q_out,
+ *   k_out, v_out   as ddq_prefill_rope_kv
+ *   workspace  at least ddq_w8a16_gemm_workspace_size(B * S, N, K) bytes,
+ *              256-byte aligned
+ * Alignment: x and wq 16 bytes; q_out, k_out, v_out, the caches, cos and sin
+ * 32 bytes (whole-sector accesses), cache_batch_stride a multiple of 16.
+ * Returns DDQ_ERR_SHAPE (nothing launched) where the fused kernel does not
+ * take the shape: D != 64, or B * S below the prefill kernel's minimum
+ * (ddq_w8a16_gemm_kernel_count(B * S, N, K) == 2 with B * S > 64); the caller
+ * then runs the two calls it replaces.
+ */
+int ddq_w8a16_gemm_qkv_rope_kv(const void* x, const uint8_t* wq, const float* scales,
+                               const void* bias, int bias_dtype, int64_t B, int64_t S, int64_t K,
+                               int64_t Hq, int64_t Hkv, int64_t D, void* k_cache, void* v_cache,
+                               int64_t cache_batch_stride, int64_t capacity, const float* cos,
+                               const float* sin, int64_t start, void* q_out, void* k_out,
+                               void* v_out, void* workspace, size_t workspace_bytes,
+                               void* stream);
+
+/*
  * Residual add + RMSNorm over rows of H (H % 8 == 0, 16-byte aligned rows):
  *   s = fp16(x + delta)   (delta may be NULL: s = x); written to x_out if
  *                         non-NULL (x_out may be x)
