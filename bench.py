@@ -373,7 +373,7 @@ def run_prefill(args, device, world, peaks):
             "tflops": round(tf, 1), "ms_per_pass": round(ms, 3), "flops_per_pass": flops,
             "frac_of_bf16_peak_per_gpu": round(per_gpu / peaks["bf16_tflops"], 4),
             "peak_tflops": peaks["bf16_tflops"], "peak_source": peaks["source"],
-            "kernel": "e4m3_to_f16_kernel + w8a16_pf_kernel (exact weight expansion, tcgen05 kind::f16)"}
+            "kernel": "e4m3_to_f16_kernel + w8a16_pf_kernel (exact weight expansion, tcgen05 kind::f16; CTA pairs with cta_group::2 for the 9728-row gate/up)"}
 
 
 def run_config1(args, device, world, peaks):

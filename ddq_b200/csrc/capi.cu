@@ -91,7 +91,7 @@ int g_debug_flags = 0;
 // (bit 6, which takes no 1..16-token shape) keep it (it writes phase stamps
 // too).
 bool thin_shape(int64_t M, int64_t N, int64_t K) {
-  if (M > thin_max_m() || (g_debug_flags & ~(2 | 8 | 64)) != 0) return false;
+  if (M > thin_max_m() || (g_debug_flags & ~(2 | 8 | 64 | 128)) != 0) return false;
   const int dev = current_device();
   return dev >= 0 && thin_eligible(M, N, K, device_sm_count(dev));
 }
@@ -101,7 +101,7 @@ bool thin_shape(int64_t M, int64_t N, int64_t K) {
 // thin kernel (which then takes the ones it fits); bit 6 (the tensor-core
 // resident-slice kernel for 17..64 tokens) leaves both of them in place.
 bool rs_shape(int64_t M, int64_t N, int64_t K) {
-  if ((g_debug_flags & ~(2 | 64)) != 0) return false;
+  if ((g_debug_flags & ~(2 | 64 | 128)) != 0) return false;
   const int dev = current_device();
   return dev >= 0 && rs_eligible(M, N, K, device_sm_count(dev));
 }
@@ -113,7 +113,7 @@ bool rs_shape(int64_t M, int64_t N, int64_t K) {
 // it takes 17..64-token shapes before every other path; any further bit but
 // the trace (1) and its timeout hook (4) sends them to the older paths.
 bool rt_shape(int64_t M, int64_t N, int64_t K, bool swiglu) {
-  if ((g_debug_flags & 64) == 0 || (g_debug_flags & ~(2 | 16 | 64)) != 0) return false;
+  if ((g_debug_flags & 64) == 0 || (g_debug_flags & ~(2 | 16 | 64 | 128)) != 0) return false;
   const int dev = current_device();
   return dev >= 0 && rt_eligible(M, N, K, device_sm_count(dev), swiglu);
 }

@@ -29,7 +29,9 @@
 // drains its copies and MMAs, frees TMEM and exits.
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <cstring>
+#include <type_traits>
 #include <mutex>
 #include <iterator>
 #include <unordered_map>
@@ -43,25 +45,30 @@ namespace ddq {
 constexpr int PF_BM = 128;       // tokens per tile (MMA M, TMEM lanes)
 constexpr int PF_BN = 256;       // weight rows per tile (MMA N, TMEM columns)
 constexpr int PF_BK = 64;        // K elements per stage (128 B of fp16)
-constexpr int PF_ST = 4;         // ring stages
+constexpr int PF_ST = 4;         // ring stages, one CTA per tile
+constexpr int PF_ST2 = 6;        // ring stages, CTA pairs (half the weight rows per CTA)
 constexpr int PF_THREADS = 384;  // 12 warps
 constexpr int PF_CH = 32;        // epilogue column chunk
 
-struct PfLayout {
+template <int ST, int BROWS>
+struct PfLayoutT {
+  static constexpr int STAGES = ST;
   static constexpr int A_BYTES = PF_BM * PF_BK * 2;   // 16 KB x tile
-  static constexpr int B_BYTES = PF_BN * PF_BK * 2;   // 32 KB w16 tile
+  static constexpr int B_BYTES = BROWS * PF_BK * 2;   // this CTA's w16 rows (32 or 16 KB)
   static constexpr int S_BYTES = A_BYTES + B_BYTES;
   static constexpr int OW_BYTES = 32 * PF_CH * 2;     // one warp's staging (32 x 32 fp16)
-  static constexpr int OFF_O = PF_ST * S_BYTES;       // 8 warps x 1 staging buffer
+  static constexpr int OFF_O = ST * S_BYTES;          // 8 warps x 1 staging buffer
   static constexpr int OFF_SB = OFF_O + 8 * OW_BYTES;   // [2 tiles][scale 256 | bias 256] fp32
   static constexpr int OFF_BAR = OFF_SB + 2 * 2 * PF_BN * 4;
-  static constexpr int NBAR = 2 * PF_ST + 4 + 1;      // full, empty; acc x2 x2; drain
+  static constexpr int NBAR = 2 * ST + 4 + 1;         // full, empty; acc x2 x2; drain
   static constexpr int OFF_MISC = (OFF_BAR + NBAR * 8 + 15) & ~15;
   static constexpr int BYTES = OFF_MISC + 16;
   static constexpr int ALLOC = BYTES + 1024;
   static_assert(S_BYTES % 1024 == 0 && A_BYTES % 1024 == 0, "1024-B aligned operand tiles");
   static_assert(ALLOC <= 232448, "shared memory budget");
 };
+using PfLayout = PfLayoutT<PF_ST, PF_BN>;        // 4 stages x 48 KB
+using PfLayout2 = PfLayoutT<PF_ST2, PF_BN / 2>;  // 6 stages x 32 KB
 
 constexpr int PF_EPI_STORE = 0, PF_EPI_SWIGLU = 1, PF_EPI_ROPE = 2;
 
@@ -173,14 +180,25 @@ __global__ void __launch_bounds__(256) e4m3_to_f16_kernel(const uint8_t* __restr
 // kernel (rope.cu) and writes q token-major and k, v into the cache (and
 // token-major copies): bit for bit the result of the GEMM followed by
 // ddq_prefill_rope_kv, without the qkv round trip.
-template <int EPI>
+//
+// PAIR: clusters of two CTAs run 256-token tiles with tcgen05 .cta_group::2
+// MMAs (M = 256, issued by rank 0): each CTA loads its own 128 tokens of x
+// and half of the tile's weight rows (32 KB a stage instead of 48 KB, so six
+// stages fit), rank 0's full barrier counts both CTAs' bytes, rank 0's
+// commits arrive on both CTAs' empty and accumulator barriers, and both
+// CTAs' epilogues release rank 0's accumulator barrier.  Each CTA's TMEM
+// holds its 128 tokens x all the tile's columns, so the epilogues are those
+// of the single-CTA kernel.
+template <int EPI, bool PAIR>
 __global__ void __launch_bounds__(PF_THREADS, 1)
     w8a16_pf_kernel(const __grid_constant__ CUtensorMap tm_x,
                     const __grid_constant__ CUtensorMap tm_w,
                     const __grid_constant__ CUtensorMap tm_y, const PfArgs args) {
   constexpr bool SWIGLU = EPI == PF_EPI_SWIGLU;
   constexpr bool ROPE = EPI == PF_EPI_ROPE;
-  using L = PfLayout;
+  using L = typename std::conditional<PAIR, PfLayout2, PfLayout>::type;
+  constexpr int ST = L::STAGES;
+  constexpr int TBM = PAIR ? 2 * PF_BM : PF_BM;  // tokens per tile
   constexpr uint32_t ACC_COLS = PF_BN;
   constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
   extern __shared__ uint8_t smem_raw[];
@@ -190,12 +208,15 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KS = (args.K + PF_BK - 1) / PF_BK;
   const int units = args.tiles_m * args.tiles_n;
+  const int rank = PAIR ? (int)ptx::cluster_ctarank() : 0;  // 0 issues the pair's MMAs
+  const int unit0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int ustride = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
   const uint64_t tmo = args.timeout_ns;
   const bool tr = (args.debug_flags & 2) != 0;
 
   const uint32_t bar_full = sbase + L::OFF_BAR;
-  const uint32_t bar_empty = bar_full + 8 * PF_ST;
-  const uint32_t bar_accfull = bar_empty + 8 * PF_ST;  // [2]
+  const uint32_t bar_empty = bar_full + 8 * ST;
+  const uint32_t bar_accfull = bar_empty + 8 * ST;     // [2]
   const uint32_t bar_accempty = bar_accfull + 16;      // [2]
   const uint32_t bar_drain = bar_accempty + 16;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
@@ -203,13 +224,13 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 
   if (threadIdx.x == 0) trace_stamp(tr, 0);
   if (threadIdx.x == 0) {
-    for (int s = 0; s < PF_ST; ++s) {
+    for (int s = 0; s < ST; ++s) {
       ptx::mbar_init(bar_full + 8 * s, 1);
       ptx::mbar_init(bar_empty + 8 * s, 1);
     }
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(bar_accfull + 8 * b, 1);
-      ptx::mbar_init(bar_accempty + 8 * b, 8);
+      ptx::mbar_init(bar_accempty + 8 * b, PAIR ? 16 : 8);  // epilogue warps (of both CTAs)
     }
     ptx::mbar_init(bar_drain, 1);
     *abort_flag = 0;
@@ -219,13 +240,23 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     ptx::prefetch_tmap(&tm_y);
   }
   if (warp == 0) {
-    ptx::tmem_alloc(ptx::smem_u32(tmem_holder), TMEM_COLS);
-    ptx::tmem_relinquish();
+    if constexpr (PAIR) {
+      ptx::tmem_alloc_pair(ptx::smem_u32(tmem_holder), TMEM_COLS);
+      ptx::tmem_relinquish_pair();
+    } else {
+      ptx::tmem_alloc(ptx::smem_u32(tmem_holder), TMEM_COLS);
+      ptx::tmem_relinquish();
+    }
   }
   ptx::tc_fence_before();
   __syncthreads();
+  // pairs: both CTAs' barriers are initialised before either signals the other's
+  if constexpr (PAIR) ptx::cluster_sync();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  // rank 0's full and accumulator-empty barriers as cluster addresses
+  const uint32_t full0 = PAIR ? ptx::mapa_shared(bar_full, 0) : bar_full;
+  const uint32_t accempty0 = PAIR ? ptx::mapa_shared(bar_accempty, 0) : bar_accempty;
   if (threadIdx.x == 0) trace_stamp(tr, 1);
 
   if (warp == 0) {
@@ -238,60 +269,92 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
       ptx::pdl_launch_dependents();
       int g = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        const int m0 = (u / args.tiles_n) * PF_BM, n0 = (u % args.tiles_n) * args.bn;
+      // this CTA's weight rows of a tile: all of them, or its half of a pair's
+      const int brows = PAIR ? args.bn >> 1 : args.bn;
+      for (int u = unit0; u < units && ok; u += ustride) {
+        const int m0 = (u / args.tiles_n) * TBM + rank * PF_BM;
+        const int n0 = (u % args.tiles_n) * args.bn + rank * brows;
         for (int ks = 0; ks < KS; ++ks, ++g) {
-          const int s = g % PF_ST;
-          if (!ptx::mbar_wait(bar_empty + 8 * s, ((uint32_t)(g / PF_ST) & 1u) ^ 1u, tmo,
+          const int s = g % ST;
+          if (!ptx::mbar_wait(bar_empty + 8 * s, ((uint32_t)(g / ST) & 1u) ^ 1u, tmo,
                               abort_flag)) {
             ok = false;
             break;
           }
-          const uint32_t full = bar_full + 8 * s;
           const uint32_t dst = sbase + s * L::S_BYTES;
-          ptx::mbar_arrive_expect_tx(full, (uint32_t)(L::A_BYTES + args.bn * PF_BK * 2));
-          ptx::tma_load_2d(dst, &tm_x, ks * PF_BK, m0, full);
-          ptx::tma_load_2d(dst + L::A_BYTES, &tm_w, ks * PF_BK, n0, full);
+          if constexpr (PAIR) {
+            // rank 0's barrier counts the bytes of both CTAs
+            if (rank == 0)
+              ptx::mbar_arrive_expect_tx(bar_full + 8 * s,
+                                         (uint32_t)(2 * (L::A_BYTES + brows * PF_BK * 2)));
+            ptx::tma_load_2d_pair(dst, &tm_x, ks * PF_BK, m0, full0 + 8 * s);
+            ptx::tma_load_2d_pair(dst + L::A_BYTES, &tm_w, ks * PF_BK, n0, full0 + 8 * s);
+          } else {
+            const uint32_t full = bar_full + 8 * s;
+            ptx::mbar_arrive_expect_tx(full, (uint32_t)(L::A_BYTES + brows * PF_BK * 2));
+            ptx::tma_load_2d(dst, &tm_x, ks * PF_BK, m0, full);
+            ptx::tma_load_2d(dst + L::A_BYTES, &tm_w, ks * PF_BK, n0, full);
+          }
         }
       }
       if (*abort_flag) {
-        for (int i = g > PF_ST ? g - PF_ST : 0; i < g; ++i)
-          pf_wait_drain(bar_full + 8 * (i % PF_ST), (uint32_t)(i / PF_ST) & 1u, tmo);
+        if (!PAIR || rank == 0) {
+          for (int i = g > ST ? g - ST : 0; i < g; ++i)
+            pf_wait_drain(bar_full + 8 * (i % ST), (uint32_t)(i / ST) & 1u, tmo);
+        }
+        // a pair's rank 1 has no barrier of its own for its copies: they
+        // land within microseconds; the teardown waits before exiting
       }
     }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc = ptx::idesc_f16_f32(PF_BM, args.bn);
+    if (lane == 0 && rank == 0) {
+      const uint32_t idesc = ptx::idesc_f16_f32(TBM, args.bn);
       const uint64_t desc0 = ptx::smem_desc_sw128(sbase);
       ptx::pdl_wait();
       bool ok = true;
       int g = 0, it = 0;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++it) {
+      for (int u = unit0; u < units && ok; u += ustride, ++it) {
         const int b = it & 1;
         const uint32_t tmem_d = tmem_base + (uint32_t)(b * ACC_COLS);
-        ok = ptx::mbar_wait(bar_accempty + 8 * b, ((uint32_t)(it >> 1) & 1u) ^ 1u, tmo, abort_flag);
+        const uint32_t par = ((uint32_t)(it >> 1) & 1u) ^ 1u;
+        ok = PAIR ? ptx::mbar_wait_cluster(bar_accempty + 8 * b, par, tmo, abort_flag)
+                  : ptx::mbar_wait(bar_accempty + 8 * b, par, tmo, abort_flag);
         if (!ok) break;
         ptx::tc_fence_after();
         for (int ks = 0; ks < KS; ++ks, ++g) {
-          const int s = g % PF_ST;
-          ok = ptx::mbar_wait(bar_full + 8 * s, (uint32_t)(g / PF_ST) & 1u, tmo, abort_flag);
+          const int s = g % ST;
+          ok = ptx::mbar_wait(bar_full + 8 * s, (uint32_t)(g / ST) & 1u, tmo, abort_flag);
           if (!ok) break;
           ptx::tc_fence_after();
           const uint64_t da = desc0 + (uint64_t)((s * L::S_BYTES) >> 4);
           const uint64_t db = da + (uint64_t)(L::A_BYTES >> 4);
 #pragma unroll
-          for (int kk = 0; kk < PF_BK / 16; ++kk)  // 32 bytes of K per MMA
-            ptx::mma_f16_ss(tmem_d, da + (uint64_t)(2 * kk), db + (uint64_t)(2 * kk), idesc,
-                            (ks | kk) != 0 ? 1u : 0u);
-          ptx::mma_commit(bar_empty + 8 * s);
+          for (int kk = 0; kk < PF_BK / 16; ++kk) {  // 32 bytes of K per MMA
+            if constexpr (PAIR)
+              ptx::mma_f16_ss_pair(tmem_d, da + (uint64_t)(2 * kk), db + (uint64_t)(2 * kk),
+                                   idesc, (ks | kk) != 0 ? 1u : 0u);
+            else
+              ptx::mma_f16_ss(tmem_d, da + (uint64_t)(2 * kk), db + (uint64_t)(2 * kk), idesc,
+                              (ks | kk) != 0 ? 1u : 0u);
+          }
+          if constexpr (PAIR)
+            ptx::mma_commit_pair_mc(bar_empty + 8 * s, (uint16_t)3);
+          else
+            ptx::mma_commit(bar_empty + 8 * s);
         }
         if (!ok) break;
-        ptx::mma_commit(bar_accfull + 8 * b);
+        if constexpr (PAIR)
+          ptx::mma_commit_pair_mc(bar_accfull + 8 * b, (uint16_t)3);
+        else
+          ptx::mma_commit(bar_accfull + 8 * b);
       }
       trace_stamp(tr, 4);
-      ptx::mma_commit(bar_drain);
+      if constexpr (PAIR)
+        ptx::mma_commit_pair(bar_drain);
+      else
+        ptx::mma_commit(bar_drain);
       pf_wait_drain(bar_drain, 0, tmo);
     }
     __syncwarp();
@@ -303,8 +366,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     const int e = threadIdx.x - 128;     // 0..255: one column's scale and bias per tile
     ptx::pdl_wait();
     int it = 0;
-    for (int u = blockIdx.x; u < units; u += gridDim.x, ++it) {
-      const int m0 = (u / args.tiles_n) * PF_BM, n0 = (u % args.tiles_n) * args.bn;
+    for (int u = unit0; u < units; u += ustride, ++it) {
+      // this CTA's 128 tokens of the tile, all of the tile's columns
+      const int m0 = (u / args.tiles_n) * TBM + rank * PF_BM, n0 = (u % args.tiles_n) * args.bn;
       const int b = it & 1;
       // the tile's weight scales and biases, once, into shared memory (two
       // buffers by tile parity: the barrier below keeps every warp within one
@@ -489,10 +553,16 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
           ptx::bulk_commit_group();
         }
       }
-      // release the accumulator once this warp's TMEM loads are done
+      // release the accumulator once this warp's TMEM loads are done (a
+      // pair's MMAs wait on rank 0's barrier for the warps of both CTAs)
       ptx::tc_fence_before();
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(bar_accempty + 8 * b);
+      if (lane == 0) {
+        if constexpr (PAIR)
+          ptx::mbar_arrive_cluster(accempty0 + 8 * b);
+        else
+          ptx::mbar_arrive(bar_accempty + 8 * b);
+      }
     }
     if (lane == 0) ptx::bulk_wait_group0();
     __syncwarp();
@@ -501,9 +571,23 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
   if (threadIdx.x == 128) trace_stamp(tr, 6);
   ptx::tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) {
+    // neither CTA exits (or frees TMEM) while the other may still signal its
+    // barriers or run MMAs on its shared memory; after a timeout, rank 1's
+    // copies in flight (counted on rank 0's barriers) get 20 us to land
+    ptx::cluster_sync();
+    if (*abort_flag) {
+      const uint64_t t0 = ptx::globaltimer_ns();
+      while (ptx::globaltimer_ns() - t0 < 20000ull) __nanosleep(1000);
+    }
+    __syncthreads();
+  }
   if (warp == 0) {
     ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem_base, TMEM_COLS);
+    if constexpr (PAIR)
+      ptx::tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else
+      ptx::tmem_dealloc(tmem_base, TMEM_COLS);
   }
   if (threadIdx.x == 0 && *abort_flag) record_device_error(DDQ_ERR_TIMEOUT);
   if (threadIdx.x == 0) trace_stamp(tr, 7);
@@ -550,15 +634,29 @@ cudaLaunchAttribute pdl_attr() {
 }
 
 // Tile width over the weight rows: the MMA time of a tile grows with its
-// width, and the CTAs run ceil(tiles / SMs) tiles each; pick the width that
-// minimises waves x (width + a fixed per-tile cost of ~48 columns).
-int pf_pick_bn(int M, int N, int sms, int step = 32) {
-  const int tm = (M + PF_BM - 1) / PF_BM;
+// width, and the CTAs (or CTA pairs) run ceil(tiles / slots) tiles each; pick
+// the width that minimises waves x (width + a fixed per-tile cost of ~48
+// columns).
+// Token count from which prefill GEMMs run on CTA pairs; DDQ_PF_PAIR_MIN_M
+// overrides it for measurements (0: never).
+int64_t pf_pair_min_m() {
+  static const int64_t v = [] {
+    const char* e = std::getenv("DDQ_PF_PAIR_MIN_M");
+    const int64_t n = e ? (int64_t)std::atoll(e) : (int64_t)512;
+    return n <= 0 ? (int64_t)1 << 62 : n;
+  }();
+  return v;
+}
+
+int pf_pick_bn(int M, int N, int sms, int step, bool pair) {
+  const int tbm = pair ? 2 * PF_BM : PF_BM;
+  const int tm = (M + tbm - 1) / tbm;
+  const int slots = pair ? sms / 2 : sms;
   int best = PF_BN;
   long best_cost = -1;
   for (int bn = PF_BN; bn >= 128; bn -= step) {
     const long tiles = (long)tm * ((N + bn - 1) / bn);
-    const long waves = (tiles + sms - 1) / sms;
+    const long waves = (tiles + slots - 1) / slots;
     const long cost = waves * (bn + 48);
     if (best_cost < 0 || cost < best_cost) {
       best_cost = cost;
@@ -688,20 +786,31 @@ int launch_pf(const __half* x, const uint8_t* wq, const float* scales, const voi
       return DDQ_ERR_LAUNCH;
     }
   }
-  // 2) the fp16 GEMM
+  // 2) the fp16 GEMM, on CTA pairs from pf_pair_min_m() tokens for wide
+  //    weights (gate/up at 4096 tokens: 62.3 against 64.1 us; the 896- and
+  //    1152-row projections measured 1-11 % slower on pairs)
+  const bool pair =
+      (debug_flags & 128) == 0 && M >= pf_pair_min_m() && N >= 2048 && sms >= 2;
   const int epi = rope ? PF_EPI_ROPE : swiglu ? PF_EPI_SWIGLU : PF_EPI_STORE;
-  auto kern = epi == PF_EPI_ROPE     ? w8a16_pf_kernel<PF_EPI_ROPE>
-              : epi == PF_EPI_SWIGLU ? w8a16_pf_kernel<PF_EPI_SWIGLU>
-                                     : w8a16_pf_kernel<PF_EPI_STORE>;
-  static SmemAttrOnce attr[3];
-  const int ast = ensure_smem_attr(attr[epi], dev, kern, PfLayout::ALLOC);
+  using PfKernel = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, PfArgs);
+  static const PfKernel kernels[2][3] = {
+      {w8a16_pf_kernel<PF_EPI_STORE, false>, w8a16_pf_kernel<PF_EPI_SWIGLU, false>,
+       w8a16_pf_kernel<PF_EPI_ROPE, false>},
+      {w8a16_pf_kernel<PF_EPI_STORE, true>, w8a16_pf_kernel<PF_EPI_SWIGLU, true>,
+       w8a16_pf_kernel<PF_EPI_ROPE, true>}};
+  const PfKernel kern = kernels[pair ? 1 : 0][epi];
+  const int alloc = pair ? PfLayout2::ALLOC : PfLayout::ALLOC;
+  static SmemAttrOnce attr[2][3];
+  const int ast = ensure_smem_attr(attr[pair ? 1 : 0][epi], dev, kern, alloc);
   if (ast) return ast;
   CUtensorMap tm_x, tm_w, tm_y;
   int st = pf_tmap(&tm_x, x, (uint64_t)K, (uint64_t)M, PF_BK, PF_BM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st) return st;
   // the RoPE epilogue takes whole 64-row heads: head-aligned tile widths
-  const int bn = pf_pick_bn(M, N, sms, rope ? 64 : 32);
-  st = pf_tmap(&tm_w, w16, (uint64_t)K, (uint64_t)N, PF_BK, (uint32_t)bn, CU_TENSOR_MAP_SWIZZLE_128B);
+  const int bn = pf_pick_bn(M, N, sms, rope ? 64 : 32, pair);
+  // a pair's CTAs load half of the tile's weight rows each
+  st = pf_tmap(&tm_w, w16, (uint64_t)K, (uint64_t)N, PF_BK, (uint32_t)(pair ? bn / 2 : bn),
+               CU_TENSOR_MAP_SWIZZLE_128B);
   if (st) return st;
   if (rope)
     tm_y = tm_x;  // not stored through: the RoPE epilogue writes q, k, v directly
@@ -718,20 +827,28 @@ int launch_pf(const __half* x, const uint8_t* wq, const float* scales, const voi
   a.N = N;
   a.K = K;
   a.bn = bn;
-  a.tiles_m = (M + PF_BM - 1) / PF_BM;
+  const int tbm = pair ? 2 * PF_BM : PF_BM;
+  a.tiles_m = (M + tbm - 1) / tbm;
   a.tiles_n = (N + bn - 1) / bn;
   a.timeout_ns = timeout_ns;
   a.debug_flags = debug_flags;
   if (rope) a.rope = *rope;
   const int units = a.tiles_m * a.tiles_n;
+  const int slots = pair ? sms / 2 : sms;
+  const int grid = (units < slots ? units : slots) * (pair ? 2 : 1);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(units < sms ? units : sms));
+  cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3(PF_THREADS);
-  cfg.dynamicSmemBytes = PfLayout::ALLOC;
+  cfg.dynamicSmemBytes = alloc;
   cfg.stream = s;
-  cudaLaunchAttribute at = pdl_attr();
-  cfg.attrs = &at;
-  cfg.numAttrs = 1;
+  cudaLaunchAttribute at[2];
+  at[0] = pdl_attr();
+  at[1].id = cudaLaunchAttributeClusterDimension;
+  at[1].val.clusterDim.x = 2;
+  at[1].val.clusterDim.y = 1;
+  at[1].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pair ? 2 : 1;
   if (cudaLaunchKernelEx(&cfg, kern, tm_x, tm_w, tm_y, a) != cudaSuccess) {
     cudaGetLastError();
     return DDQ_ERR_LAUNCH;

@@ -374,8 +374,9 @@ int ddq_device_error(int* code, void* stream);
  * (bit 2 alone selects exactly that, e.g. to compare a fused producer's
  * planes with the GEMM's own pre-pass); while bit 3 is set, the mma.sync
  * resident-slice kernel's shapes go to the thin kernel where it takes them
- * (to test that kernel); with any bit but 1, 4 and 6 set, the opt-in kernel
- * takes no shape.
+ * (to test that kernel); with any bit but 1, 4, 6 and 7 set, the opt-in
+ * kernel takes no shape.  Bit 7 runs the prefill GEMMs that use CTA pairs
+ * (512 tokens and more, N >= 2048) on single CTAs, to compare the two.
  * A wait that runs out is followed by a second bounded wait for the CTA's own
  * copies in flight; should that one run out too, the CTA exits with copies
  * outstanding and the context's further behaviour is undefined (it has not
