@@ -270,16 +270,8 @@ __device__ __forceinline__ void mma_f16_ss_pair(uint32_t d_tmem, uint64_t a_desc
       : "memory");
 }
 
-// arrive once on the mbarrier at offset `bar` in every CTA of `mask` when this
-// thread's earlier pair MMAs finish
-__device__ __forceinline__ void mma_commit_pair_mc(uint32_t bar, uint16_t mask) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
-      " [%0], %1;" ::"r"(bar),
-      "h"(mask)
-      : "memory");
-}
-
+// arrive once on the mbarrier `bar` (a cluster address: this CTA's or the
+// peer's) when this thread's earlier pair MMAs finish
 __device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                    bar)

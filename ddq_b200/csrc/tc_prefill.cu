@@ -184,8 +184,8 @@ __global__ void __launch_bounds__(256) e4m3_to_f16_kernel(const uint8_t* __restr
 // PAIR: clusters of two CTAs run 256-token tiles with tcgen05 .cta_group::2
 // MMAs (M = 256, issued by rank 0): each CTA loads its own 128 tokens of x
 // and half of the tile's weight rows (32 KB a stage instead of 48 KB, so six
-// stages fit), rank 0's full barrier counts both CTAs' bytes, rank 0's
-// commits arrive on both CTAs' empty and accumulator barriers, and both
+// stages fit), rank 0's full barrier counts both CTAs' bytes, rank 0
+// commits to both CTAs' empty and accumulator barriers, and both
 // CTAs' epilogues release rank 0's accumulator barrier.  Each CTA's TMEM
 // holds its 128 tokens x all the tile's columns, so the epilogues are those
 // of the single-CTA kernel.
@@ -257,6 +257,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
   // rank 0's full and accumulator-empty barriers as cluster addresses
   const uint32_t full0 = PAIR ? ptx::mapa_shared(bar_full, 0) : bar_full;
   const uint32_t accempty0 = PAIR ? ptx::mapa_shared(bar_accempty, 0) : bar_accempty;
+  // rank 1's empty and accumulator-full barriers, which rank 0's commits signal too
+  const uint32_t empty1 = PAIR ? ptx::mapa_shared(bar_empty, 1) : bar_empty;
+  const uint32_t accfull1 = PAIR ? ptx::mapa_shared(bar_accfull, 1) : bar_accfull;
   if (threadIdx.x == 0) trace_stamp(tr, 1);
 
   if (warp == 0) {
@@ -339,16 +342,20 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
               ptx::mma_f16_ss(tmem_d, da + (uint64_t)(2 * kk), db + (uint64_t)(2 * kk), idesc,
                               (ks | kk) != 0 ? 1u : 0u);
           }
-          if constexpr (PAIR)
-            ptx::mma_commit_pair_mc(bar_empty + 8 * s, (uint16_t)3);
-          else
+          if constexpr (PAIR) {  // the stage is free in both CTAs
+            ptx::mma_commit_pair(bar_empty + 8 * s);
+            ptx::mma_commit_pair(empty1 + 8 * s);
+          } else {
             ptx::mma_commit(bar_empty + 8 * s);
+          }
         }
         if (!ok) break;
-        if constexpr (PAIR)
-          ptx::mma_commit_pair_mc(bar_accfull + 8 * b, (uint16_t)3);
-        else
+        if constexpr (PAIR) {
+          ptx::mma_commit_pair(bar_accfull + 8 * b);
+          ptx::mma_commit_pair(accfull1 + 8 * b);
+        } else {
           ptx::mma_commit(bar_accfull + 8 * b);
+        }
       }
       trace_stamp(tr, 4);
       if constexpr (PAIR)
