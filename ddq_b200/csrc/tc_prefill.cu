@@ -640,10 +640,20 @@ cudaLaunchAttribute pdl_attr() {
   return at;
 }
 
-// Tile width over the weight rows: the MMA time of a tile grows with its
-// width, and the CTAs (or CTA pairs) run ceil(tiles / slots) tiles each; pick
-// the width that minimises waves x (width + a fixed per-tile cost of ~48
-// columns).
+// Tile width over the weight rows: the time of a tile grows with its width,
+// and the CTAs (or CTA pairs) run ceil(tiles / slots) tiles each; pick the
+// width that minimises waves x (width + a fixed per-tile cost).  The cost,
+// ~300 columns' worth, is fitted to gate/up at 4096 tokens on pairs: 60.5,
+// 62.4, 68.4 and 78.0 us at widths 256, 224, 192 and 160 (9, 10, 12 and 14
+// waves), i.e. ~3.65 us a wave plus ~0.012 us a column.
+int pf_env_bn() {
+  static const int v = [] {
+    const char* e = std::getenv("DDQ_PF_BN");
+    return e ? std::atoi(e) : 0;
+  }();
+  return v;
+}
+
 // Token count from which prefill GEMMs run on CTA pairs; DDQ_PF_PAIR_MIN_M
 // overrides it for measurements (0: never).
 int64_t pf_pair_min_m() {
@@ -664,7 +674,7 @@ int pf_pick_bn(int M, int N, int sms, int step, bool pair) {
   for (int bn = PF_BN; bn >= 128; bn -= step) {
     const long tiles = (long)tm * ((N + bn - 1) / bn);
     const long waves = (tiles + slots - 1) / slots;
-    const long cost = waves * (bn + 48);
+    const long cost = waves * (bn + 300);
     if (best_cost < 0 || cost < best_cost) {
       best_cost = cost;
       best = bn;
@@ -814,7 +824,11 @@ int launch_pf(const __half* x, const uint8_t* wq, const float* scales, const voi
   int st = pf_tmap(&tm_x, x, (uint64_t)K, (uint64_t)M, PF_BK, PF_BM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st) return st;
   // the RoPE epilogue takes whole 64-row heads: head-aligned tile widths
-  const int bn = pf_pick_bn(M, N, sms, rope ? 64 : 32, pair);
+  // (DDQ_PF_BN fixes the width, for measurements)
+  const int bn_env = pf_env_bn();
+  const int bn = bn_env >= 128 && bn_env <= PF_BN && bn_env % (rope ? 64 : 32) == 0
+                     ? bn_env
+                     : pf_pick_bn(M, N, sms, rope ? 64 : 32, pair);
   // a pair's CTAs load half of the tile's weight rows each
   st = pf_tmap(&tm_w, w16, (uint64_t)K, (uint64_t)N, PF_BK, (uint32_t)(pair ? bn / 2 : bn),
                CU_TENSOR_MAP_SWIZZLE_128B);
