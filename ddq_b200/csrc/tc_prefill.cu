@@ -46,19 +46,20 @@ constexpr int PF_BM = 128;       // tokens per tile (MMA M, TMEM lanes)
 constexpr int PF_BN = 256;       // weight rows per tile (MMA N, TMEM columns)
 constexpr int PF_BK = 64;        // K elements per stage (128 B of fp16)
 constexpr int PF_ST = 4;         // ring stages, one CTA per tile
-constexpr int PF_ST2 = 6;        // ring stages, CTA pairs (half the weight rows per CTA)
+constexpr int PF_ST2 = 5;        // ring stages, CTA pairs (half the weight rows per CTA)
 constexpr int PF_THREADS = 384;  // 12 warps
 constexpr int PF_CH = 32;        // epilogue column chunk
 
-template <int ST, int BROWS>
+template <int ST, int BROWS, int NSTG>
 struct PfLayoutT {
   static constexpr int STAGES = ST;
+  static constexpr int NSTAGING = NSTG;             // staging buffers per epilogue warp
   static constexpr int A_BYTES = PF_BM * PF_BK * 2;   // 16 KB x tile
   static constexpr int B_BYTES = BROWS * PF_BK * 2;   // this CTA's w16 rows (32 or 16 KB)
   static constexpr int S_BYTES = A_BYTES + B_BYTES;
   static constexpr int OW_BYTES = 32 * PF_CH * 2;     // one warp's staging (32 x 32 fp16)
-  static constexpr int OFF_O = ST * S_BYTES;          // 8 warps x 1 staging buffer
-  static constexpr int OFF_SB = OFF_O + 8 * OW_BYTES;   // [2 tiles][scale 256 | bias 256] fp32
+  static constexpr int OFF_O = ST * S_BYTES;          // 8 warps x NSTG staging buffers
+  static constexpr int OFF_SB = OFF_O + 8 * NSTG * OW_BYTES;  // [2 tiles][scale | bias] fp32
   static constexpr int OFF_BAR = OFF_SB + 2 * 2 * PF_BN * 4;
   static constexpr int NBAR = 2 * ST + 4 + 1;         // full, empty; acc x2 x2; drain
   static constexpr int OFF_MISC = (OFF_BAR + NBAR * 8 + 15) & ~15;
@@ -67,8 +68,8 @@ struct PfLayoutT {
   static_assert(S_BYTES % 1024 == 0 && A_BYTES % 1024 == 0, "1024-B aligned operand tiles");
   static_assert(ALLOC <= 232448, "shared memory budget");
 };
-using PfLayout = PfLayoutT<PF_ST, PF_BN>;        // 4 stages x 48 KB
-using PfLayout2 = PfLayoutT<PF_ST2, PF_BN / 2>;  // 6 stages x 32 KB
+using PfLayout = PfLayoutT<PF_ST, PF_BN, 1>;        // 4 stages x 48 KB
+using PfLayout2 = PfLayoutT<PF_ST2, PF_BN / 2, 2>;  // 5 stages x 32 KB, 2 staging buffers
 
 constexpr int PF_EPI_STORE = 0, PF_EPI_SWIGLU = 1, PF_EPI_ROPE = 2;
 
@@ -369,7 +370,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;              // TMEM lanes 32 q .. 32 q + 31 = tokens
     const int grp = (warp - 4) >> 2;     // column chunks grp, grp + 2, ...
-    const uint32_t stg = sbase + L::OFF_O + (uint32_t)((warp - 4) * L::OW_BYTES);
+    const uint32_t stg0 = sbase + L::OFF_O + (uint32_t)((warp - 4) * L::NSTAGING * L::OW_BYTES);
+    int nchunk = 0;  // this warp's chunks so far: staging buffer nchunk % NSTAGING
     const int e = threadIdx.x - 128;     // 0..255: one column's scale and bias per tile
     ptx::pdl_wait();
     int it = 0;
@@ -504,8 +506,16 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         }
         ptx::tmem_ld_wait();
         pf_reg_fence(r);
-        if (lane == 0) ptx::bulk_wait_group_read0();  // the staging buffer is free again
+        // the staging buffer is free again once at most NSTAGING - 1 of this
+        // warp's stores are still reading
+        if (lane == 0) {
+          if constexpr (L::NSTAGING == 2)
+            ptx::bulk_wait_group_read1();
+          else
+            ptx::bulk_wait_group_read0();
+        }
         __syncwarp();
+        const uint32_t stg = stg0 + (uint32_t)((nchunk++ % L::NSTAGING) * L::OW_BYTES);
         if constexpr (SWIGLU) {
           // a 32-column chunk is one interleave block: columns 0-15 are gate
           // rows 16 b .. 16 b + 15, columns 16-31 the matching up rows.  gate
