@@ -323,9 +323,11 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         const int b = it & 1;
         const uint32_t tmem_d = tmem_base + (uint32_t)(b * ACC_COLS);
         const uint32_t par = ((uint32_t)(it >> 1) & 1u) ^ 1u;
+        if (it == 2) trace_stamp(tr, 13);  // the third tile wants the first buffer back
         ok = PAIR ? ptx::mbar_wait_cluster(bar_accempty + 8 * b, par, tmo, abort_flag)
                   : ptx::mbar_wait(bar_accempty + 8 * b, par, tmo, abort_flag);
         if (!ok) break;
+        if (it == 2) trace_stamp(tr, 14);
         ptx::tc_fence_after();
         for (int ks = 0; ks < KS; ++ks, ++g) {
           const int s = g % ST;
@@ -357,6 +359,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         } else {
           ptx::mma_commit(bar_accfull + 8 * b);
         }
+        // the tile's last MMA issued (its last stage landed)
+        if (it < 2) trace_stamp(tr, 2 + it);
+        else if (it == 2) trace_stamp(tr, 12);
       }
       trace_stamp(tr, 4);
       if constexpr (PAIR)
@@ -415,6 +420,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
       }
       if (!ptx::mbar_wait(bar_accfull + 8 * b, (uint32_t)(it >> 1) & 1u, tmo, abort_flag)) break;
       if (warp == 4 && lane == 0 && it == 0) trace_stamp(tr, 5);
+      if (warp == 4 && lane == 0 && it == 1) trace_stamp(tr, 10);
       ptx::tc_fence_after();
       const uint32_t taddr = tmem_base + (uint32_t)(b * ACC_COLS) + ((uint32_t)(q * 32) << 16);
       if constexpr (ROPE) {
@@ -579,6 +585,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
           ptx::mbar_arrive_cluster(accempty0 + 8 * b);
         else
           ptx::mbar_arrive(bar_accempty + 8 * b);
+        if (warp == 4 && it < 2) trace_stamp(tr, 9 + 2 * it);  // tile 0 / 1 released
       }
     }
     if (lane == 0) ptx::bulk_wait_group0();
@@ -656,6 +663,16 @@ cudaLaunchAttribute pdl_attr() {
 // ~300 columns' worth, is fitted to gate/up at 4096 tokens on pairs: 60.5,
 // 62.4, 68.4 and 78.0 us at widths 256, 224, 192 and 160 (9, 10, 12 and 14
 // waves), i.e. ~3.65 us a wave plus ~0.012 us a column.
+// Weight rows from which pairs are used; DDQ_PF_PAIR_MIN_N overrides it for
+// measurements.
+int64_t pf_pair_min_n() {
+  static const int64_t v = [] {
+    const char* e = std::getenv("DDQ_PF_PAIR_MIN_N");
+    return e ? (int64_t)std::atoll(e) : (int64_t)2048;
+  }();
+  return v;
+}
+
 int pf_env_bn() {
   static const int v = [] {
     const char* e = std::getenv("DDQ_PF_BN");
@@ -817,7 +834,7 @@ int launch_pf(const __half* x, const uint8_t* wq, const float* scales, const voi
   //    weights (gate/up at 4096 tokens: 62.3 against 64.1 us; the 896- and
   //    1152-row projections measured 1-11 % slower on pairs)
   const bool pair =
-      (debug_flags & 128) == 0 && M >= pf_pair_min_m() && N >= 2048 && sms >= 2;
+      (debug_flags & 128) == 0 && M >= pf_pair_min_m() && N >= pf_pair_min_n() && sms >= 2;
   const int epi = rope ? PF_EPI_ROPE : swiglu ? PF_EPI_SWIGLU : PF_EPI_STORE;
   using PfKernel = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, PfArgs);
   static const PfKernel kernels[2][3] = {
