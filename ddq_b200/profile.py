@@ -104,6 +104,10 @@ def main(argv=None):
     ap.add_argument("--trace", action="store_true",
                     help="also run one launch with the per-CTA phase trace and summarise it "
                          "(with --chain: the chain's last launch, traced in place)")
+    ap.add_argument("--qkv-rope", action="store_true",
+                    help="time the q/k/v GEMM with RoPE and the KV-cache write in its epilogue "
+                         "(ddq_w8a16_gemm_qkv_rope_kv): --batch sequences of --m / --batch tokens, "
+                         "--heads / --kv-heads / --head-dim, N from them, fp32 bias")
     ap.add_argument("--attention", action="store_true",
                     help="time the decode-step attention kernel instead of a GEMM")
     ap.add_argument("--batch", type=int, default=64)
@@ -119,6 +123,10 @@ def main(argv=None):
         return
     L = _lib.load()
     M, N, K = a.m, a.n, a.k
+    if a.qkv_rope:
+        if M % a.batch:
+            raise SystemExit("--qkv-rope: --m must be a multiple of --batch")
+        N = (a.heads + 2 * a.kv_heads) * a.head_dim
     l2 = torch.cuda.get_device_properties(dev).L2_cache_size
     copies = a.copies or max(2, math.ceil(2.2 * l2 / (N * K)))
     copies = min(copies, max(2, int(4e9 // (N * K))))
@@ -141,6 +149,16 @@ def main(argv=None):
 
     ids = torch.empty(M, dtype=torch.int64, device=dev)
 
+    if a.qkv_rope:  # one sequence batch: caches of exactly S positions, written at 0
+        S = M // a.batch
+        kc = torch.zeros(a.batch, a.kv_heads, S, a.head_dim, dtype=torch.float16, device=dev)
+        vc = torch.zeros_like(kc)
+        cs = torch.rand(S, a.head_dim, generator=g, device=dev)
+        sn = torch.rand(S, a.head_dim, generator=g, device=dev)
+        q_out = torch.empty(M, a.heads * a.head_dim, dtype=torch.float16, device=dev)
+        kv_out = torch.empty(2, M, a.kv_heads * a.head_dim, dtype=torch.float16, device=dev)
+        b = torch.randn(N, generator=g, device=dev) * 0.02
+
     w16 = None
     if a.torch_fp16:
         w16 = [torch.randn(N, K, generator=g, device=dev).half() * 0.02 for _ in range(copies)]
@@ -150,7 +168,15 @@ def main(argv=None):
         if a.torch_fp16:
             torch.matmul(x, w16[i % copies].t(), out=y)
             return
-        if a.empty:  # a trivial kernel of this library: the launch + event floor
+        if a.qkv_rope:
+            st = L.ddq_w8a16_gemm_qkv_rope_kv(
+                x.data_ptr(), wq.data_ptr(), s.data_ptr(), b.data_ptr(), _lib.DTYPE_F32,
+                a.batch, M // a.batch, K, a.heads, a.kv_heads, a.head_dim, kc.data_ptr(),
+                vc.data_ptr(), kc.stride(0), kc.shape[2], cs.data_ptr(), sn.data_ptr(), 0,
+                q_out.data_ptr(), kv_out[0].data_ptr(), kv_out[1].data_ptr(),
+                ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+                stream.cuda_stream)
+        elif a.empty:  # a trivial kernel of this library: the launch + event floor
             st = L.ddq_unpack_argmax(packed.data_ptr(), 1, ids.data_ptr(), stream.cuda_stream)
         elif a.lm_head:
             st = L.ddq_lm_head_argmax(x.data_ptr(), wq.data_ptr(), s.data_ptr(), M, N, K, 0,
