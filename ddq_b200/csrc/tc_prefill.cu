@@ -316,6 +316,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     if (lane == 0 && rank == 0) {
       const uint32_t idesc = ptx::idesc_f16_f32(TBM, args.bn);
       const uint64_t desc0 = ptx::smem_desc_sw128(sbase);
+      // test hook (ddq_set_debug bit 0): no accumulator-ready signal, so the
+      // epilogues' bounded waits run out and every role winds down
+      const bool skip_accfull = (args.debug_flags & 1) != 0;
       ptx::pdl_wait();
       bool ok = true;
       int g = 0, it = 0;
@@ -353,11 +356,13 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
           }
         }
         if (!ok) break;
-        if constexpr (PAIR) {
-          ptx::mma_commit_pair(bar_accfull + 8 * b);
-          ptx::mma_commit_pair(accfull1 + 8 * b);
-        } else {
-          ptx::mma_commit(bar_accfull + 8 * b);
+        if (!skip_accfull) {
+          if constexpr (PAIR) {
+            ptx::mma_commit_pair(bar_accfull + 8 * b);
+            ptx::mma_commit_pair(accfull1 + 8 * b);
+          } else {
+            ptx::mma_commit(bar_accfull + 8 * b);
+          }
         }
         // the tile's last MMA issued (its last stage landed)
         if (it < 2) trace_stamp(tr, 2 + it);

@@ -363,8 +363,9 @@ int ddq_device_error(int* code, void* stream);
 /*
  * Test hook (no reference counterpart): set the limit of every device-side
  * bounded wait (0 = the 1 s default) and debug flags for later launches in
- * this process.  flags bit 0 makes the tensor-core kernel skip the
- * accumulator-ready signal, so its epilogue wait runs out and reports
+ * this process.  flags bit 0 makes the tensor-core decode and prefill
+ * kernels skip the accumulator-ready signal, so their epilogue waits run out
+ * and report
  * DDQ_ERR_TIMEOUT through ddq_device_error() without faulting the GPU;
  * bit 1 turns on the phase trace read by ddq_read_trace(); bit 6 switches
  * on the opt-in 17..64-token tcgen05 resident-slice kernel, and bit 4 makes

@@ -42,3 +42,29 @@ def test_bounded_wait_reports_timeout_and_context_survives(cuda_device):
     torch.cuda.synchronize()
     assert device_error(lib) == 0
     assert o.normwise_rel_err(y.cpu().numpy(), o.f8_forward(x, wq, s)) <= 3e-3
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 9728, 896), (600, 896, 896), (1024, 2048, 256)])
+def test_prefill_bounded_waits_report_timeout(cuda_device, M, N, K):
+    """The same hook in the prefill GEMM, on CTA pairs (N >= 2048: the pair's
+    rank 0 commits for both CTAs, and both epilogues wait) and on single
+    CTAs: DDQ_ERR_TIMEOUT, every role winds down, the context stays usable."""
+    from ddq_b200 import _lib, gemm_fp8
+    lib = _lib.load()
+    g = torch.Generator(device="cuda").manual_seed(M + N)
+    xd = torch.randn(M, K, generator=g, device="cuda").half()
+    wqd, sd = gemm_fp8.quantize(torch.randn(N, K, generator=g, device="cuda") * 0.02)
+    ref = gemm_fp8.f8_forward(xd, wqd, sd)
+    torch.cuda.synchronize()
+    assert device_error(lib) == 0
+    try:
+        assert lib.ddq_set_debug(1, 20_000_000) == 0
+        gemm_fp8.f8_forward(xd, wqd, sd)
+        torch.cuda.synchronize()
+        assert device_error(lib) == DDQ_ERR_TIMEOUT
+    finally:
+        lib.ddq_set_debug(0, 0)
+    y = gemm_fp8.f8_forward(xd, wqd, sd)
+    torch.cuda.synchronize()
+    assert device_error(lib) == 0
+    assert torch.equal(y, ref)
