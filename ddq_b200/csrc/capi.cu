@@ -453,7 +453,18 @@ extern "C" int ddq_lm_head_argmax(const void* x, const uint8_t* wq, const float*
     dws = static_cast<uint8_t*>(workspace) + area;
     dws_bytes = workspace_bytes - area;
   }
-  if (cudaMemsetAsync(packed, 0, (size_t)M * sizeof(uint64_t), s) != cudaSuccess) return DDQ_ERR_LAUNCH;
+  // every chunk on the decode kernel: its split pre-pass zeroes the chunk's
+  // packed words, and its last CTA writes the ids (arrival counter at byte 64
+  // of the streaming kernel's area, zero between calls); otherwise a memset
+  // before and the unpack kernel after
+  const int64_t last_mc = M - (M - 1) / kLmChunk * kLmChunk;  // the smallest chunk
+  const bool dec_all = N > 0 && last_mc >= tc_min_m();
+  unsigned int* counter =
+      dec_all && ids && dws ? reinterpret_cast<unsigned int*>(static_cast<uint8_t*>(workspace) + 64)
+                            : nullptr;
+  if (!dec_all &&
+      cudaMemsetAsync(packed, 0, (size_t)M * sizeof(uint64_t), s) != cudaSuccess)
+    return DDQ_ERR_LAUNCH;
   if (N > 0) {
     const __half* xh = reinterpret_cast<const __half*>(x);
     unsigned long long* pk = reinterpret_cast<unsigned long long*>(packed);
@@ -463,14 +474,16 @@ extern "C" int ddq_lm_head_argmax(const void* x, const uint8_t* wq, const float*
       if (mc >= tc_min_m())
         st = launch_dec(xh + m0 * K, wq, scales, nullptr, DDQ_DTYPE_NONE, nullptr, pk + m0,
                         vocab_offset, mc, (int)N, (int)K, dws, dws_bytes,
-                        g_wait_timeout_ns, g_debug_flags, s);
+                        g_wait_timeout_ns, g_debug_flags, s, false, nullptr, nullptr,
+                        counter ? ids + m0 : nullptr, counter);
       else
         st = launch_skinny_argmax(xh + m0 * K, wq, scales, pk + m0, vocab_offset, mc, (int)N,
                                   (int)K, s);
       if (st != DDQ_OK) return st;
     }
   }
-  if (ids) return launch_unpack_argmax(reinterpret_cast<const unsigned long long*>(packed), M, ids, s);
+  if (ids && !counter)
+    return launch_unpack_argmax(reinterpret_cast<const unsigned long long*>(packed), M, ids, s);
   return DDQ_OK;
 }
 

@@ -44,7 +44,11 @@ int launch_dec(const __half* x, const uint8_t* wq, const float* scales, const vo
                int bias_dtype, __half* y, unsigned long long* packed, int64_t vocab_offset, int M,
                int N, int K, void* ws, size_t ws_bytes, unsigned long long timeout_ns,
                int debug_flags, cudaStream_t s, bool swiglu = false,
-               const uint8_t* ext_planes = nullptr, const float* ext_xscale = nullptr);
+               const uint8_t* ext_planes = nullptr, const float* ext_xscale = nullptr,
+               int64_t* ids = nullptr, unsigned int* counter = nullptr);
+// With packed (the greedy epilogue) and no ext_planes, the split pre-pass
+// zeroes packed[0, M) before the GEMM's atomicMax; with ids and counter (a
+// zero word the call leaves at zero) the GEMM's last CTA also writes ids.
 // 1..16 tokens, K % 64 == 0: each SM's weight slice resident in shared memory
 // before the grid dependency, mma.sync on fp16 activations (thin.cu).  No
 // workspace.  thin_eligible says whether launch_thin takes the shape.

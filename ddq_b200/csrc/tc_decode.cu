@@ -64,7 +64,8 @@ __host__ __device__ constexpr int dc_stage_k(int bt) { return bt <= 32 ? 256 : 1
 template <int CPT>
 __global__ void __launch_bounds__(256) xsplit_kernel(const __half* __restrict__ x,
                                                      uint8_t* __restrict__ planes,
-                                                     float* __restrict__ xscale, int M, int K) {
+                                                     float* __restrict__ xscale, int M, int K,
+                                                     unsigned long long* __restrict__ zero_packed) {
   // Let the GEMM that follows launch now (it prefetches its weights while
   // this grid and the one before it finish), then wait for x, which may be
   // the previous kernel's output (both no-ops without PDL).
@@ -72,6 +73,9 @@ __global__ void __launch_bounds__(256) xsplit_kernel(const __half* __restrict__ 
   ptx::pdl_wait();
   const int m = blockIdx.x;
   const int nch = K / 8;
+  // the greedy GEMM after this pass takes its per-token maxima with atomicMax
+  // (after its own grid dependency on this pass): start them at zero here
+  if (zero_packed != nullptr && threadIdx.x == 0) zero_packed[m] = 0ull;
   const __half* xr = x + (size_t)m * K;
   constexpr int R = CPT > 0 ? CPT : 1;
   uint4 v[R];
@@ -214,6 +218,8 @@ struct DcArgs {
   int y_tma;
   unsigned long long timeout_ns;
   int debug_flags;
+  long long* ids;          // greedy epilogue: token ids, written by the last CTA (or NULL)
+  unsigned int* counter;   // its arrival counter, zero between calls (NULL: no ids here)
 };
 
 __device__ __forceinline__ float dc_load_bias(const void* bias, int bias_dtype, int n) {
@@ -869,12 +875,36 @@ __global__ void __launch_bounds__(DC_THREADS, 1)
     ptx::cluster_sync();
   }
 
+  // greedy epilogue with ids: this thread's atomicMax words are visible
+  // device-wide before the CTA's arrival below
+  if (ARGMAX && args.counter != nullptr) __threadfence();
   if (threadIdx.x == 128) trace_stamp(tr, 6);
   ptx::tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+  if constexpr (ARGMAX) {
+    if (args.counter != nullptr) {
+      // the last CTA to arrive (timed-out CTAs arrive too) turns every
+      // token's packed word into its id - the unpack kernel's work - and
+      // clears the counter for the next call
+      volatile int* last = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 8);
+      if (threadIdx.x == 0) {
+        const unsigned int total = gridDim.x * gridDim.y * gridDim.z;
+        *last = atomicAdd(args.counter, 1u) == total - 1u ? 1 : 0;
+      }
+      __syncthreads();
+      if (*last) {
+        __threadfence();
+        for (int m = threadIdx.x; m < args.M; m += blockDim.x) {
+          const unsigned long long v = __ldcg(args.packed + m);
+          args.ids[m] = v ? (long long)(0xFFFFFFFFull - (v & 0xFFFFFFFFull)) : 0ll;
+        }
+        if (threadIdx.x == 0) *args.counter = 0u;
+      }
+    }
   }
   if (threadIdx.x == 0 && *abort_flag) record_device_error(DDQ_ERR_TIMEOUT);
   if (threadIdx.x == 0) trace_stamp(tr, 7);
@@ -1010,7 +1040,7 @@ int launch_dec(const __half* x, const uint8_t* wq, const float* scales, const vo
                int bias_dtype, __half* y, unsigned long long* packed, int64_t vocab_offset, int M,
                int N, int K, void* ws, size_t ws_bytes, unsigned long long timeout_ns,
                int debug_flags, cudaStream_t s, bool swiglu, const uint8_t* ext_planes,
-               const float* ext_xscale) {
+               const float* ext_xscale, int64_t* ids, unsigned int* counter) {
   const int sms = device_sm_count(current_device());
   if (sms <= 0) return DDQ_ERR_DEVICE;
   if (M < 1 || M > 64) return DDQ_ERR_SHAPE;
@@ -1044,11 +1074,11 @@ int launch_dec(const __half* x, const uint8_t* wq, const float* scales, const vo
     cfg.numAttrs = 1;
     const int nch = K / 8;
     cudaError_t le;
-    if (nch <= 256) le = cudaLaunchKernelEx(&cfg, xsplit_kernel<1>, x, planes, xscale, M, K);
-    else if (nch <= 512) le = cudaLaunchKernelEx(&cfg, xsplit_kernel<2>, x, planes, xscale, M, K);
-    else if (nch <= 768) le = cudaLaunchKernelEx(&cfg, xsplit_kernel<3>, x, planes, xscale, M, K);
-    else if (nch <= 1024) le = cudaLaunchKernelEx(&cfg, xsplit_kernel<4>, x, planes, xscale, M, K);
-    else le = cudaLaunchKernelEx(&cfg, xsplit_kernel<0>, x, planes, xscale, M, K);
+    if (nch <= 256) le = cudaLaunchKernelEx(&cfg, xsplit_kernel<1>, x, planes, xscale, M, K, packed);
+    else if (nch <= 512) le = cudaLaunchKernelEx(&cfg, xsplit_kernel<2>, x, planes, xscale, M, K, packed);
+    else if (nch <= 768) le = cudaLaunchKernelEx(&cfg, xsplit_kernel<3>, x, planes, xscale, M, K, packed);
+    else if (nch <= 1024) le = cudaLaunchKernelEx(&cfg, xsplit_kernel<4>, x, planes, xscale, M, K, packed);
+    else le = cudaLaunchKernelEx(&cfg, xsplit_kernel<0>, x, planes, xscale, M, K, packed);
     if (le != cudaSuccess) {
       cudaGetLastError();
       return DDQ_ERR_LAUNCH;
@@ -1070,6 +1100,8 @@ int launch_dec(const __half* x, const uint8_t* wq, const float* scales, const vo
   a.timeout_ns = timeout_ns;
   a.debug_flags = debug_flags;
   a.out_n = swiglu ? N / 2 : N;
+  a.ids = packed && ids && counter ? reinterpret_cast<long long*>(ids) : nullptr;
+  a.counter = a.ids ? counter : nullptr;
   const int epi = packed ? DC_EPI_ARGMAX : swiglu ? DC_EPI_SWIGLU : DC_EPI_STORE;
 #define DDQ_DC_CASE(BT_, ST_)                                                                  \
   case BT_:                                                                                    \

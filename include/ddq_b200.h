@@ -316,13 +316,14 @@ int ddq_argmax_f16(const void* logits, int64_t B, int64_t V, int64_t* out,
                    void* stream);
 
 /*
- * Bytes of workspace ddq_lm_head_argmax needs.  It starts with an arrival
- * counter and one word per CTA and token (1..16 tokens: one streaming kernel
- * whose last CTA combines them), followed by the activation planes of the
- * decode-kernel path used for more tokens.  Zero-fill it once before its
- * first use; every call leaves the counter at zero.  Keep it for
- * ddq_lm_head_argmax calls only (other entry points would overwrite the
- * counter), one workspace per stream.
+ * Bytes of workspace ddq_lm_head_argmax needs.  It starts with two arrival
+ * counters (bytes 0 and 64: the last CTA to arrive combines the results, of
+ * the streaming kernel and of the decode kernel) and one word per CTA and
+ * token of the streaming kernel (its tokens: see below), followed by the
+ * activation planes of the decode-kernel path used for more tokens.
+ * Zero-fill it once before its first use; every call leaves the counters at
+ * zero.  Keep it for ddq_lm_head_argmax calls only (other entry points
+ * would overwrite the counters), one workspace per stream.
  */
 size_t ddq_lm_head_argmax_workspace_size(int64_t M, int64_t N, int64_t K);
 
@@ -337,8 +338,11 @@ size_t ddq_lm_head_argmax_workspace_size(int64_t M, int64_t N, int64_t K);
  * receives the decoded global index of this shard's best logit.
  * The logits are never written to memory.  1..16 tokens with K % 64 == 0
  * (K <= 4096) run one kernel that streams 16-row weight tiles and writes
- * packed[] and ids[] itself; other shapes run the activation split, the
- * decode kernel with an argmax epilogue and an unpack kernel.
+ * packed[] and ids[] itself; other shapes run the activation split (which
+ * also zeroes packed[]) and the decode kernel with an argmax epilogue, whose
+ * last CTA writes ids[] (with the workspace's counter; a call whose chunks
+ * of 64 tokens include one below the decode kernel's minimum runs a memset
+ * and an unpack kernel instead).
  * Replaces: engine.py:338 (lm_head via gemm_d) + engine.py:345/351
  * (sampler_d.forward on the last position), sampler_d.cu:10-49.
  */

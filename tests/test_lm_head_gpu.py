@@ -132,3 +132,54 @@ def test_full_vocab_lm_head(mods, M):
     # wherever the pick differs, the chosen logit is within 2 ulps of the max
     chosen = ref.gather(1, ids[:, None]).squeeze(1)
     assert ((top2[:, 0] - chosen) <= 2 * ulp).all()
+
+
+@pytest.mark.parametrize("M,N", [(20, 1000), (64, 18992), (100, 20000), (130, 5000)])
+def test_decode_path_zeroes_packed_and_writes_ids(mods, M, N):
+    """Beyond the streaming kernel's token counts the lm_head runs the split
+    pre-pass, which zeroes packed, and the decode GEMM, whose last CTA writes
+    ids from packed and clears its arrival counter.  A packed buffer full of
+    stale maxima must not leak into the result; ids decode packed; and a call
+    repeated after one on other activations gives the same words (the counter
+    was left at zero).  Shapes: split-K clusters (N = 1000), one 64-token
+    chunk, two chunks (100, 130 tokens)."""
+    import ctypes
+    from ddq_b200 import _lib
+    g, lm, _ = mods
+    L = _lib.load()
+    rng = np.random.default_rng(M + N)
+    x1 = dev(rng.normal(0, 1, (M, HIDDEN)).astype(np.float16))
+    x2 = dev((rng.normal(0, 1, (M, HIDDEN)) * 3).astype(np.float16))
+    wq, s = o.quantize(rng.normal(0, 0.02, (N, HIDDEN)).astype(np.float32))
+    wq, s = dev(wq), dev(s)
+
+    def call(x):
+        packed = torch.full((M,), -1, dtype=torch.int64, device="cuda")  # all bits set
+        ids = torch.full((M,), -7, dtype=torch.int64, device="cuda")
+        nws = L.ddq_lm_head_argmax_workspace_size(M, N, HIDDEN)
+        ws = lm.lm_workspace(x.device, nws)
+        st = L.ddq_lm_head_argmax(x.data_ptr(), wq.data_ptr(), s.data_ptr(), M, N, HIDDEN, 0,
+                                  packed.data_ptr(), ids.data_ptr(), ws.data_ptr(), ws.numel(),
+                                  torch.cuda.current_stream().cuda_stream)
+        assert st == 0, _lib.status_string(st)
+        torch.cuda.synchronize()
+        return ids, packed
+
+    ids1, p1 = call(x1)
+    ids2, p2 = call(x2)
+    ids1b, p1b = call(x1)
+    code = ctypes.c_int(-1)
+    assert L.ddq_device_error(ctypes.byref(code), torch.cuda.current_stream().cuda_stream) == 0
+    assert code.value == 0
+    assert torch.equal(p1, p1b) and torch.equal(ids1, ids1b)
+    for ids, p in ((ids1, p1), (ids2, p2)):
+        assert torch.equal(ids, lm.unpack(p))
+        assert (p != -1).all()
+    # the picks: the sampler's over f8_forward's logits where the top two are clear
+    for x, ids in ((x1, ids1), (x2, ids2)):
+        logits = g.f8_forward(x, wq, s).float().cpu().numpy()
+        top = np.sort(logits, axis=1)[:, -2:]
+        ulp = np.spacing(np.abs(top[:, 1]).astype(np.float16)).astype(np.float32)
+        clear = (top[:, 1] - top[:, 0]) > 2 * ulp
+        np.testing.assert_array_equal(ids.cpu().numpy()[clear], o.argmax_f16(logits)[clear])
+        assert clear.mean() > 0.8
