@@ -124,3 +124,33 @@ def test_argument_validation_of_the_fused_operators_without_gpu(lib):
     assert lib.ddq_w8a16_gemm_planes(A, A, A, A, None, 0, A, 65, 896, 896, 0, None) == SHAPE
     assert lib.ddq_w8a16_gemm_planes(A, A, A, A, None, 9, A, 16, 896, 896, 0, None) == INVALID
     assert lib.ddq_w8a16_gemm_planes(A, A, U, A, None, 0, A, 16, 896, 896, 0, None) == ALIGN
+
+
+def test_argument_validation_of_the_fused_qkv_rope_gemm_without_gpu(lib):
+    """ddq_w8a16_gemm_qkv_rope_kv returns its status before any CUDA call for
+    bad arguments, for the shapes its fused epilogue does not take
+    (DDQ_ERR_SHAPE: the caller then runs the GEMM and ddq_prefill_rope_kv) and
+    for pointers that are not 32-byte aligned (fake addresses, nothing is
+    dereferenced)."""
+    A, A16, U = 256, 272, 258     # 32-byte aligned, 16- but not 32-byte, misaligned
+    OK, INVALID, SHAPE, ALIGN = 0, 1, 2, 3
+    hq, hkv, d, K = 14, 2, 64, 896
+
+    def fused(x=A, bias_dtype=0, B=8, S=64, D=d, cap=64, start=0, q=A, kc=A, cs=A,
+              bstride=None, null_x=False):
+        bstride = hkv * cap * d if bstride is None else bstride
+        return lib.ddq_w8a16_gemm_qkv_rope_kv(
+            None if null_x else x, A, A, None, bias_dtype, B, S, K, hq, hkv, D, kc, A, bstride,
+            cap, cs, A, start, q, None, None, A, 1 << 20, None)
+    assert fused(B=-1) == SHAPE
+    assert fused(B=0) == OK
+    assert fused(null_x=True) == INVALID
+    assert fused(bias_dtype=5) == INVALID
+    assert fused(D=128) == SHAPE            # the fused epilogue takes 64-wide heads
+    assert fused(B=1, S=16) == SHAPE        # 16 tokens: below the prefill kernel
+    assert fused(start=8) == SHAPE          # start + S beyond the capacity
+    assert fused(bstride=hkv * 64 * d - 8) == SHAPE
+    assert fused(x=U) == ALIGN
+    assert fused(q=A16) == ALIGN            # whole-sector stores need 32 bytes
+    assert fused(kc=A16) == ALIGN
+    assert fused(cs=A16) == ALIGN
