@@ -554,11 +554,16 @@ def run_generation(args, device, rank, world, peaks):
     if world > 1:
         torch.distributed.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st = {}
     e0.record()
-    toks = eng.generate(prompts, args.gen_new_tokens)
+    toks = eng.generate(prompts, args.gen_new_tokens, stats=st)
     e1.record()
     torch.cuda.synchronize(device)
     ms = reduce_max(e0.elapsed_time(e1), world, device)
+    # the replayed decode steps alone (device time between events recorded
+    # after the step's capture), max over ranks
+    d0, d1 = st["decode_events"]
+    decode_ms = reduce_max(d0.elapsed_time(d1), world, device)
     # the prefill share of that time: the same prompts, first token only
     e0.record()
     eng.generate(prompts, 1)
@@ -575,7 +580,7 @@ def run_generation(args, device, rank, world, peaks):
     ctx = args.gen_prompt_len + args.gen_new_tokens / 2
     kv = L * 2 * per * Hkv * ctx * D * 2
     step_bytes_gpu = L * layer_w + lm_w + kv
-    step_ms = (ms - prefill_ms) / max(1, args.gen_new_tokens - 1)
+    step_ms = decode_ms / max(1, st["decode_steps"])
     parity = None
     if world == 1 and not args.no_parity:
         parity = generation_parity(eng, prompts, toks)
@@ -586,6 +591,10 @@ def run_generation(args, device, rank, world, peaks):
             "tok_s": round(total / (ms * 1e-3), 1), "ms": round(ms, 1),
             "prefill_ms": round(prefill_ms, 1),
             "decode_ms_per_step": round(step_ms, 3),
+            "capture_and_host_ms": round(ms - prefill_ms - decode_ms, 1),
+            "decode_timing": "CUDA events around the replayed decode steps (the step is "
+                             "captured once per generate call, after the prefill is queued; "
+                             "tok_s and ms include prefill, capture and any host wait)",
             "decode_step_hbm_bytes_per_gpu": int(step_bytes_gpu),
             "decode_roofline_frac": round(step_bytes_gpu / (step_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
                                           4),

@@ -437,7 +437,8 @@ class Engine:
     # ------------------------------------------------------------------ generation
     @torch.no_grad()
     def generate(self, prompts: torch.Tensor, max_new_tokens: int, prefill_chunk: int = 64,
-                 use_graph: bool = True, teacher: Optional[torch.Tensor] = None) -> torch.Tensor:
+                 use_graph: bool = True, teacher: Optional[torch.Tensor] = None,
+                 stats: Optional[dict] = None) -> torch.Tensor:
         """Greedy generation for a batch of equal-length prompts [B, S] -> tokens [B, max_new].
 
         Prefill runs in chunks of `prefill_chunk` sequences (M = chunk * S tokens per
@@ -447,7 +448,9 @@ class Engine:
         device.  With `teacher` [B, max_new]
         the next input at each step is the teacher's token instead of the generated
         one (used to compare against the oracle step by step); the returned tokens
-        are still this engine's greedy picks.
+        are still this engine's greedy picks.  A `stats` dict receives
+        "decode_events": CUDA events recorded around the decode steps (after
+        the step's capture) and "decode_steps", their number.
         """
         B, S = prompts.shape
         cap = S + max_new_tokens
@@ -494,11 +497,18 @@ class Engine:
                     step()
                 finally:
                     graph.capture_end()
+        if stats is not None:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record()
         for _ in range(1, max_new_tokens):
             if graph is not None:
                 graph.replay()
             else:
                 step()
+        if stats is not None:
+            ev[1].record()
+            stats["decode_events"] = ev
+            stats["decode_steps"] = max_new_tokens - 1
         if graph is not None:
             del graph
         return out
