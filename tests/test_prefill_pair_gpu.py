@@ -45,7 +45,9 @@ def weights(N, K, seed):
 @pytest.mark.parametrize("M,N,K,bias", [
     (512, 9728, 896, None), (4096, 1152, 896, torch.float32), (1000, 896, 4864, None),
     (700, 896, 896, torch.float16), (777, 4096, 128, torch.float32), (2048, 4864, 896, None),
-    (1300, 2080, 896, torch.float16)])
+    (1300, 2080, 896, torch.float16),
+    # K % 64 != 0: the last K stage is a partial box, zero-filled past K
+    (600, 2048, 144, torch.float32), (300, 896, 208, None)])
 def test_pair_equals_single_cta(lib, M, N, K, bias):
     from ddq_b200 import _lib, gemm_fp8
     wq, s, g = weights(N, K, M + N)
@@ -92,3 +94,19 @@ def test_qkv_rope_unaffected_by_the_switch(lib, B, S, start):
     for a, b in zip(pair, single):
         assert torch.equal(a, b)
     assert torch.equal(caches[0][0], caches[1][0]) and torch.equal(caches[0][1], caches[1][1])
+
+
+@pytest.mark.parametrize("M,N,K", [(600, 2048, 144), (300, 896, 208), (520, 2080, 80)])
+def test_partial_last_k_stage_matches_oracle(lib, M, N, K):
+    """K a multiple of 16 but not of 64: the last K stage's box reaches past K
+    and is zero-filled; pairs (N >= 2048) and single CTAs against the oracle."""
+    import numpy as np
+    from oracle import w8a16 as o
+    from ddq_b200 import gemm_fp8
+    rng = np.random.default_rng(M + K)
+    x = rng.normal(0, 1, (M, K)).astype(np.float16)
+    wq, s = o.quantize(rng.normal(0, 0.02, (N, K)).astype(np.float32))
+    y = gemm_fp8.f8_forward(torch.from_numpy(x).cuda(), torch.from_numpy(wq).cuda(),
+                            torch.from_numpy(s).cuda())
+    torch.cuda.synchronize()
+    assert o.normwise_rel_err(y.cpu().numpy(), o.f8_forward(x, wq, s)) <= 3e-3
